@@ -1,0 +1,436 @@
+"""Benchmark: sink-attention kept-block TFLOP/s and layer latency at the Wan
+32K shape, on 1..8 B200 GPUs (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one sink-attention forward of one Wan2.1 self-attention layer:
+B=2 (CFG pair), H=12, S=32760 tokens padded to 32768 (256 blocks of 128),
+D=128, bf16, with the benchmark's ~20% block mask (key block 0 | diagonal |
+Bernoulli(0.2), seed 1). `value` is whole-job kept-block TFLOP/s
+(4*D*sum of valid rows x valid cols over kept blocks, all ranks) over the
+max-over-ranks device time of the K timed steps. Inputs (603 MB) exceed L2.
+
+Multi-GPU (torchrun): the work shards by (batch, head) unit with no
+collective on the data path. Weak scaling: every rank runs its own Wan layer
+(24 units, seed = rank), so the job has 24*N units.
+
+Extra figures in the same JSON line: the density of the coverage-rule mask on
+the stated generator (~0.83) and its TFLOP/s, the calibration pass (pooling
++ pooled softmax + batch mean + coverage mask of one cfg3 layer), the
+end-to-end number through the reference-facing API with host buffers, the
+roofline of the attention kernel, sampled clocks, and the CPU oracle timed on
+the host cores.
+
+--impl reference times the reference's CPU path for this operation (dense
+masked fp32 attention, the oracle port in oracle/sinkattn_oracle.py) on the
+host cores, on a bounded sample of the same workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "sink-attn TFLOPS (kept blocks) & layer latency, Wan 32K seq, 1/2/4/8 B200"
+UNIT = "TFLOP/s"
+B, H, S, D = 2, 12, 32768, 128
+NB = S // 128
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        if not self.lines:
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower() in ("active", "1"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world: int, backend: str):
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=300))
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# CPU (reference path) timing
+# ---------------------------------------------------------------------------
+def cpu_attention_sample(q, k, v, mask, units, q_blocks):
+    """Time the oracle's dense masked attention (the reference's CPU path) on
+    `units` (b, h) pairs x `q_blocks` query blocks each. Returns
+    (seconds, kept FLOPs of the sample)."""
+    from oracle import sinkattn_oracle as orc
+
+    flops = 0.0
+    t0 = time.perf_counter()
+    for (b, h) in units:
+        rows = slice(0, q_blocks * 128)
+        qq = q[b:b + 1, h:h + 1, rows]
+        kk = k[b:b + 1, h:h + 1]
+        vv = v[b:b + 1, h:h + 1]
+        m = mask[0:1, h:h + 1, :q_blocks]
+        orc.dense_masked_attention(qq, kk, vv, m, row_chunk=256)
+        flops += orc.kept_block_flops(m, 1, 1, q_blocks * 128, S)
+    return time.perf_counter() - t0, flops
+
+
+def make_cpu_sample(seed=0):
+    from tests.gen import cfg1_mask, wan_qk
+
+    q, k, v = wan_qk(seed=seed, B=1, H=2, dtype=torch.float32)
+    mask = cfg1_mask(12, NB, NB, seed=1).unsqueeze(0).numpy()[:, :2]
+    # bf16-valued fp32, like the GPU inputs
+    q, k, v = (t.bfloat16().float().numpy() for t in (q, k, v))
+    return q, k, v, mask
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v, mask = make_cpu_sample()
+    units = [(0, 0), (0, 1)]
+    q_blocks = 32
+    for _ in range(max(0, args.warmup)):
+        cpu_attention_sample(q, k, v, mask, units[:1], 4)
+    times, flops = [], 0.0
+    for _ in range(args.steps):
+        dt, flops = cpu_attention_sample(q, k, v, mask, units, q_blocks)
+        times.append(dt)
+    total = sum(times)
+    value = flops * args.steps / total / 1e12
+    sample = (f"{len(units)} (b,h) units x {q_blocks} query blocks x all 256 key blocks of the "
+              f"Wan layer (cfg1-style mask, rho~0.21), dense masked fp32 numpy per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE cfg2 generator)",
+        "config": {"workload": "wan_sink_attention_layer", "B": B, "H": H, "S": S, "D": D,
+                   "mask": "col0|diag|bernoulli(0.2)", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def kept_flops(mask_bhqk: torch.Tensor) -> float:
+    # S is a multiple of 128 here: every kept block is a full 128 x 128 tile
+    return 4.0 * D * 128 * 128 * float(mask_bhqk.sum().item())
+
+
+def time_steps(fn, steps, stream, per_launch_events=True):
+    """Device time of `steps` calls (ms) with CUDA events on `stream`."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    return t0.elapsed_time(t1), per
+
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_dist(world, "nccl")
+    from sinkattn_b200 import _lib, ops
+    from sinkattn_b200.reference_api import _block_sparse_attn
+    from tests.gen import cfg1_mask, wan_qk
+
+    _lib.load()
+    peaks, peak_kind = load_peaks()
+    stream = torch.cuda.current_stream(dev)
+
+    # inputs: Wan layout (BSHD memory viewed as BHSD), seed = rank
+    qh, kh, vh = wan_qk(seed=rank, dtype=torch.bfloat16)  # [B,H,S,D] on CPU
+    q_bshd = qh.permute(0, 2, 1, 3).contiguous()
+    k_bshd = kh.permute(0, 2, 1, 3).contiguous()
+    v_bshd = vh.permute(0, 2, 1, 3).contiguous()
+    del qh, kh, vh
+    q = q_bshd.to(dev).permute(0, 2, 1, 3)
+    k = k_bshd.to(dev).permute(0, 2, 1, 3)
+    v = v_bshd.to(dev).permute(0, 2, 1, 3)
+    mask20 = cfg1_mask(H, NB, NB, seed=1).unsqueeze(0).expand(B, -1, -1, -1).contiguous().to(dev)
+    flops20 = kept_flops(mask20)
+    out = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=dev).permute(0, 2, 1, 3)
+    lse = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+
+    def step20():
+        ops.bsattn_fwd(q, k, v, mask20, out=out, lse=lse)
+
+    # calibration pass on this layer's Q/K: pool + softmax + batch mean + mask
+    ws = torch.empty(ops.pool_scores_workspace_size(B, H, S, D), dtype=torch.uint8, device=dev)
+    calib = {}
+
+    def step_calib():
+        _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
+        calib["mask"], _ = ops.coverage_mask(bm, force_sink_col=True)
+
+    step_calib()
+    torch.cuda.synchronize()
+    mask83 = calib["mask"].unsqueeze(0).expand(B, -1, -1, -1).contiguous()
+    density83 = float(mask83.float().mean().item())
+    flops83 = kept_flops(mask83)
+
+    def step83():
+        ops.bsattn_fwd(q, k, v, mask83, out=out, lse=lse)
+
+    for _ in range(max(3, args.warmup)):
+        step20()
+        step83()
+        step_calib()
+    torch.cuda.synchronize()
+
+    # ---- headline: rho ~ 0.21 -------------------------------------------
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        total_ms, per_ms = time_steps(step20, args.steps, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    max_ms = max_over_ranks(total_ms, world, dev)
+    ms_step = max_ms / args.steps
+    value = flops20 * world * args.steps / (max_ms / 1e3) / 1e12
+    avg_launch_ms = statistics.mean(per_ms)
+    achieved = flops20 / (avg_launch_ms / 1e3) / 1e12
+
+    # ---- coverage-rule mask (rho ~ 0.83) ----------------------------------
+    barrier(world)
+    t83, per83 = time_steps(step83, args.steps, stream)
+    t83 = max_over_ranks(t83, world, dev)
+    # ---- calibration pass ---------------------------------------------------
+    tcal, percal = time_steps(step_calib, args.steps, stream)
+    tcal = max_over_ranks(tcal, world, dev)
+    calib_bytes = 2 * B * H * S * D * 2 + H * NB * NB  # read Q,K (bf16) + write mask
+    pool_only = {}
+
+    def step_pool_only():
+        ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
+
+    tpool, _ = time_steps(step_pool_only, args.steps, stream)
+
+    # ---- end to end through the reference-facing API (host buffers) ---------
+    qp = q_bshd.pin_memory()
+    kp = k_bshd.pin_memory()
+    vp = v_bshd.pin_memory()
+    out_h = torch.empty(B, S, H, D, dtype=torch.bfloat16).pin_memory()
+    lse_h = torch.empty(B, H, S, 1, dtype=torch.bfloat16).pin_memory()
+    q_d = torch.empty_like(q_bshd, device=dev)
+    k_d = torch.empty_like(k_bshd, device=dev)
+    v_d = torch.empty_like(v_bshd, device=dev)
+
+    def step_e2e():
+        q_d.copy_(qp, non_blocking=True)
+        k_d.copy_(kp, non_blocking=True)
+        v_d.copy_(vp, non_blocking=True)
+        o, l = _block_sparse_attn(q_d.permute(0, 2, 1, 3), k_d.permute(0, 2, 1, 3),
+                                  v_d.permute(0, 2, 1, 3), mask20, return_lse=True)
+        out_h.copy_(o.permute(0, 2, 1, 3), non_blocking=True)
+        lse_h.copy_(l, non_blocking=True)
+
+    for _ in range(2):
+        step_e2e()
+    torch.cuda.synchronize()
+    barrier(world)
+    te2e, _ = time_steps(step_e2e, args.steps, stream)
+    barrier(world)
+    te2e = max_over_ranks(te2e, world, dev)
+    e2e_value = flops20 * world * args.steps / (te2e / 1e3) / 1e12
+    h2d = 3 * B * S * H * D * 2
+    d2h = B * S * H * D * 2 + B * H * S * 2
+
+    # ---- CPU baseline (rank 0, N=1 only) ------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        cq, ck, cv, cm = make_cpu_sample()
+        cpu_attention_sample(cq, ck, cv, cm, [(0, 0)], 2)
+        dt, fl = cpu_attention_sample(cq, ck, cv, cm, [(0, 0), (0, 1)], 32)
+        cpu = {"value": fl / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": "2 (b,h) units x 32 query blocks x 256 key blocks, rho~0.21, "
+                         "dense masked fp32 numpy oracle (the reference's CPU path)"}
+
+    traffic = load_traffic().get("bsattn_fwd_wan_rho21")
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded BASELINE cfg2 generator: N(0,1) + 0.5*PE3D, V ~ N(0,1))",
+        "config": {"workload": "wan_sink_attention_layer (cfg2: B=2,H=12,S=32768,D=128)",
+                   "global_batch": B * world, "seq_len": S, "heads": H, "head_dim": D,
+                   "parallelism": f"(b,h)-units x{world}, no collective",
+                   "mask": "col0|diag|bernoulli(0.2) seed 1",
+                   "density": float(mask20.float().mean().item()),
+                   "l2": "inputs 603 MB > L2 (no flush)"},
+        "layer_latency_ms": ms_step,
+        "coverage_rule_mask": {"density": density83, "ms_per_step": t83 / args.steps,
+                               "value": flops83 * world * args.steps / (t83 / 1e3) / 1e12,
+                               "unit": UNIT},
+        "calibration_layer": {"ms_per_layer": tcal / args.steps,
+                              "pool_scores_ms": tpool / args.steps,
+                              "bytes": calib_bytes,
+                              "gbs": calib_bytes / (tcal / args.steps / 1e3) / 1e9,
+                              "frac_of_hbm": calib_bytes / (tcal / args.steps / 1e3) / 1e9
+                              / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
+                "api": "sinkattn_b200.reference_api._block_sparse_attn"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "sa::attn::bsattn_fwd_kernel",
+                     "peak_kind": f"bf16_tflops ({peak_kind}, burst)",
+                     "algorithmic_flops_per_launch": flops20},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    from sinkattn_b200.ops import DeviceStatus
+
+    DeviceStatus.check(dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

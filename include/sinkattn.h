@@ -1,0 +1,203 @@
+/*
+ * sinkattn.h — C ABI of libsinkattn.so, the sm_100a (B200) implementation of
+ * SinkAttention's two hot paths:
+ *
+ *   1. block-sparse attention forward over kept 128x128 blocks
+ *      (tcgen05 tensor cores, TMEM accumulators, TMA tile loads), and
+ *   2. the calibration chain: 128-token mean pooling of Q/K, pooled-score
+ *      softmax, batch mean / running accumulation, and the 0.85-coverage
+ *      per-row block-mask build.
+ *
+ * Conventions shared by every entry point
+ *   - All pointers are device pointers unless the parameter says "host".
+ *   - Strides are in ELEMENTS, ordered (batch, head, seq, dim) for 4-D
+ *     tensors; the innermost (dim) stride must be 1.
+ *   - Every call is stream-ordered on `stream` and performs no host
+ *     synchronisation and no device allocation; scratch memory, where a
+ *     kernel needs any, is passed in by the caller (see *_workspace_size).
+ *   - Return value: SA_OK (0) or a negative SA_E* code. The message of the
+ *     last failure on the calling thread is returned by sa_last_error().
+ *   - `status` arguments (nullable) point to one device int32 that a kernel
+ *     sets to a non-zero SA_DEV_* code when one of its bounded waits gives
+ *     up; the kernel then returns early instead of spinning. The host reads
+ *     it when convenient (it is never read inside these calls).
+ */
+#ifndef SINKATTN_H_
+#define SINKATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#define SA_API __attribute__((visibility("default")))
+#else
+#define SA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SA_OK 0
+#define SA_EINVAL (-1)       /* bad argument (shape, stride, alignment, null) */
+#define SA_EUNSUPPORTED (-2) /* valid request this build does not implement */
+#define SA_ETIMEOUT (-3)     /* reserved: a device wait gave up (see status) */
+#define SA_ECUDA (-4)        /* a CUDA runtime / driver call failed */
+
+/* Device status codes written into `status` by kernels. */
+#define SA_DEV_OK 0
+#define SA_DEV_WAIT_TIMEOUT 1 /* an mbarrier wait exceeded its iteration limit */
+#define SA_DEV_BAD_INDEX 2    /* an index check failed (bounds-check builds) */
+
+/* Mask-builder modes (offline_text_video_coverage_mode). */
+#define SA_COVERAGE_JOINT 0
+#define SA_COVERAGE_VIDEO_RESIDUAL 1
+
+/* Row flags written by sa_coverage_mask (bit set). */
+#define SA_ROW_TIE_AT_CUT 1u      /* equal scores straddle the cut: order is a tie-break */
+#define SA_ROW_NEAR_TARGET 2u     /* a cumulative sum is within 2 ulp of the target */
+#define SA_ROW_EMPTY_FALLBACK 4u  /* the row was empty and kept its top-1 block */
+
+SA_API const char* sa_last_error(void);
+SA_API int sa_version(void);
+/* Number of SMs of the current device (cached per device). */
+SA_API int sa_device_sm_count(void);
+
+/*
+ * Block-sparse attention forward.
+ * Replaces: block_sparse_attn_func(q_unpad, k_unpad, v_unpad, cu_seqlens_q,
+ *   cu_seqlens_k, head_mask_type, streaming_info, base_blockmask, max_seqlen_q,
+ *   max_seqlen_k, p_dropout=0.0, deterministic=True, softmax_scale=None,
+ *   is_causal=False, exact_streaming=False, return_attn_probs=...)
+ *   called at sinkattention/sparse_attention.py:735-771 (external package
+ *   mit-han-lab/Block-Sparse-Attention, imported at sparse_attention.py:22-28).
+ *
+ * q [B,H,Sq,D], k/v [B,H,Sk,D], out [B,H,Sq,D]: bf16, any layout whose
+ *   strides are multiples of 8 elements (16 bytes) with stride(dim)=1 and
+ *   16-byte aligned base pointers. D must be 128.
+ * block_mask: uint8 (torch.bool) [Bm, Hm, ceil(Sq/128), ceil(Sk/128)] with
+ *   element strides m_strides (Bm is 1 or B; a batch stride of 0 broadcasts).
+ * head_mask_type: nullable device int32 [H]. NULL => head h uses mask head h
+ *   (requires Hm == H). Otherwise value t > 0 => head h uses mask head t-1
+ *   and value 0 => head h is dense (all blocks). Negative values (streaming
+ *   heads upstream) are not supported; the library never reads device
+ *   memory on the host, so the Python layer rejects them before the call and
+ *   the kernel treats them as dense.
+ * softmax_scale: <= 0 selects 1/sqrt(D).
+ * lse: nullable fp32 [B,H,Sq] contiguous, natural-log logsumexp per row. Rows
+ *   whose mask row keeps no block produce out = 0 and lse = -inf.
+ */
+SA_API int sa_bsattn_fwd(const void* q, const void* k, const void* v,
+                  const int64_t q_strides[4], const int64_t k_strides[4],
+                  const int64_t v_strides[4], int B, int H, int Sq, int Sk,
+                  int D, const uint8_t* block_mask, const int64_t m_strides[4],
+                  int Hm, const int32_t* head_mask_type, float softmax_scale,
+                  void* out, const int64_t o_strides[4], float* lse,
+                  int32_t* status, cudaStream_t stream);
+
+/*
+ * Scratch bytes sa_pool_scores needs: pooled Q and K in fp32 plus the fp32
+ * pooled logits, 4 * B * H * nb * (2 * D + nb) bytes with nb = ceil(S/block).
+ */
+SA_API size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int block);
+
+/*
+ * Pooled block scores, `mean` mode.
+ * Replaces: _compute_pooled_qk_block_scores (sinkattention/sparse_attention.py:118-142)
+ *   with pooling_mode="mean": q_pool = _mean_pool_sequence(q.float(), block)
+ *   (replicate-pads the last partial block with the final token,
+ *   sparse_attention.py:79-94), scores = q_pool @ k_pool^T * scale,
+ *   softmax over the key-block axis.
+ * q, k: bf16 [B,H,S,D] strided (stride(dim) == 1). D <= 256, block >= 1.
+ * scores: nullable fp32 [B,H,nb,nb] contiguous softmax rows.
+ * batch_mean: nullable fp32 [H,nb,nb] contiguous = scores.mean(dim=0)
+ *   (SinkMaskCalibrator.record, sparse_attention.py:580-581).
+ * At least one of scores / batch_mean must be non-NULL.
+ * workspace: device scratch of sa_pool_scores_workspace_size() bytes.
+ * scale <= 0 selects 1/sqrt(D).
+ */
+SA_API int sa_pool_scores(const void* q, const void* k, const int64_t q_strides[4],
+                   const int64_t k_strides[4], int B, int H, int S, int D,
+                   int block, float scale, float* scores, float* batch_mean,
+                   void* workspace, size_t ws_bytes, cudaStream_t stream);
+
+/*
+ * Running score statistics of one layer.
+ * Replaces: SinkMaskCalibrator._accumulate_score (sparse_attention.py:537-549)
+ *   on a device-resident accumulator: sum += x, sumsq += x*x, where x is an
+ *   fp32 [n] tensor (typically the batch mean [H,nq,nk]). With `first` != 0
+ *   the accumulators are overwritten (sum = x, sumsq = x*x).
+ */
+SA_API int sa_score_accumulate(const float* x, int64_t n, float* sum, float* sumsq,
+                        int first, cudaStream_t stream);
+
+/*
+ * mean = sum / count; std = sqrt(clamp_min(sumsq / count - mean^2, 0)).
+ * Replaces: SinkMaskCalibrator._build_mean_and_masks (sparse_attention.py:563-566).
+ * `count` is a device fp32 tensor [n] (presence-weighted, as in Z-Image,
+ * zimg/runtime/sink_sparse_zimage.py:330-334) or NULL with a scalar
+ * `scalar_count`. std is nullable.
+ */
+SA_API int sa_score_finalize(const float* sum, const float* sumsq, const float* count,
+                      float scalar_count, int64_t n, float* mean, float* std_out,
+                      cudaStream_t stream);
+
+/*
+ * Per-row minimal coverage block mask.
+ * Replaces: _build_direct_mean_coverage_mask (sinkattention/sparse_attention.py:268-376)
+ *   including _build_offline_required_mask (sparse_attention.py:241-265).
+ * scores: fp32 [H,nq,nk] with element strides s_strides[3] (stride(-1) == 1).
+ * mode: SA_COVERAGE_JOINT (lines 334-376) or SA_COVERAGE_VIDEO_RESIDUAL
+ *   (lines 286-332; needs text_blocks > 0, else JOINT is used as upstream does).
+ * coverage: offline_direct_coverage (clamped to [0,1] as line 276 does).
+ * text_blocks: number of required leading query rows / key columns
+ *   (ceil(text_length/block_size) when force_text_global_attention, else 0).
+ * force_sink_col: non-zero adds key column 0 to the required set of every
+ *   row before the coverage step (the "always keep key-block 0" rule; 0
+ *   reproduces the unmodified reference).
+ * row_total / row_selected: nullable fp32 [H,nq] contiguous. When given, they
+ *   are used verbatim as sum_j s[j] and sum_j s[j]*req[j] (lines 334, 339);
+ *   when NULL they are computed on the device in fp64 and rounded to fp32.
+ * mask_out: uint8 [H,nq,nk] contiguous (0/1, torch.bool compatible).
+ * row_flags: nullable int32 [H,nq], SA_ROW_* bits.
+ * nk <= 4096.
+ */
+SA_API int sa_coverage_mask(const float* scores, const int64_t s_strides[3], int H,
+                     int nq, int nk, int mode, float coverage,
+                     int keep_diagonal, int text_blocks, int force_sink_col,
+                     const float* row_total, const float* row_selected,
+                     uint8_t* mask_out, int32_t* row_flags,
+                     cudaStream_t stream);
+
+/*
+ * Sequence mean pooling with optional kept prefix.
+ * Replaces: _mean_pool_sequence_preserve_prefix (sparse_attention.py:97-115),
+ *   used for the pooled K/V of the dynamic branch
+ *   (wanx/runtime/sink_sparse_wan.py:220-232). The tail is replicate-padded
+ *   to a multiple of `pool` (sparse_attention.py:79-85). x, out: bf16,
+ *   [B,H,S,D] -> [B,H,prefix + ceil((S-prefix)/pool),D]; fp32 accumulation,
+ *   one rounding to bf16.
+ */
+SA_API int sa_mean_pool_seq(const void* x, const int64_t x_strides[4], int B, int H,
+                     int S, int D, int pool, int prefix, void* out,
+                     const int64_t o_strides[4], cudaStream_t stream);
+
+/*
+ * Adaptive LSE mix of the sink and dynamic branches.
+ * Replaces: _mix_attention_outputs (sinkattention/sparse_attention.py:898-919)
+ *   with mixing_mode="adaptive": w_s = lse_s, w_d = lse_d + ln(gap),
+ *   alpha = e^{w_s}/(e^{w_s}+e^{w_d}), out = alpha*o_s + (1-alpha)*o_d.
+ * o_s, o_d, out: bf16 [B,H,S,D] strided; lse_s, lse_d: fp32 [B,H,S]
+ *   contiguous (natural log).
+ */
+SA_API int sa_mix_outputs(const void* o_s, const int64_t os_strides[4], const float* lse_s,
+                   const void* o_d, const int64_t od_strides[4], const float* lse_d,
+                   int B, int H, int S, int D, float log_gap, void* out,
+                   const int64_t o_strides[4], cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SINKATTN_H_ */

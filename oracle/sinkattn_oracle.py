@@ -1,0 +1,357 @@
+"""CPU oracle for the SinkAttention hot path — TEST INFRASTRUCTURE ONLY.
+
+This module restates, in numpy, the reference algorithms that the CUDA
+library replaces. It is the checker used by tests/, by
+__graft_entry__.smoke() and by bench.py's CPU-baseline / reference arm. The
+product path (sinkattn_b200) never imports it.
+
+Pinning:
+  * Pooling, pooled-score softmax and the coverage mask builder are pinned
+    against golden vectors produced by importing the reference itself
+    (tests/golden/make_golden.py -> tests/golden/*.npz).
+  * Attention: the reference obtains block-sparse attention from the external
+    package mit-han-lab/Block-Sparse-Attention (unpinned, cloned at HEAD per
+    README.md:26-33, absent here), so there is no reference output for masked
+    attention. The dense-masked fp32 definition below is pinned against the
+    reference's own dense path `_dense_short_attention_with_lse`
+    (sinkattention/sparse_attention.py:870-895) on all-true masks and through
+    the reference's WanSinkSparseInnerAttention with this oracle installed as
+    block_sparse_attn_func (golden vectors); the masked case itself is
+    "parity unpinned" beyond that definition.
+
+Rounding facts reproduced (probed on CPU torch 2.11):
+  * torch.cumsum on fp32 accumulates in fp64 and rounds every prefix to fp32.
+  * coverage * total is an fp32 multiply (python float cast to fp32).
+  * torch.sum's fp32 order is implementation-defined (vectorised cascade);
+    callers that need bit-exact decisions pass the reference's own totals.
+  * torch.sort on CPU is not stable; this oracle sorts stably (value
+    descending, index ascending) and reports rows whose cut splits a tie.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+LN2 = math.log(2.0)
+
+
+# ---------------------------------------------------------------------------
+# bf16 helpers (inputs on the GPU are bf16; the reference upcasts with .float())
+# ---------------------------------------------------------------------------
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to the nearest bf16 (ties to even), returned as fp32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    lsb = (u >> 16) & 1
+    r = ((u + 0x7FFF + lsb) >> 16) << 16
+    out = r.astype(np.uint32).view(np.float32)
+    nan = np.isnan(x)
+    if nan.any():
+        out = out.copy()
+        out[nan] = np.nan
+    return out
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 values already on the bf16 grid -> uint16 bit patterns."""
+    return (np.ascontiguousarray(x, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def from_bf16_bits(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Pooling and pooled scores
+# ---------------------------------------------------------------------------
+def mean_pool_sequence(x: np.ndarray, pool: int) -> np.ndarray:
+    """_mean_pool_sequence (sinkattention/sparse_attention.py:88-94) with the
+    replicate padding of _pad_to_multiple (lines 79-85). x: [B,H,S,D] fp32."""
+    if pool <= 1:
+        return x
+    B, H, S, D = x.shape
+    rem = S % pool
+    if rem:
+        pad = np.repeat(x[:, :, -1:, :], pool - rem, axis=2)
+        x = np.concatenate([x, pad], axis=2)
+    nb = x.shape[2] // pool
+    return x.reshape(B, H, nb, pool, D).astype(np.float64).mean(axis=3).astype(np.float32)
+
+
+def mean_pool_sequence_preserve_prefix(x: np.ndarray, pool: int, prefix: int = 0) -> np.ndarray:
+    """_mean_pool_sequence_preserve_prefix (sparse_attention.py:97-115)."""
+    if pool <= 1:
+        return x
+    S = x.shape[2]
+    prefix = min(max(int(prefix), 0), S)
+    if prefix <= 0:
+        return mean_pool_sequence(x, pool)
+    if prefix >= S:
+        return x
+    return np.concatenate([x[:, :, :prefix], mean_pool_sequence(x[:, :, prefix:], pool)], axis=2)
+
+
+def softmax_lastdim(x: np.ndarray) -> np.ndarray:
+    m = x.max(axis=-1, keepdims=True)
+    e = np.exp((x - m).astype(np.float64))
+    return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+
+
+def pooled_block_scores(q: np.ndarray, k: np.ndarray, block: int = 128) -> np.ndarray:
+    """_compute_pooled_qk_block_scores, pooling_mode="mean"
+    (sparse_attention.py:138-142). q, k: [B,H,S,D] fp32 (bf16 values)."""
+    D = q.shape[-1]
+    qp = mean_pool_sequence(q.astype(np.float32), block)
+    kp = mean_pool_sequence(k.astype(np.float32), block)
+    logits = np.matmul(qp.astype(np.float64), np.swapaxes(kp, -1, -2).astype(np.float64))
+    logits = (logits.astype(np.float32) * np.float32(1.0 / math.sqrt(D))).astype(np.float32)
+    return softmax_lastdim(logits)
+
+
+# ---------------------------------------------------------------------------
+# Coverage mask builder
+# ---------------------------------------------------------------------------
+@dataclass
+class CoverageResult:
+    mask: np.ndarray        # bool [H, nq, nk]
+    tie_rows: np.ndarray    # bool [H, nq]: cut separates equal scores
+    empty_rows: np.ndarray  # bool [H, nq]: top-1 fallback used
+
+
+def required_mask(nq: int, nk: int, text_blocks: int, force_sink_col: bool = False) -> np.ndarray:
+    """_build_offline_required_mask (sparse_attention.py:241-265): the first
+    `text_blocks` key columns and query rows are required. force_sink_col adds
+    key column 0 (the "always keep key-block 0" rule of the benchmark config)."""
+    req = np.zeros((nq, nk), dtype=bool)
+    T = min(text_blocks, nq, nk) if text_blocks > 0 else 0
+    if T > 0:
+        req[:, :T] = True
+        req[:T, :] = True
+    if force_sink_col:
+        req[:, 0] = True
+    return req
+
+
+def _first_reach(cum32: np.ndarray, target: np.float32) -> int:
+    hit = np.nonzero(cum32 >= target)[0]
+    return int(hit[0]) if hit.size else -1
+
+
+def coverage_mask(
+    scores: np.ndarray,
+    coverage: float = 0.85,
+    keep_diagonal: bool = True,
+    text_blocks: int = 0,
+    mode: str = "joint",
+    force_sink_col: bool = False,
+    row_total: np.ndarray | None = None,
+    row_selected: np.ndarray | None = None,
+) -> CoverageResult:
+    """_build_direct_mean_coverage_mask (sparse_attention.py:268-376).
+
+    joint (lines 334-376) and video_residual (lines 286-332, only with
+    text_blocks > 0, as line 286-290 requires). row_total / row_selected, when
+    given, replace the fp32 row sums of lines 334 and 339 (video mode: the
+    sum over columns >= T of line 301); otherwise they are fp64 sums rounded
+    to fp32.
+    """
+    s = np.ascontiguousarray(scores, dtype=np.float32)
+    H, nq, nk = s.shape
+    cov = np.float32(min(max(float(coverage), 0.0), 1.0))
+    T = min(text_blocks, nq, nk) if text_blocks > 0 else 0
+    video = mode in ("video_residual", "video_residual_only", "residual_video") and T > 0
+    req = required_mask(nq, nk, T, force_sink_col and not video)
+    mask = np.zeros((H, nq, nk), dtype=bool)
+    ties = np.zeros((H, nq), dtype=bool)
+    empty = np.zeros((H, nq), dtype=bool)
+    eps = np.float32(1e-6)
+    for h in range(H):
+        for i in range(nq):
+            row = s[h, i]
+            if T > 0 and i < T:
+                mask[h, i, :] = True
+                continue
+            if video:
+                cols = np.arange(T, nk)
+                vals = row[T:]
+                if row_total is not None:
+                    total = np.float32(row_total[h, i])
+                else:
+                    total = np.float32(vals.astype(np.float64).sum())
+                total = max(total, eps)
+                target = np.float32(cov * total)
+                keep = np.zeros(nk, dtype=bool)
+                keep[:T] = True
+                order = np.argsort(-vals.astype(np.float64), kind="stable")
+                sv = vals[order]
+                sv = np.where(np.isfinite(sv), sv, np.float32(0)).astype(np.float32)
+                cum = np.cumsum(sv.astype(np.float64)).astype(np.float32)
+                n_cand = nk - T
+                if target > eps:
+                    f = _first_reach(cum, target)
+                    k = f + 1 if f >= 0 else n_cand
+                else:
+                    k = 0
+                k = max(0, min(k, n_cand))
+                keep[cols[order[:k]]] = True
+                if 0 < k < n_cand and sv[k - 1] == sv[k]:
+                    ties[h, i] = True
+                if not keep.any():
+                    keep[int(np.argmax(row))] = True
+                    empty[h, i] = True
+                mask[h, i] = keep
+                continue
+            r = req[i]
+            if row_total is not None:
+                total = np.float32(row_total[h, i])
+            else:
+                total = np.float32(row.astype(np.float64).sum())
+            if row_selected is not None:
+                selected = np.float32(row_selected[h, i])
+            else:
+                selected = np.float32((row.astype(np.float64) * r).sum())
+            total = max(total, eps)
+            target = np.float32(cov * total)
+            resid = np.float32(max(np.float32(target - selected), np.float32(0.0)))
+            cand = np.where(r, -np.inf, row.astype(np.float64))
+            order = np.argsort(-cand, kind="stable")
+            sv = row[order].astype(np.float32)
+            sv = np.where(r[order], np.float32(0), sv)
+            sv = np.where(np.isfinite(sv), sv, np.float32(0)).astype(np.float32)
+            cum = np.cumsum(sv.astype(np.float64)).astype(np.float32)
+            n_cand = int((~r).sum())
+            if resid > eps:
+                f = _first_reach(cum, resid)
+                k = f + 1 if f >= 0 else n_cand
+            else:
+                k = 0
+            k = max(0, min(k, nk))
+            keep = r.copy()
+            keep[order[:k]] = True
+            if 0 < k < n_cand and sv[k - 1] == sv[k]:
+                ties[h, i] = True
+            if keep_diagonal and i < min(nq, nk):
+                keep[i] = True
+            if not keep.any():
+                keep[order[0]] = True
+                empty[h, i] = True
+                if n_cand > 1 and sv[0] == sv[1]:
+                    ties[h, i] = True
+            mask[h, i] = keep
+    return CoverageResult(mask=mask, tie_rows=ties, empty_rows=empty)
+
+
+# ---------------------------------------------------------------------------
+# Calibrator statistics
+# ---------------------------------------------------------------------------
+def accumulate(sum_: np.ndarray | None, sumsq: np.ndarray | None, x: np.ndarray):
+    """SinkMaskCalibrator._accumulate_score (sparse_attention.py:537-549)."""
+    x = x.astype(np.float32)
+    if sum_ is None:
+        return x.copy(), (x * x).astype(np.float32)
+    return (sum_ + x).astype(np.float32), (sumsq + x * x).astype(np.float32)
+
+
+def finalize(sum_: np.ndarray, sumsq: np.ndarray, count) -> tuple[np.ndarray, np.ndarray]:
+    """_build_mean_and_masks (sparse_attention.py:563-566)."""
+    mean = (sum_ / np.float32(count) if np.isscalar(count) else sum_ / count).astype(np.float32)
+    second = (sumsq / np.float32(count) if np.isscalar(count) else sumsq / count).astype(np.float32)
+    var = np.maximum(second - mean * mean, 0).astype(np.float32)
+    return mean, np.sqrt(var).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------
+def dense_masked_attention(
+    q: np.ndarray,
+    k: np.ndarray,
+    v: np.ndarray,
+    block_mask: np.ndarray,
+    scale: float | None = None,
+    block: int = 128,
+    head_mask_type: np.ndarray | None = None,
+    row_chunk: int = 512,
+) -> tuple[np.ndarray, np.ndarray]:
+    """Dense masked attention, the definition of block_sparse_attn_func
+    (called at sinkattention/sparse_attention.py:735-771): per (b, h),
+    softmax(q k^T * scale + M) v where M is -inf outside kept 128x128 blocks.
+
+    q [B,H,Sq,D], k/v [B,H,Sk,D] fp32; block_mask bool [Bm,Hm,nq,nk] (Bm 1 or B).
+    head_mask_type None => head h uses mask head h; else value t>0 => mask
+    head t-1, 0 => dense. Returns out fp32 [B,H,Sq,D] and natural-log
+    lse fp32 [B,H,Sq]; rows with no kept block give out 0 and lse -inf.
+    """
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    out = np.zeros((B, H, Sq, D), dtype=np.float32)
+    lse = np.full((B, H, Sq), -np.inf, dtype=np.float32)
+    for b in range(B):
+        mb = block_mask[b if block_mask.shape[0] > 1 else 0]
+        for h in range(H):
+            if head_mask_type is None:
+                bm = mb[h]
+            elif int(head_mask_type[h]) > 0:
+                bm = mb[int(head_mask_type[h]) - 1]
+            else:
+                bm = np.ones_like(mb[0])
+            tok = np.repeat(np.repeat(bm, block, axis=0), block, axis=1)[:Sq, :Sk]
+            kt = k[b, h].astype(np.float32).T
+            for r0 in range(0, Sq, row_chunk):
+                r1 = min(Sq, r0 + row_chunk)
+                sc = (q[b, h, r0:r1].astype(np.float32) @ kt) * np.float32(scale)
+                sc = np.where(tok[r0:r1], sc, -np.inf)
+                m = sc.max(axis=-1, keepdims=True)
+                ok = np.isfinite(m[:, 0])
+                m = np.where(np.isfinite(m), m, 0)
+                p = np.exp(sc - m)
+                l = p.sum(axis=-1, keepdims=True)
+                with np.errstate(invalid="ignore", divide="ignore"):
+                    o = (p @ v[b, h].astype(np.float32)) / l
+                    lr = (np.log(l[:, 0]) + m[:, 0]).astype(np.float32)
+                o[~ok] = 0
+                lr[~ok] = -np.inf
+                out[b, h, r0:r1] = o
+                lse[b, h, r0:r1] = lr
+    return out, lse
+
+
+def mix_outputs(sink_out, sink_lse, dyn_out, dyn_lse, sample_gap: int):
+    """_mix_attention_outputs, adaptive (sparse_attention.py:898-919), in fp32.
+    lse arrays [B,H,S] (natural log)."""
+    lg = math.log(float(max(1, int(sample_gap))))
+    ws = sink_lse.astype(np.float64)
+    wd = dyn_lse.astype(np.float64) + lg
+    m = np.maximum(ws, wd)
+    es, ed = np.exp(ws - m), np.exp(wd - m)
+    alpha = (es / (es + ed))[..., None]
+    return (sink_out * alpha + dyn_out * (1 - alpha)).astype(np.float32)
+
+
+def kept_block_flops(block_mask: np.ndarray, B: int, H: int, Sq: int, Sk: int, D: int = 128,
+                     block: int = 128, head_mask_type=None) -> float:
+    """Algorithmic FLOPs of masked attention: 4*D per kept (query, key) pair,
+    counting valid rows x valid columns of every kept block."""
+    nq = (Sq + block - 1) // block
+    nk = (Sk + block - 1) // block
+    rows = np.full(nq, block, dtype=np.int64)
+    rows[-1] = Sq - (nq - 1) * block
+    cols = np.full(nk, block, dtype=np.int64)
+    cols[-1] = Sk - (nk - 1) * block
+    area = np.outer(rows, cols)
+    total = 0
+    for b in range(B):
+        mb = block_mask[b if block_mask.shape[0] > 1 else 0]
+        for h in range(H):
+            if head_mask_type is None:
+                bm = mb[h]
+            elif int(head_mask_type[h]) > 0:
+                bm = mb[int(head_mask_type[h]) - 1]
+            else:
+                bm = np.ones_like(mb[0])
+            total += int((area * bm[:nq, :nk]).sum())
+    return 4.0 * D * total

@@ -1,0 +1,480 @@
+// bsattn_fwd.cu — block-sparse attention forward for sm_100a.
+//
+// Computes, per (batch b, head h, 128-row query tile i), softmax(Q K^T * scale)
+// V over the key blocks j whose mask bit (b, hm(h), i, j) is set, plus the
+// natural-log logsumexp of every query row. This is the operation the
+// reference obtains from the external block_sparse_attn_func
+// (sinkattention/sparse_attention.py:735-771): 128x128 blocks, no dropout,
+// not causal, scale 1/sqrt(D) by default.
+//
+// Kernel structure (one CTA per SM, 384 threads):
+//   warp 0      TMA producer: Q tiles once, then K/V tiles into a 4-slot ring
+//   warp 1      MMA issuer (one thread): S = Q K^T (SS), O += P V (TS)
+//   warp 2      TMEM allocator + kept-block list of slot 0
+//   warp 3      kept-block list of slot 1
+//   warps 4-7   softmax warpgroup of slot 0 (thread t owns query row t)
+//   warps 8-11  softmax warpgroup of slot 1
+// A CTA carries two query tiles ("slots") that ping-pong: while one slot's
+// softmax runs on the CUDA cores, the tensor core works on the other slot.
+//
+// TMEM (512 columns x 128 lanes, fp32): S0 [0,128) S1 [128,256)
+// O0 [256,384) O1 [384,512). P (bf16 pairs) overwrites the first 64 columns
+// of its slot's S and is the A operand of the PV MMA straight from TMEM.
+//
+// Shared memory: Q0, Q1 (32 KB each) and a ring of 4 x 32 KB K/V tiles, all
+// in the 128-byte-swizzled layout TMA writes and UMMA reads (two 64-column
+// boxes per 128x128 tile).
+//
+// Online softmax uses base-2 exponentials with a lazily updated row maximum:
+// the running maximum is only raised (and O, l rescaled) when a block's
+// maximum exceeds it by more than 8 (a factor 256), which keeps every P
+// value <= 256 and leaves the result exact up to rounding.
+
+#include <math.h>
+
+#include "sa_common.cuh"
+
+namespace sa {
+namespace attn {
+
+constexpr int kBM = 128;      // query rows per tile
+constexpr int kBN = 128;      // keys per block
+constexpr int kHD = 128;      // head dim
+constexpr int kStages = 4;    // K/V ring slots
+constexpr int kThreads = 384;
+constexpr int kTileBytes = kBM * kHD * 2;   // 32 KB bf16 tile
+constexpr int kBoxBytes = kTileBytes / 2;   // one 64-column box
+constexpr int kMaxBlocks = 1024;            // max key blocks per row (S <= 131072)
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+struct Params {
+  int B, H, Sq, Sk, nq, nk;
+  const uint8_t* mask;
+  int64_t ms0, ms1, ms2, ms3;
+  const int32_t* head_mask_type;
+  float scale_log2;  // softmax_scale * log2(e)
+  __nv_bfloat16* out;
+  int64_t os0, os1, os2;
+  float* lse;
+  int32_t* status;
+};
+
+struct __align__(8) SmemCtl {
+  uint64_t q_full[2];
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_final[2];
+  uint64_t mma_drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int n_blocks[2];
+  int q_tile[2];
+  int16_t list[2][kMaxBlocks];
+};
+
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
+                              sizeof(SmemCtl);
+
+// The deterministic order in which K/V tiles are produced and consumed:
+//   K(0,0) K(1,0) then for every j: V(0,j) K(0,j+1) V(1,j) K(1,j+1)
+// (entries whose block index is past the slot's count are skipped).
+struct SeqItem {
+  int slot, j, is_v;
+};
+
+template <typename F>
+__device__ __forceinline__ void for_each_item(const int n0, const int n1, F&& f) {
+  const int n[2] = {n0, n1};
+  if (n[0] > 0 && !f(SeqItem{0, 0, 0})) return;
+  if (n[1] > 0 && !f(SeqItem{1, 0, 0})) return;
+  const int nmax = n0 > n1 ? n0 : n1;
+  for (int j = 0; j < nmax; ++j) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      if (j < n[s]) {
+        if (!f(SeqItem{s, j, 1})) return;
+        if (j + 1 < n[s])
+          if (!f(SeqItem{s, j + 1, 0})) return;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bsattn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* q_smem = smem;                      // 2 tiles
+  uint8_t* ring = smem + 2 * kTileBytes;       // kStages tiles
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(ring + kStages * kTileBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.z;
+  const int h = blockIdx.y;
+
+  // ---- set-up: barriers, TMEM, kept-block lists ---------------------------
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&ctl->q_full[s], 1);
+      mbar_init(&ctl->s_full[s], 1);
+      mbar_init(&ctl->p_full[s], kBM);
+      mbar_init(&ctl->o_final[s], 1);
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&ctl->kv_full[i], 1);
+      mbar_init(&ctl->kv_empty[i], 1);
+    }
+    mbar_init(&ctl->mma_drain, 1);
+    ctl->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+  }
+  if (warp == 2) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 2 || warp == 3) {
+    const int s = warp - 2;
+    const int qt = blockIdx.x * 2 + s;
+    int count = 0;
+    if (qt < p.nq) {
+      int mh = h;
+      bool dense = false;
+      if (p.head_mask_type != nullptr) {
+        const int t = p.head_mask_type[h];
+        if (t > 0) mh = t - 1; else dense = true;
+      }
+      const uint8_t* row = p.mask + (int64_t)b * p.ms0 + (int64_t)mh * p.ms1 + (int64_t)qt * p.ms2;
+      for (int c0 = 0; c0 < p.nk; c0 += 32) {
+        const int c = c0 + lane;
+        const bool keep = c < p.nk && (dense || row[(int64_t)c * p.ms3] != 0);
+        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) ctl->list[s][count + __popc(bal & ((1u << lane) - 1u))] = (int16_t)c;
+        count += __popc(bal);
+      }
+    }
+    if (lane == 0) {
+      ctl->n_blocks[s] = count;
+      ctl->q_tile[s] = qt;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem = ctl->tmem_base;
+  const int n0 = ctl->n_blocks[0];
+  const int n1 = ctl->n_blocks[1];
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      for (int s = 0; s < 2; ++s) {
+        if (ctl->n_blocks[s] == 0) continue;
+        uint8_t* dst = q_smem + s * kTileBytes;
+        mbar_arrive_expect_tx(&ctl->q_full[s], kTileBytes);
+        const int row0 = ctl->q_tile[s] * kBM;
+        tma_load_4d(&tm_q, &ctl->q_full[s], dst, 0, row0, h, b);
+        tma_load_4d(&tm_q, &ctl->q_full[s], dst + kBoxBytes, 64, row0, h, b);
+      }
+      int it = 0;
+      for_each_item(n0, n1, [&](const SeqItem& item) -> bool {
+        const int stage = it % kStages;
+        const uint32_t phase = (uint32_t)(it / kStages) & 1u;
+        if (!mbar_wait(&ctl->kv_empty[stage], phase ^ 1u, p.status, abort_flag)) return false;
+        uint8_t* dst = ring + stage * kTileBytes;
+        const int kb = ctl->list[item.slot][item.j];
+        const CUtensorMap* map = item.is_v ? &tm_v : &tm_k;
+        mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
+        tma_load_4d(map, &ctl->kv_full[stage], dst, 0, kb * kBN, h, b);
+        tma_load_4d(map, &ctl->kv_full[stage], dst + kBoxBytes, 64, kb * kBN, h, b);
+        ++it;
+        return true;
+      });
+      // Drain: make sure no TMA write is still in flight before the CTA exits.
+      for (int k = (it > kStages ? it - kStages : 0); k < it; ++k) {
+        mbar_wait(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u, p.status,
+                  abort_flag);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = make_idesc_bf16(kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(kBM, kHD, 0, 1);
+      bool ok = true;
+      for (int s = 0; s < 2 && ok; ++s)
+        if (ctl->n_blocks[s] > 0) ok = mbar_wait(&ctl->q_full[s], 0, p.status, abort_flag);
+      tc_fence_after();
+      const uint32_t q_base = smem_u32(q_smem);
+      const uint32_t ring_base = smem_u32(ring);
+      int it = 0;
+      if (ok) {
+        for_each_item(n0, n1, [&](const SeqItem& item) -> bool {
+          const int stage = it % kStages;
+          const uint32_t phase = (uint32_t)(it / kStages) & 1u;
+          if (!mbar_wait(&ctl->kv_full[stage], phase, p.status, abort_flag)) return false;
+          const uint32_t tile = ring_base + stage * kTileBytes;
+          const int s = item.slot;
+          if (!item.is_v) {
+            tc_fence_after();
+            const uint32_t qa = q_base + s * kTileBytes;
+            const uint32_t d = tmem + s * 128;
+#pragma unroll
+            for (int kk = 0; kk < kHD / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+              const uint64_t ad = make_sdesc_sw128(qa + off, 16, 1024);
+              const uint64_t bd = make_sdesc_sw128(tile + off, 16, 1024);
+              mma_ss(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&ctl->kv_empty[stage]);
+            mma_commit(&ctl->s_full[s]);
+          } else {
+            if (!mbar_wait(&ctl->p_full[s], (uint32_t)item.j & 1u, p.status, abort_flag))
+              return false;
+            tc_fence_after();
+            const uint32_t d = tmem + 256 + s * 128;
+            const uint32_t pa = tmem + s * 128;
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              const uint64_t bd = make_sdesc_sw128(tile + kk * 2048, kBoxBytes, 1024);
+              mma_ts(d, pa + kk * 8, bd, idesc_pv, (item.j > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&ctl->kv_empty[stage]);
+            if (item.j == ctl->n_blocks[s] - 1) mma_commit(&ctl->o_final[s]);
+          }
+          ++it;
+          return true;
+        });
+      }
+      // Drain every MMA this thread issued before TMEM can be released.
+      mma_commit(&ctl->mma_drain);
+      mbar_wait(&ctl->mma_drain, 0, p.status, nullptr);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ---------------- softmax warpgroups ----------------
+    const int s = (warp - 4) >> 2;
+    const int wq = warp & 3;                  // TMEM lane quarter of this warp
+    const int row = wq * 32 + lane;           // query row within the tile
+    const int n = ctl->n_blocks[s];
+    const int qt = ctl->q_tile[s];
+    const int grow = qt * kBM + row;          // global query row
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + s * 128;
+    const uint32_t o_addr = tmem + lane_off + 256 + s * 128;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n && ok; ++j) {
+      if (!mbar_wait(&ctl->s_full[s], (uint32_t)j & 1u, p.status, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[4][32];
+      tmem_ld32(s_addr + 0, r[0]);
+      tmem_ld32(s_addr + 32, r[1]);
+      tmem_ld32(s_addr + 64, r[2]);
+      tmem_ld32(s_addr + 96, r[3]);
+      tmem_wait_ld();
+      const int kb = ctl->list[s][j];
+      const int valid = min(kBN, p.Sk - kb * kBN);
+      if (valid < kBN) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(r[c >> 5][c & 31]));
+      mx *= p.scale_log2;
+      float alpha = 1.0f;
+      const bool rescale = mx > m_used + kRescaleThreshold;
+      if (rescale) {
+        alpha = ex2_approx(m_used - mx);  // 0 when m_used = -inf
+        l *= alpha;
+        m_used = mx;
+      }
+      const float neg_m = -m_used;
+      // P = exp2(S*scale*log2e - m) as bf16 pairs over the first 64 columns of S.
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int c = half * 64 + 2 * e;
+          const float p0 = ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, neg_m));
+          const float p1 =
+              ex2_approx(fmaf(__uint_as_float(r[(c + 1) >> 5][(c + 1) & 31]), p.scale_log2, neg_m));
+          l += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        tmem_st32(s_addr + half * 32, pk);
+      }
+      // O was complete for blocks < j when s_full(j) fired; PV(j) waits for p_full.
+      if (rescale && j > 0) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(o_addr + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&ctl->p_full[s]);
+    }
+    // Epilogue: O / l -> bf16 row, natural-log LSE.
+    if (ok && n > 0) ok = mbar_wait(&ctl->o_final[s], 0, p.status, abort_flag);
+    tc_fence_after();
+    if (qt < p.nq) {
+      const bool write = grow < p.Sq;
+      __nv_bfloat16* orow = p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)grow * p.os2;
+      if (n > 0 && ok) {
+        const float inv_l = 1.0f / l;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_wait_ld();
+          if (write) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+              w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+              w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+              w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+              dst[v] = w;
+            }
+          }
+        }
+        if (write && p.lse != nullptr)
+          p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = (m_used + __log2f(l)) * 0.69314718055994531f;
+      } else if (write) {
+        uint4* dst = reinterpret_cast<uint4*>(orow);
+        for (int v = 0; v < kHD / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+        if (p.lse != nullptr) p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = -INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace attn
+}  // namespace sa
+
+// ---------------------------------------------------------------------------
+// Host entry point
+// ---------------------------------------------------------------------------
+namespace {
+
+int make_map_bshd(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int S,
+                  int D) {
+  sa::EncodeTiledFn enc = sa::encode_tiled_fn();
+  if (enc == nullptr) return SA_ECUDA;
+  // dims innermost first: (D, S, H, B); strides in bytes for dims 1..3.
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    sa::set_error("cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return SA_ECUDA;
+  }
+  return SA_OK;
+}
+
+bool strides_ok(const int64_t st[4]) {
+  if (st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] < 0 || (st[i] % 8) != 0) return false;
+  return true;
+}
+
+}  // namespace
+
+extern "C" int sa_bsattn_fwd(const void* q, const void* k, const void* v,
+                             const int64_t q_strides[4], const int64_t k_strides[4],
+                             const int64_t v_strides[4], int B, int H, int Sq, int Sk, int D,
+                             const uint8_t* block_mask, const int64_t m_strides[4], int Hm,
+                             const int32_t* head_mask_type, float softmax_scale, void* out,
+                             const int64_t o_strides[4], float* lse, int32_t* status,
+                             cudaStream_t stream) {
+  using namespace sa::attn;
+  SA_CHECK_ARG(q && k && v && out && block_mask, "sa_bsattn_fwd: null tensor pointer");
+  SA_CHECK_ARG(q_strides && k_strides && v_strides && o_strides && m_strides,
+               "sa_bsattn_fwd: null stride array");
+  SA_CHECK_ARG(D == kHD, "sa_bsattn_fwd: head dim must be 128, got %d", D);
+  SA_CHECK_ARG(B >= 1 && H >= 1 && Sq >= 1 && Sk >= 1,
+               "sa_bsattn_fwd: B, H, Sq, Sk must be >= 1 (got %d, %d, %d, %d)", B, H, Sq, Sk);
+  const int nq = (Sq + kBM - 1) / kBM;
+  const int nk = (Sk + kBN - 1) / kBN;
+  SA_CHECK_ARG(nk <= kMaxBlocks, "sa_bsattn_fwd: Sk=%d exceeds %d key blocks", Sk, kMaxBlocks);
+  SA_CHECK_ARG(B <= 65535 && H <= 65535, "sa_bsattn_fwd: B/H too large");
+  SA_CHECK_ARG(strides_ok(q_strides) && strides_ok(k_strides) && strides_ok(v_strides) &&
+                   strides_ok(o_strides),
+               "sa_bsattn_fwd: q/k/v/out need stride(dim)=1 and other strides multiple of 8 "
+               "elements (16 bytes)");
+  SA_CHECK_ARG(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) % 16 == 0,
+               "sa_bsattn_fwd: q/k/v/out base pointers must be 16-byte aligned");
+  SA_CHECK_ARG(head_mask_type != nullptr || Hm == H,
+               "sa_bsattn_fwd: mask has %d heads but H=%d and no head_mask_type", Hm, H);
+  SA_CHECK_ARG(Hm >= 1, "sa_bsattn_fwd: mask heads must be >= 1");
+
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = make_map_bshd(&tq, q, q_strides, B, H, Sq, D)) != SA_OK) return rc;
+  if ((rc = make_map_bshd(&tk, k, k_strides, B, H, Sk, D)) != SA_OK) return rc;
+  if ((rc = make_map_bshd(&tv, v, v_strides, B, H, Sk, D)) != SA_OK) return rc;
+
+  Params p;
+  p.B = B; p.H = H; p.Sq = Sq; p.Sk = Sk; p.nq = nq; p.nk = nk;
+  p.mask = block_mask;
+  p.ms0 = m_strides[0]; p.ms1 = m_strides[1]; p.ms2 = m_strides[2]; p.ms3 = m_strides[3];
+  p.head_mask_type = head_mask_type;
+  const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf((float)D);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.os0 = o_strides[0]; p.os1 = o_strides[1]; p.os2 = o_strides[2];
+  p.lse = lse;
+  p.status = status;
+
+  int dev = 0;
+  SA_CUDA_TRY(cudaGetDevice(&dev));
+  static bool attr_set[64] = {};  // the attribute is per device
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    SA_CUDA_TRY(cudaFuncSetAttribute(bsattn_fwd_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kSmemBytes));
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  dim3 grid((nq + 1) / 2, H, B);
+  bsattn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}

@@ -1,0 +1,222 @@
+// misc_kernels.cu — the small kernels either side of the two hot paths:
+// device-resident score accumulation and finalisation of the calibrator,
+// sequence mean pooling for the pooled-K/V dynamic branch, and the adaptive
+// LSE mix of the sink and dynamic branches.
+
+#include <math.h>
+
+#include "sa_common.cuh"
+
+namespace sa {
+namespace misc {
+
+// SinkMaskCalibrator._accumulate_score (sinkattention/sparse_attention.py:537-549)
+__global__ void accumulate_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ sum,
+                                  float* __restrict__ sumsq, int first) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const float sq = v * v;
+    if (first) {
+      sum[i] = v;
+      sumsq[i] = sq;
+    } else {
+      sum[i] += v;
+      sumsq[i] += sq;
+    }
+  }
+}
+
+// SinkMaskCalibrator._build_mean_and_masks (sparse_attention.py:563-566) and the
+// presence-weighted variant of zimg/runtime/sink_sparse_zimage.py:330-334.
+__global__ void finalize_kernel(const float* __restrict__ sum, const float* __restrict__ sumsq,
+                                const float* __restrict__ count, float scalar_count, int64_t n,
+                                float* __restrict__ mean, float* __restrict__ std_out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float c = count != nullptr ? count[i] : scalar_count;
+    const float m = sum[i] / c;
+    mean[i] = m;
+    if (std_out != nullptr) {
+      const float second = sumsq[i] / c;
+      std_out[i] = sqrtf(fmaxf(second - m * m, 0.f));
+    }
+  }
+}
+
+// _mean_pool_sequence_preserve_prefix (sparse_attention.py:97-115).
+// grid: (out_rows, B*H); block: D/8 threads x 8 token groups.
+__global__ void mean_pool_seq_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs0, int64_t xs1,
+                                     int64_t xs2, int H, int S, int D, int pool, int prefix,
+                                     __nv_bfloat16* __restrict__ out, int64_t os0, int64_t os1,
+                                     int64_t os2) {
+  __shared__ float red[8][256];
+  const int orow = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int tpr = D >> 3;
+  const int c = threadIdx.x % tpr;
+  const int g = threadIdx.x / tpr;  // 0..7
+  const __nv_bfloat16* base = x + (int64_t)b * xs0 + (int64_t)h * xs1 + (int64_t)c * 8;
+  __nv_bfloat16* obase = out + (int64_t)b * os0 + (int64_t)h * os1 + (int64_t)orow * os2 + c * 8;
+  if (orow < prefix) {
+    if (g == 0)
+      *reinterpret_cast<uint4*>(obase) =
+          __ldg(reinterpret_cast<const uint4*>(base + (int64_t)orow * xs2));
+    return;
+  }
+  const int lo = prefix + (orow - prefix) * pool;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int r = g; r < pool; r += 8) {
+    const int t = min(lo + r, S - 1);  // replicate padding of the final token
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)t * xs2));
+    const __nv_bfloat162* pv = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(pv[e]);
+      acc[2 * e] += f.x;
+      acc[2 * e + 1] += f.y;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[g][c * 8 + e] = acc[e];
+  __syncthreads();
+  if (g == 0) {
+    const float inv = 1.0f / (float)pool;
+    uint4 w;
+    uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        s0 += red[q][c * 8 + 2 * e];
+        s1 += red[q][c * 8 + 2 * e + 1];
+      }
+      pw[e] = pack_bf16x2(s0 * inv, s1 * inv);
+    }
+    *reinterpret_cast<uint4*>(obase) = w;
+  }
+}
+
+// _mix_attention_outputs, adaptive mode (sparse_attention.py:898-919).
+// One thread per 8 output elements.
+__global__ void mix_kernel(const __nv_bfloat16* __restrict__ os, int64_t a0, int64_t a1, int64_t a2,
+                           const float* __restrict__ lse_s, const __nv_bfloat16* __restrict__ od,
+                           int64_t b0, int64_t b1, int64_t b2, const float* __restrict__ lse_d,
+                           int H, int S, int D, float log_gap, __nv_bfloat16* __restrict__ out,
+                           int64_t c0, int64_t c1, int64_t c2, int64_t total_vec) {
+  const int vpr = D >> 3;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total_vec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int vc = (int)(i % vpr);
+    const int64_t r = i / vpr;  // (b*H + h)*S + s
+    const int s = (int)(r % S);
+    const int64_t bh = r / S;
+    const int h = (int)(bh % H);
+    const int b = (int)(bh / H);
+    const float ws = lse_s[r];
+    const float wd = lse_d[r] + log_gap;
+    const float m = fmaxf(ws, wd);
+    const float es = expf(ws - m), ed = expf(wd - m);
+    const float alpha = es / (es + ed);
+    const uint4 va = __ldg(reinterpret_cast<const uint4*>(os + b * a0 + h * a1 + s * a2 + vc * 8));
+    const uint4 vb = __ldg(reinterpret_cast<const uint4*>(od + b * b0 + h * b1 + s * b2 + vc * 8));
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&va);
+    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&vb);
+    uint4 w;
+    uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 fa = __bfloat1622float2(pa[e]);
+      const float2 fb = __bfloat1622float2(pb[e]);
+      pw[e] = pack_bf16x2(fa.x * alpha + fb.x * (1.f - alpha), fa.y * alpha + fb.y * (1.f - alpha));
+    }
+    *reinterpret_cast<uint4*>(out + b * c0 + h * c1 + s * c2 + vc * 8) = w;
+  }
+}
+
+inline unsigned grid_for(int64_t n, int threads) {
+  const int64_t g = (n + threads - 1) / threads;
+  const int64_t cap = (int64_t)sa::sm_count_current_device() * 16;
+  return (unsigned)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+bool strides4_ok(const int64_t s[4]) {
+  return s[3] == 1 && s[0] % 8 == 0 && s[1] % 8 == 0 && s[2] % 8 == 0;
+}
+
+}  // namespace misc
+}  // namespace sa
+
+extern "C" int sa_score_accumulate(const float* x, int64_t n, float* sum, float* sumsq, int first,
+                                   cudaStream_t stream) {
+  SA_CHECK_ARG(x && sum && sumsq, "sa_score_accumulate: null pointer argument");
+  SA_CHECK_ARG(n >= 0, "sa_score_accumulate: n must be >= 0");
+  if (n == 0) return SA_OK;
+  sa::misc::accumulate_kernel<<<sa::misc::grid_for(n, 256), 256, 0, stream>>>(x, n, sum, sumsq,
+                                                                              first);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_score_finalize(const float* sum, const float* sumsq, const float* count,
+                                 float scalar_count, int64_t n, float* mean, float* std_out,
+                                 cudaStream_t stream) {
+  SA_CHECK_ARG(sum && mean, "sa_score_finalize: null pointer argument");
+  SA_CHECK_ARG(std_out == nullptr || sumsq != nullptr, "sa_score_finalize: std needs sumsq");
+  SA_CHECK_ARG(count != nullptr || scalar_count > 0.f, "sa_score_finalize: count must be > 0");
+  SA_CHECK_ARG(n >= 0, "sa_score_finalize: n must be >= 0");
+  if (n == 0) return SA_OK;
+  sa::misc::finalize_kernel<<<sa::misc::grid_for(n, 256), 256, 0, stream>>>(
+      sum, sumsq, count, scalar_count, n, mean, std_out);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_mean_pool_seq(const void* x, const int64_t x_strides[4], int B, int H, int S,
+                                int D, int pool, int prefix, void* out,
+                                const int64_t o_strides[4], cudaStream_t stream) {
+  SA_CHECK_ARG(x && out && x_strides && o_strides, "sa_mean_pool_seq: null pointer argument");
+  SA_CHECK_ARG(B >= 1 && H >= 1 && S >= 1 && pool >= 1, "sa_mean_pool_seq: bad sizes");
+  SA_CHECK_ARG(D >= 8 && D <= 256 && D % 8 == 0, "sa_mean_pool_seq: D must be a multiple of 8 in [8,256]");
+  SA_CHECK_ARG(sa::misc::strides4_ok(x_strides) && sa::misc::strides4_ok(o_strides),
+               "sa_mean_pool_seq: stride(dim) must be 1 and other strides multiples of 8");
+  SA_CHECK_ARG(((uintptr_t)x | (uintptr_t)out) % 16 == 0, "sa_mean_pool_seq: 16-byte alignment");
+  SA_CHECK_ARG((int64_t)B * H <= 65535, "sa_mean_pool_seq: B*H too large");
+  prefix = prefix < 0 ? 0 : (prefix > S ? S : prefix);
+  const int out_rows = (prefix >= S) ? S : prefix + (S - prefix + pool - 1) / pool;
+  const int threads = (D / 8) * 8;
+  // prefix >= S means "no pooling" (line 108-109): every row is a prefix row.
+  const int eff_prefix = prefix >= S ? S : prefix;
+  sa::misc::mean_pool_seq_kernel<<<dim3(out_rows, B * H), threads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), x_strides[0], x_strides[1], x_strides[2], H, S, D,
+      pool, eff_prefix, reinterpret_cast<__nv_bfloat16*>(out), o_strides[0], o_strides[1],
+      o_strides[2]);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_mix_outputs(const void* o_s, const int64_t os_strides[4], const float* lse_s,
+                              const void* o_d, const int64_t od_strides[4], const float* lse_d,
+                              int B, int H, int S, int D, float log_gap, void* out,
+                              const int64_t o_strides[4], cudaStream_t stream) {
+  SA_CHECK_ARG(o_s && o_d && lse_s && lse_d && out && os_strides && od_strides && o_strides,
+               "sa_mix_outputs: null pointer argument");
+  SA_CHECK_ARG(B >= 1 && H >= 1 && S >= 1 && D % 8 == 0 && D >= 8, "sa_mix_outputs: bad sizes");
+  SA_CHECK_ARG(sa::misc::strides4_ok(os_strides) && sa::misc::strides4_ok(od_strides) &&
+                   sa::misc::strides4_ok(o_strides),
+               "sa_mix_outputs: stride(dim) must be 1 and other strides multiples of 8");
+  SA_CHECK_ARG(((uintptr_t)o_s | (uintptr_t)o_d | (uintptr_t)out) % 16 == 0,
+               "sa_mix_outputs: 16-byte alignment");
+  const int64_t total_vec = (int64_t)B * H * S * (D / 8);
+  sa::misc::mix_kernel<<<sa::misc::grid_for(total_vec, 256), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o_s), os_strides[0], os_strides[1], os_strides[2],
+      lse_s, reinterpret_cast<const __nv_bfloat16*>(o_d), od_strides[0], od_strides[1],
+      od_strides[2], lse_d, H, S, D, log_gap, reinterpret_cast<__nv_bfloat16*>(out), o_strides[0],
+      o_strides[1], o_strides[2], total_vec);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}

@@ -1,0 +1,309 @@
+"""Tensor-level wrappers over libsinkattn (torch provides memory and streams).
+
+Every function takes CUDA tensors, passes their data pointers and element
+strides straight to the C ABI (no copies for any strided layout the kernels
+accept) and launches on torch's current stream. CPU tensors are rejected:
+there is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+BLOCK = 128
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "sinkattn_b200 runs on CUDA tensors only (got a tensor on "
+                f"{t.device}); there is no CPU fallback"
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _bf16_view_ok(t: torch.Tensor) -> bool:
+    if t.stride(-1) != 1:
+        return False
+    if any(s % 8 for s in t.stride()[:-1]):
+        return False
+    return t.data_ptr() % 16 == 0
+
+
+def _as_kernel_layout(t: torch.Tensor) -> torch.Tensor:
+    """Return t itself when its strides are TMA/16-byte compatible, else a
+    contiguous copy (the only case where a copy is made)."""
+    return t if _bf16_view_ok(t) else t.contiguous()
+
+
+class DeviceStatus:
+    """One int32 per device that kernels set when a bounded wait gives up."""
+
+    _flags: dict[int, torch.Tensor] = {}
+
+    @classmethod
+    def get(cls, device: torch.device) -> torch.Tensor:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        t = cls._flags.get(idx)
+        if t is None:
+            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+            cls._flags[idx] = t
+        return t
+
+    @classmethod
+    def check(cls, device: Optional[torch.device] = None) -> None:
+        """Synchronise and raise if any kernel on `device` reported a timeout."""
+        devs = [device] if device is not None else [torch.device("cuda", i) for i in cls._flags]
+        for d in devs:
+            t = cls.get(d)
+            v = int(t.item())
+            if v != _lib.SA_DEV_OK:
+                t.zero_()
+                raise RuntimeError(f"sinkattn_b200 device status {v} on {d} "
+                                   "(a bounded wait in a kernel gave up)")
+
+
+def bsattn_fwd(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    block_mask: torch.Tensor,
+    softmax_scale: Optional[float] = None,
+    head_mask_type: Optional[torch.Tensor] = None,
+    return_lse: bool = True,
+    out: Optional[torch.Tensor] = None,
+    lse: Optional[torch.Tensor] = None,
+):
+    """Block-sparse attention forward on [B,H,S,D] bf16 views (any strides).
+
+    block_mask: bool [Bm,Hm,ceil(Sq/128),ceil(Sk/128)], Bm in {1,B}.
+    head_mask_type: optional int32 [H] on the device (t>0 -> mask head t-1,
+    0 -> dense); None -> mask head h for head h.
+    Returns (out [B,H,Sq,D] bf16, lse fp32 [B,H,Sq] or None). `out` defaults to
+    a [B,Sq,H,D]-contiguous buffer viewed as [B,H,Sq,D].
+    """
+    dev = _require_cuda(q, k, v, block_mask, head_mask_type)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RuntimeError(f"bsattn_fwd expects bf16 q/k/v, got {q.dtype}/{k.dtype}/{v.dtype}")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise RuntimeError("bsattn_fwd expects 4-D [B,H,S,D] tensors")
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if k.shape != (B, H, Sk, D) or v.shape != (B, H, Sk, D):
+        raise RuntimeError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    nq, nk = math.ceil(Sq / BLOCK), math.ceil(Sk / BLOCK)
+    if block_mask.dim() != 4 or block_mask.shape[-2:] != (nq, nk):
+        raise RuntimeError(
+            f"block_mask must be [B|1, Hm, {nq}, {nk}], got {tuple(block_mask.shape)}")
+    if block_mask.shape[0] not in (1, B):
+        raise RuntimeError(f"block_mask batch dim must be 1 or {B}")
+    if block_mask.dtype not in (torch.bool, torch.uint8):
+        raise RuntimeError(f"block_mask must be bool/uint8, got {block_mask.dtype}")
+    Hm = block_mask.shape[1]
+    if head_mask_type is not None:
+        if head_mask_type.dtype != torch.int32 or head_mask_type.numel() != H:
+            raise RuntimeError("head_mask_type must be int32 [H]")
+        head_mask_type = head_mask_type.contiguous()
+    q, k, v = _as_kernel_layout(q), _as_kernel_layout(k), _as_kernel_layout(v)
+    if out is None:
+        out = torch.empty((B, Sq, H, D), dtype=q.dtype, device=dev).permute(0, 2, 1, 3)
+    elif not _bf16_view_ok(out):
+        raise RuntimeError("out must have stride(-1)=1, 16-byte strides and alignment")
+    if return_lse and lse is None:
+        lse = torch.empty((B, H, Sq), dtype=torch.float32, device=dev)
+    ms = list(block_mask.stride())
+    if block_mask.shape[0] == 1:
+        ms[0] = 0
+    mstr = (_lib.ctypes.c_int64 * 4)(*ms)
+    scale = -1.0 if softmax_scale is None else float(softmax_scale)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_bsattn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            _lib.strides4(q), _lib.strides4(k), _lib.strides4(v),
+            B, H, Sq, Sk, D,
+            block_mask.data_ptr(), mstr, Hm,
+            _ptr(head_mask_type), scale,
+            out.data_ptr(), _lib.strides4(out),
+            _ptr(lse) if return_lse else None,
+            DeviceStatus.get(dev).data_ptr(),
+            _stream(dev),
+        )
+    _lib.check(rc, "sa_bsattn_fwd")
+    return out, (lse if return_lse else None)
+
+
+def pool_scores_workspace_size(B: int, H: int, S: int, D: int, block: int = BLOCK) -> int:
+    return int(_lib.load().sa_pool_scores_workspace_size(B, H, S, D, block))
+
+
+def pool_scores(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    block: int = BLOCK,
+    scale: Optional[float] = None,
+    want_scores: bool = True,
+    want_batch_mean: bool = False,
+    workspace: Optional[torch.Tensor] = None,
+):
+    """Mean-pooled block scores softmax(pool(q) pool(k)^T * scale).
+
+    q, k: bf16 [B,H,S,D] (any strides with stride(-1)=1). Returns
+    (scores fp32 [B,H,nb,nb] or None, batch_mean fp32 [H,nb,nb] or None).
+    """
+    dev = _require_cuda(q, k)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise RuntimeError("pool_scores expects bf16 q/k")
+    if q.shape != k.shape or q.dim() != 4:
+        raise RuntimeError("pool_scores expects q, k of equal shape [B,H,S,D]")
+    B, H, S, D = q.shape
+    nb = math.ceil(S / block)
+    q, k = _as_kernel_layout(q), _as_kernel_layout(k)
+    need = pool_scores_workspace_size(B, H, S, D, block)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    scores = torch.empty((B, H, nb, nb), dtype=torch.float32, device=dev) if want_scores else None
+    bmean = torch.empty((H, nb, nb), dtype=torch.float32, device=dev) if want_batch_mean else None
+    sc = -1.0 if scale is None else float(scale)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_pool_scores(
+            q.data_ptr(), k.data_ptr(), _lib.strides4(q), _lib.strides4(k),
+            B, H, S, D, block, sc, _ptr(scores), _ptr(bmean),
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream(dev),
+        )
+    _lib.check(rc, "sa_pool_scores")
+    return scores, bmean
+
+
+def coverage_mask(
+    scores: torch.Tensor,
+    coverage: float = 0.85,
+    keep_diagonal: bool = True,
+    text_blocks: int = 0,
+    mode: str = "joint",
+    force_sink_col: bool = False,
+    row_total: Optional[torch.Tensor] = None,
+    row_selected: Optional[torch.Tensor] = None,
+    want_flags: bool = False,
+):
+    """Per-row minimal-coverage block mask from fp32 scores [H,nq,nk] (CUDA).
+
+    Returns (mask bool [H,nq,nk], flags int32 [H,nq] or None)."""
+    dev = _require_cuda(scores, row_total, row_selected)
+    if scores.dim() != 3:
+        raise ValueError(f"Expected [heads, blocks_q, blocks_k] scores, got {tuple(scores.shape)}")
+    if scores.dtype != torch.float32:
+        scores = scores.float()
+    if scores.stride(-1) != 1:
+        scores = scores.contiguous()
+    H, nq, nk = scores.shape
+    mode_id = (_lib.SA_COVERAGE_VIDEO_RESIDUAL
+               if str(mode).strip().lower() in {"video_residual", "video_residual_only", "residual_video"}
+               else _lib.SA_COVERAGE_JOINT)
+    for name, t in (("row_total", row_total), ("row_selected", row_selected)):
+        if t is not None and (t.shape != (H, nq) or t.dtype != torch.float32):
+            raise ValueError(f"{name} must be fp32 [H, nq]")
+    row_total = None if row_total is None else row_total.contiguous()
+    row_selected = None if row_selected is None else row_selected.contiguous()
+    mask = torch.empty((H, nq, nk), dtype=torch.bool, device=dev)
+    flags = torch.empty((H, nq), dtype=torch.int32, device=dev) if want_flags else None
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_coverage_mask(
+            scores.data_ptr(), _lib.strides3(scores), H, nq, nk, mode_id, float(coverage),
+            int(bool(keep_diagonal)), int(text_blocks), int(bool(force_sink_col)),
+            _ptr(row_total), _ptr(row_selected), mask.data_ptr(), _ptr(flags), _stream(dev),
+        )
+    _lib.check(rc, "sa_coverage_mask")
+    return mask, flags
+
+
+def score_accumulate(x: torch.Tensor, sum_: torch.Tensor, sumsq: torch.Tensor, first: bool) -> None:
+    dev = _require_cuda(x, sum_, sumsq)
+    for t in (x, sum_, sumsq):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise RuntimeError("score_accumulate expects contiguous fp32 tensors")
+    if x.numel() != sum_.numel() or x.numel() != sumsq.numel():
+        raise RuntimeError("score_accumulate: size mismatch")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_score_accumulate(x.data_ptr(), x.numel(), sum_.data_ptr(), sumsq.data_ptr(),
+                                     int(bool(first)), _stream(dev))
+    _lib.check(rc, "sa_score_accumulate")
+
+
+def score_finalize(sum_: torch.Tensor, sumsq: torch.Tensor, count) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(sum_, sumsq)
+    mean = torch.empty_like(sum_)
+    std = torch.empty_like(sum_)
+    cnt_t = count if isinstance(count, torch.Tensor) else None
+    if cnt_t is not None:
+        cnt_t = cnt_t.to(device=dev, dtype=torch.float32).contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_score_finalize(sum_.data_ptr(), sumsq.data_ptr(), _ptr(cnt_t),
+                                   float(count) if cnt_t is None else 0.0, sum_.numel(),
+                                   mean.data_ptr(), std.data_ptr(), _stream(dev))
+    _lib.check(rc, "sa_score_finalize")
+    return mean, std
+
+
+def mean_pool_seq(x: torch.Tensor, pool: int, prefix: int = 0) -> torch.Tensor:
+    """_mean_pool_sequence_preserve_prefix on a bf16 [B,H,S,D] view."""
+    dev = _require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError("mean_pool_seq expects bf16")
+    B, H, S, D = x.shape
+    if pool <= 1:
+        return x
+    prefix = min(max(int(prefix), 0), S)
+    if prefix >= S:
+        return x
+    out_rows = prefix + math.ceil((S - prefix) / pool)
+    x = _as_kernel_layout(x)
+    out = torch.empty((B, out_rows, H, D), dtype=x.dtype, device=dev).permute(0, 2, 1, 3)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_mean_pool_seq(x.data_ptr(), _lib.strides4(x), B, H, S, D, int(pool), prefix,
+                                  out.data_ptr(), _lib.strides4(out), _stream(dev))
+    _lib.check(rc, "sa_mean_pool_seq")
+    return out
+
+
+def mix_outputs(sink_out, sink_lse, dyn_out, dyn_lse, sample_gap: int) -> torch.Tensor:
+    """Adaptive LSE mix; lse tensors fp32 [B,H,S] (natural log)."""
+    dev = _require_cuda(sink_out, sink_lse, dyn_out, dyn_lse)
+    B, H, S, D = sink_out.shape
+    sink_out, dyn_out = _as_kernel_layout(sink_out), _as_kernel_layout(dyn_out)
+    sink_lse = sink_lse.reshape(B, H, S).float().contiguous()
+    dyn_lse = dyn_lse.reshape(B, H, S).float().contiguous()
+    out = torch.empty((B, S, H, D), dtype=sink_out.dtype, device=dev).permute(0, 2, 1, 3)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_mix_outputs(sink_out.data_ptr(), _lib.strides4(sink_out), sink_lse.data_ptr(),
+                                dyn_out.data_ptr(), _lib.strides4(dyn_out), dyn_lse.data_ptr(),
+                                B, H, S, D, math.log(float(max(1, int(sample_gap)))),
+                                out.data_ptr(), _lib.strides4(out), _stream(dev))
+    _lib.check(rc, "sa_mix_outputs")
+    return out

@@ -1,0 +1,289 @@
+"""Drop-in replacements for the reference's hot-path entry points.
+
+The reference (bb-2020-bb/sinkattn) reaches its kernels through a handful of
+module-level names. This module provides same-named, same-signature
+functions backed by libsinkattn, and install() binds them into the
+reference's modules so the Wan and Z-Image processors run unchanged:
+
+  sinkattention.sparse_attention.block_sparse_attn_func
+      external Block-Sparse-Attention forward (sparse_attention.py:22-28, 735-771)
+  sinkattention.sparse_attention._block_sparse_attn            (lines 710-776)
+  sinkattention.sparse_attention._compute_pooled_qk_block_scores (lines 118-142)
+  sinkattention.sparse_attention._build_direct_mean_coverage_mask (lines 268-376)
+  sinkattention.sparse_attention._mean_pool_sequence_preserve_prefix (lines 97-115)
+  sinkattention.sparse_attention._mix_attention_outputs        (lines 898-919)
+
+Callers that imported a name into their own namespace are patched too
+(wanx/runtime/sink_sparse_wan.py:10-26, zimg/runtime/sink_sparse_zimage.py:15-26).
+
+Errors follow the reference: shape problems raise ValueError with the same
+messages; kernel failures raise RuntimeError. Nothing here falls back to CPU
+computation — CPU tensors raise.
+"""
+from __future__ import annotations
+
+import math
+import sys
+from typing import Optional
+
+import torch
+
+from . import ops
+
+# How head_mask_type is read by block_sparse_attn_func.
+#   "per_head" (default): a mask with one slice per head is applied per head;
+#       positive entries are ignored, 0 entries mark dense heads. This is the
+#       per-head semantics the sink masks are calibrated with.
+#   "upstream": the Block-Sparse-Attention reading — a positive entry t makes
+#       the head use mask slice t-1 (so the reference's ones(H) would apply
+#       slice 0 to every head), 0 = dense.
+HEAD_MASK_TYPE_MODE = "per_head"
+
+_BLOCK = 128
+
+
+def _hmt_host(head_mask_type: torch.Tensor) -> list[int]:
+    # small int32 [H]; cached on the tensor's identity and version counter
+    key = (head_mask_type.data_ptr(), head_mask_type._version, head_mask_type.numel())
+    cached = _HMT_CACHE.get(key)
+    if cached is None:
+        cached = [int(x) for x in head_mask_type.detach().cpu().tolist()]
+        _HMT_CACHE[key] = cached
+    return cached
+
+
+_HMT_CACHE: dict = {}
+
+
+def block_sparse_attn_func(
+    q_unpad,
+    k_unpad,
+    v_unpad,
+    cu_seqlens_q,
+    cu_seqlens_k,
+    head_mask_type,
+    streaming_info,
+    base_blockmask,
+    max_seqlen_q_,
+    max_seqlen_k_,
+    p_dropout=0.0,
+    deterministic=False,
+    softmax_scale=None,
+    is_causal=False,
+    exact_streaming=False,
+    return_attn_probs=False,
+):
+    """Block-sparse attention forward with the upstream package's signature.
+
+    q_unpad [total_q, H, D], k_unpad/v_unpad [total_k, H, D] (bf16, varlen
+    packing described by cu_seqlens_*), base_blockmask bool
+    [B, Hm, ceil(max_seqlen_q/128), ceil(max_seqlen_k/128)].
+    Returns out [total_q, H, D], or (out, softmax_lse fp32 [B, H, max_seqlen_q],
+    None) when return_attn_probs.
+    """
+    if p_dropout != 0.0:
+        raise NotImplementedError("sinkattn_b200: dropout is not supported (forward inference only)")
+    if is_causal:
+        raise NotImplementedError("sinkattn_b200: causal masking is not supported")
+    if exact_streaming:
+        raise NotImplementedError("sinkattn_b200: streaming heads are not supported")
+    total_q, H, D = q_unpad.shape
+    total_k = k_unpad.shape[0]
+    B = int(cu_seqlens_q.numel()) - 1
+    Sq, Sk = int(max_seqlen_q_), int(max_seqlen_k_)
+    hmt = None
+    if HEAD_MASK_TYPE_MODE == "upstream":
+        hv = _hmt_host(head_mask_type)
+        if any(t < 0 for t in hv):
+            raise NotImplementedError("sinkattn_b200: streaming heads (head_mask_type < 0)")
+        hmt = head_mask_type.to(torch.int32)
+    elif base_blockmask.shape[1] != H:
+        # fewer mask slices than heads only makes sense with the mapping
+        hv = _hmt_host(head_mask_type)
+        if any(t < 0 for t in hv):
+            raise NotImplementedError("sinkattn_b200: streaming heads (head_mask_type < 0)")
+        hmt = head_mask_type.to(torch.int32)
+    if total_q == B * Sq and total_k == B * Sk:
+        # uniform batch: every sequence has the maximum length (the reference's case)
+        q = q_unpad.view(B, Sq, H, D).permute(0, 2, 1, 3)
+        k = k_unpad.view(B, Sk, H, D).permute(0, 2, 1, 3)
+        v = v_unpad.view(B, Sk, H, D).permute(0, 2, 1, 3)
+        out = torch.empty_like(q_unpad)
+        out_v = out.view(B, Sq, H, D).permute(0, 2, 1, 3)
+        _, lse = ops.bsattn_fwd(q, k, v, base_blockmask, softmax_scale=softmax_scale,
+                                head_mask_type=hmt, return_lse=bool(return_attn_probs), out=out_v)
+    else:
+        # ragged varlen batch: one launch per sequence on its own slice
+        cq = [int(x) for x in cu_seqlens_q.detach().cpu().tolist()]
+        ck = [int(x) for x in cu_seqlens_k.detach().cpu().tolist()]
+        out = torch.empty_like(q_unpad)
+        lse = (torch.full((B, H, Sq), float("-inf"), dtype=torch.float32, device=q_unpad.device)
+               if return_attn_probs else None)
+        for b in range(B):
+            sq, sk = cq[b + 1] - cq[b], ck[b + 1] - ck[b]
+            if sq == 0:
+                continue
+            qb = q_unpad[cq[b]:cq[b + 1]].unsqueeze(0).permute(0, 2, 1, 3)
+            kb = k_unpad[ck[b]:ck[b + 1]].unsqueeze(0).permute(0, 2, 1, 3)
+            vb = v_unpad[ck[b]:ck[b + 1]].unsqueeze(0).permute(0, 2, 1, 3)
+            mb = base_blockmask[b:b + 1, :, : math.ceil(sq / _BLOCK), : math.ceil(sk / _BLOCK)]
+            ob = out[cq[b]:cq[b + 1]].unsqueeze(0).permute(0, 2, 1, 3)
+            if sk == 0:
+                ob.zero_()
+                continue
+            _, lb = ops.bsattn_fwd(qb, kb, vb, mb, softmax_scale=softmax_scale, head_mask_type=hmt,
+                                   return_lse=bool(return_attn_probs), out=ob)
+            if lse is not None:
+                lse[b, :, :sq] = lb[0]
+    if return_attn_probs:
+        return out, lse, None
+    return out
+
+
+def _block_sparse_attn(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    block_mask: torch.Tensor,
+    return_lse: bool = True,
+) -> tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """sparse_attention.py:710-776 without the three transpose copies: the
+    kernel reads the strided [B,H,S,D] views directly through TMA. Returns
+    out as a [B,S,H,D]-contiguous tensor viewed [B,H,S,D] (the reference's
+    layout) and lse [B,H,S,1] in q.dtype (line 776)."""
+    B, H, Sq, D = q.shape
+    if HEAD_MASK_TYPE_MODE == "upstream":
+        # the reference passes ones(H): every head reads mask slice 0
+        hmt = torch.ones(H, dtype=torch.int32, device=q.device)
+    else:
+        hmt = None
+    out, lse = ops.bsattn_fwd(q, k, v, block_mask.contiguous(), head_mask_type=hmt,
+                              return_lse=return_lse)
+    if lse is None:
+        return out, None
+    return out, lse.unsqueeze(-1).to(device=q.device, dtype=q.dtype)
+
+
+def _compute_pooled_qk_block_scores(q, k, v, config) -> torch.Tensor:
+    """sparse_attention.py:118-142: block scores softmax(pool(q) pool(k)^T /
+    sqrt(D)) per batch, [B,H,nb,nb] fp32. pooling_mode "mean" is the kernel's
+    rule; "triton" gets the same rule, as the reference itself does whenever
+    its Triton kernel is unavailable or fails (lines 124-137)."""
+    block = int(config.block_size)
+    scores, _ = ops.pool_scores(q.to(torch.bfloat16) if q.dtype != torch.bfloat16 else q,
+                                k.to(torch.bfloat16) if k.dtype != torch.bfloat16 else k,
+                                block=block, scale=1.0 / math.sqrt(q.size(-1)))
+    return scores
+
+
+def _ceil_div(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
+def _build_direct_mean_coverage_mask(mean_scores: torch.Tensor, config) -> torch.Tensor:
+    """sparse_attention.py:268-376 on the GPU. The fp32 row totals (line 334,
+    301) and selected sums (line 339) are taken with the same torch reduction
+    on the same device as the reference, so the decisions are bit-identical;
+    the sort, cumulative sums, cut and scatter run in the CUDA kernel. The
+    mask is returned on the input's device."""
+    if mean_scores.dim() != 3:
+        raise ValueError(f"Expected [heads, blocks_q, blocks_k] scores, got {tuple(mean_scores.shape)}")
+    H, nq, nk = mean_scores.shape
+    coverage = min(max(float(config.offline_direct_coverage), 0.0), 1.0)
+    mode = str(getattr(config, "offline_text_video_coverage_mode", "joint")).strip().lower()
+    text_blocks = 0
+    if bool(getattr(config, "force_text_global_attention", False)) and int(config.text_length) > 0:
+        text_blocks = _ceil_div(int(config.text_length), int(config.block_size))
+    T = min(text_blocks, nq, nk)
+    scores = mean_scores.float()
+    video = mode in {"video_residual", "video_residual_only", "residual_video"} and T > 0
+    if video:
+        row_total = torch.zeros(H, nq, dtype=torch.float32, device=scores.device)
+        if nq - T > 0 and nk - T > 0:
+            row_total[:, T:] = scores[:, T:, T:].sum(dim=-1)
+        row_selected = None
+    else:
+        row_total = scores.sum(dim=-1)
+        if T > 0:
+            req = torch.zeros(nq, nk, dtype=torch.bool, device=scores.device)
+            req[:, :T] = True
+            req[:T, :] = True
+            row_selected = (scores * req.unsqueeze(0).expand(H, -1, -1).float()).sum(dim=-1)
+        else:
+            row_selected = torch.zeros(H, nq, dtype=torch.float32, device=scores.device)
+    dev = scores.device if scores.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    mask, _ = ops.coverage_mask(
+        scores.to(dev), coverage=coverage, keep_diagonal=bool(config.keep_diagonal),
+        text_blocks=T, mode="video_residual" if video else "joint",
+        row_total=row_total.to(dev),
+        row_selected=None if row_selected is None else row_selected.to(dev),
+    )
+    return mask if mean_scores.is_cuda else mask.to(mean_scores.device)
+
+
+def _mean_pool_sequence_preserve_prefix(x: torch.Tensor, pool_size: int, *, prefix_tokens: int = 0):
+    """sparse_attention.py:97-115 (bf16 in/out, fp32 accumulation)."""
+    if pool_size <= 1:
+        return x
+    return ops.mean_pool_seq(x, int(pool_size), int(prefix_tokens))
+
+
+def _mean_pool_sequence(x: torch.Tensor, pool_size: int):
+    """sparse_attention.py:88-94 for bf16 tensors (Z-Image pooled branch)."""
+    if pool_size <= 1:
+        return x
+    return ops.mean_pool_seq(x, int(pool_size), 0)
+
+
+def _mix_attention_outputs(sink_out, sink_lse, dynamic_out, dynamic_lse, config, dynamic_sample_gap=None):
+    """sparse_attention.py:898-919 (adaptive mode) as one fused kernel."""
+    if config.mixing_mode != "adaptive":
+        raise ValueError(f"Unsupported mixing_mode: {config.mixing_mode}")
+    if sink_lse is None or dynamic_lse is None:
+        raise ValueError("Adaptive Sink-Sparse mixing requires both sink_lse and dynamic_lse.")
+    gap = config.sample_gap if dynamic_sample_gap is None else int(dynamic_sample_gap)
+    return ops.mix_outputs(sink_out, sink_lse, dynamic_out, dynamic_lse, gap)
+
+
+_PATCHES = {
+    "sinkattention.sparse_attention": {
+        "block_sparse_attn_func": block_sparse_attn_func,
+        "_HAS_BLOCK_SPARSE": True,
+        "_block_sparse_attn": _block_sparse_attn,
+        "_compute_pooled_qk_block_scores": _compute_pooled_qk_block_scores,
+        "_build_direct_mean_coverage_mask": _build_direct_mean_coverage_mask,
+        "_mean_pool_sequence_preserve_prefix": _mean_pool_sequence_preserve_prefix,
+        "_mix_attention_outputs": _mix_attention_outputs,
+    },
+    "wanx.runtime.sink_sparse_wan": {
+        "_block_sparse_attn": _block_sparse_attn,
+        "_mean_pool_sequence_preserve_prefix": _mean_pool_sequence_preserve_prefix,
+        "_mix_attention_outputs": _mix_attention_outputs,
+    },
+    "zimg.runtime.sink_sparse_zimage": {
+        "_block_sparse_attn": _block_sparse_attn,
+        "_build_direct_mean_coverage_mask": _build_direct_mean_coverage_mask,
+        "_mean_pool_sequence": _mean_pool_sequence,
+        "_mix_attention_outputs": _mix_attention_outputs,
+    },
+}
+
+
+def install(modules: Optional[list[str]] = None) -> list[str]:
+    """Bind the replacements into the reference's modules (importing them if
+    needed). Returns the list of patched module names; modules that cannot be
+    imported are skipped."""
+    import importlib
+
+    patched = []
+    for name, attrs in _PATCHES.items():
+        if modules is not None and name not in modules:
+            continue
+        try:
+            mod = sys.modules.get(name) or importlib.import_module(name)
+        except Exception:  # the caller's environment may lack that route
+            continue
+        for attr, val in attrs.items():
+            setattr(mod, attr, val)
+        patched.append(name)
+    return patched

@@ -1,0 +1,64 @@
+"""Shared pytest set-up: the `gpu` marker, golden-vector access, oracle import."""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+from tests.gen import digest  # noqa: E402
+
+GOLDEN = ROOT / "tests" / "golden" / "golden.npz"
+# Location of a reference checkout for the CPU-only drop-in tests (optional).
+REFERENCE_DIR = Path(os.environ.get("SINKATTN_REFERENCE", "/root/reference"))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA (B200) device")
+
+
+def pytest_collection_modifyitems(config, items):
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def golden():
+    return dict(np.load(GOLDEN, allow_pickle=False))
+
+
+def regen_input(g: dict, case: str, key: str) -> torch.Tensor:
+    """Regenerate a golden case's bf16 input from its seed and check the digest."""
+    shape = tuple(int(x) for x in g[f"{case}/{key}_shape"])
+    seed = int(g[f"{case}/{key}_seed"])
+    gen = torch.Generator().manual_seed(seed)
+    t = torch.randn(*shape, generator=gen).to(torch.bfloat16)
+    want = str(g[f"{case}/{key}_sha256"])
+    got = digest(t)
+    assert got == want, (
+        f"regenerated input {case}/{key} differs from the one the golden vectors were "
+        f"made with (torch generator changed?): {got} != {want}")
+    return t
+
+
+def from_bits(a: np.ndarray) -> np.ndarray:
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    sys.path.insert(0, str(ROOT))
+    from oracle import sinkattn_oracle
+
+    return sinkattn_oracle

@@ -1,0 +1,149 @@
+"""CPU-only checks of the C-ABI boundary: the library loads, exports every
+symbol include/sinkattn.h declares, and rejects bad arguments on the host
+(before any CUDA call) with SA_EINVAL and a message."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "sinkattn.h"
+
+
+def header_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^SA_API\s+[\w\s\*]+?\b(sa_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from sinkattn_b200 import _lib
+
+    return _lib.load()
+
+
+def test_header_declares_symbols():
+    syms = header_symbols()
+    assert "sa_bsattn_fwd" in syms and "sa_coverage_mask" in syms and "sa_pool_scores" in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from sinkattn_b200 import _lib
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    missing = [s for s in header_symbols() if s not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    for s in header_symbols():
+        assert hasattr(lib, s)
+    # the Python binding covers the same set
+    assert sorted(_lib.exported_names()) == header_symbols()
+
+
+def test_version(lib):
+    assert lib.sa_version() == 1
+
+
+def _i64(*v):
+    return (ctypes.c_int64 * len(v))(*v)
+
+
+def test_bsattn_rejects_bad_head_dim(lib):
+    from sinkattn_b200 import _lib
+
+    st = _i64(64 * 4 * 64, 64 * 64, 64, 1)
+    rc = lib.sa_bsattn_fwd(16, 16, 16, st, st, st, 1, 4, 64, 64, 64, 16, _i64(0, 1, 1, 1), 4,
+                           None, -1.0, 16, st, None, None, None)
+    assert rc == _lib.SA_EINVAL
+    assert "head dim must be 128" in _lib.last_error()
+
+
+def test_bsattn_rejects_misaligned_stride(lib):
+    from sinkattn_b200 import _lib
+
+    st = _i64(128 * 3 * 100, 128, 3 * 128 + 4, 1)
+    rc = lib.sa_bsattn_fwd(16, 16, 16, st, st, st, 1, 3, 100, 100, 128, 16, _i64(0, 1, 1, 1), 3,
+                           None, -1.0, 16, st, None, None, None)
+    assert rc == _lib.SA_EINVAL
+    assert "stride" in _lib.last_error()
+
+
+def test_bsattn_rejects_empty_and_null(lib):
+    from sinkattn_b200 import _lib
+
+    st = _i64(128 * 128, 128 * 128, 128, 1)
+    rc = lib.sa_bsattn_fwd(16, 16, 16, st, st, st, 1, 1, 0, 128, 128, 16, _i64(0, 1, 1, 1), 1,
+                           None, -1.0, 16, st, None, None, None)
+    assert rc == _lib.SA_EINVAL
+    rc = lib.sa_bsattn_fwd(None, 16, 16, st, st, st, 1, 1, 128, 128, 128, 16, _i64(0, 1, 1, 1), 1,
+                           None, -1.0, 16, st, None, None, None)
+    assert rc == _lib.SA_EINVAL and "null" in _lib.last_error()
+
+
+def test_bsattn_rejects_mask_head_mismatch(lib):
+    from sinkattn_b200 import _lib
+
+    st = _i64(128 * 4 * 128, 128 * 128, 128, 1)
+    rc = lib.sa_bsattn_fwd(16, 16, 16, st, st, st, 1, 4, 128, 128, 128, 16, _i64(0, 1, 1, 1), 2,
+                           None, -1.0, 16, st, None, None, None)
+    assert rc == _lib.SA_EINVAL and "head_mask_type" in _lib.last_error()
+
+
+def test_pool_scores_workspace_and_validation(lib):
+    from sinkattn_b200 import _lib
+
+    B, H, S, D = 2, 12, 32768, 128
+    nb = 256
+    assert lib.sa_pool_scores_workspace_size(B, H, S, D, 128) == 4 * B * H * nb * (2 * D + nb)
+    assert lib.sa_pool_scores_workspace_size(0, H, S, D, 128) == 0
+    st = _i64(H * S * D, S * D, D, 1)
+    rc = lib.sa_pool_scores(16, 16, st, st, B, H, S, D, 128, -1.0, 16, None, 16, 8, None)
+    assert rc == _lib.SA_EINVAL and "workspace" in _lib.last_error()
+    rc = lib.sa_pool_scores(16, 16, st, st, B, H, S, D, 128, -1.0, None, None, 16, 1 << 40, None)
+    assert rc == _lib.SA_EINVAL and "both NULL" in _lib.last_error()
+    rc = lib.sa_pool_scores(16, 16, st, st, B, H, S, 100, 128, -1.0, 16, None, 16, 1 << 40, None)
+    assert rc == _lib.SA_EINVAL
+
+
+def test_coverage_mask_validation(lib):
+    from sinkattn_b200 import _lib
+
+    st = (ctypes.c_int64 * 3)(5000 * 4, 5000, 1)
+    rc = lib.sa_coverage_mask(16, st, 1, 4, 5000, 0, 0.85, 1, 0, 0, None, None, 16, None, None)
+    assert rc == _lib.SA_EINVAL and "4096" in _lib.last_error()
+    st = (ctypes.c_int64 * 3)(64, 8, 2)
+    rc = lib.sa_coverage_mask(16, st, 1, 8, 8, 0, 0.85, 1, 0, 0, None, None, 16, None, None)
+    assert rc == _lib.SA_EINVAL and "stride" in _lib.last_error()
+    st = (ctypes.c_int64 * 3)(64, 8, 1)
+    rc = lib.sa_coverage_mask(16, st, 1, 8, 8, 7, 0.85, 1, 0, 0, None, None, 16, None, None)
+    assert rc == _lib.SA_EINVAL and "mode" in _lib.last_error()
+
+
+def test_misc_validation(lib):
+    from sinkattn_b200 import _lib
+
+    assert lib.sa_score_accumulate(None, 4, 16, 16, 1, None) == _lib.SA_EINVAL
+    assert lib.sa_score_finalize(16, None, None, 0.0, 4, 16, None, None) == _lib.SA_EINVAL
+    st = _i64(8 * 8, 8 * 8, 8, 1)
+    assert lib.sa_mean_pool_seq(16, st, 1, 1, 8, 12, 2, 0, 16, st, None) == _lib.SA_EINVAL
+
+
+def test_ops_reject_cpu_tensors():
+    """No CPU fallback: the tensor API refuses CPU tensors."""
+    import torch
+
+    from sinkattn_b200 import ops
+
+    q = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16)
+    m = torch.ones(1, 1, 1, 1, dtype=torch.bool)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.bsattn_fwd(q, q, q, m)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.pool_scores(q, q)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.coverage_mask(torch.rand(1, 4, 4))
