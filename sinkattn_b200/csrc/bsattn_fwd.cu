@@ -203,10 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       });
       // Drain: make sure no TMA write is still in flight before the CTA exits.
-      for (int k = (it > kStages ? it - kStages : 0); k < it; ++k) {
-        mbar_wait(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u, p.status,
-                  abort_flag);
-      }
+      for (int k = (it > kStages ? it - kStages : 0); k < it; ++k)
+        mbar_wait_drain(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -261,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain every MMA this thread issued before TMEM can be released.
       mma_commit(&ctl->mma_drain);
-      mbar_wait(&ctl->mma_drain, 0, p.status, nullptr);
+      mbar_wait_drain(&ctl->mma_drain, 0);
     }
     __syncwarp();
   } else if (warp >= 4) {
@@ -290,6 +288,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(s_addr + 64, r[2]);
       tmem_ld32(s_addr + 96, r[3]);
       tmem_wait_ld();
+      reg_fence32(r[0]);
+      reg_fence32(r[1]);
+      reg_fence32(r[2]);
+      reg_fence32(r[3]);
       const int kb = ctl->list[s][j];
       const int valid = min(kBN, p.Sk - kb * kBN);
       if (valid < kBN) {
@@ -331,6 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t o[32];
           tmem_ld32(o_addr + c * 32, o);
           tmem_wait_ld();
+          reg_fence32(o);
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
           tmem_st32(o_addr + c * 32, o);
@@ -353,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t o[32];
           tmem_ld32(o_addr + c * 32, o);
           tmem_wait_ld();
+          reg_fence32(o);
           if (write) {
             uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll

@@ -1,7 +1,7 @@
 // sa_common.cuh — shared host/device helpers for libsinkattn (sm_100a only).
 //
 // Device side: thin inline-PTX wrappers for mbarriers (every wait is bounded
-// by an iteration limit and reports a timeout through a status word instead
+// by a %globaltimer limit and reports a timeout through a status word instead
 // of spinning forever), TMA tiled loads (no multicast), and the tcgen05
 // family (TMEM alloc/dealloc, MMA issue, commit, TMEM <-> register moves).
 // Host side: the thread-local error message and the cuTensorMapEncodeTiled
@@ -55,10 +55,15 @@ int sm_count_current_device();
 
 namespace sa {
 
-// Iteration limit for every spin on an mbarrier phase. One try_wait already
-// blocks for a hardware-defined slice, so 2^26 polls is far beyond any
-// legitimate wait in these kernels (milliseconds of latency at most).
-constexpr uint32_t kWaitLimit = 1u << 26;
+// Time limit for every spin on an mbarrier phase (nanoseconds of
+// %globaltimer). Legitimate waits in these kernels last microseconds.
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -98,19 +103,42 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete. Returns false
-// (and records SA_DEV_WAIT_TIMEOUT in *status when non-null) if the limit is
-// reached; `abort_flag` (shared) lets other roles of the CTA see the failure.
+// Bounded wait for the phase with the given parity to complete. Gives up
+// (returns false) after kWaitNs, recording SA_DEV_WAIT_TIMEOUT in *status and
+// raising the CTA's shared abort flag; it also gives up early once another
+// role of this CTA raised the abort flag or another CTA wrote *status, so one
+// failure ends the whole grid quickly instead of every CTA timing out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status,
                                           volatile int* abort_flag) {
   const uint32_t a = smem_u32(bar);
-  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+  if (mbar_try_wait(a, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((it & 1023u) == 1023u && abort_flag != nullptr && *abort_flag) return false;
+    if ((it & 255u) == 0u) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (status != nullptr && *reinterpret_cast<volatile int32_t*>(status) != 0) {
+        if (abort_flag != nullptr) *abort_flag = 1;
+        return false;
+      }
+      if (global_timer_ns() - t0 > kWaitNs) {
+        if (abort_flag != nullptr) *abort_flag = 1;
+        if (status != nullptr) atomicExch(status, SA_DEV_WAIT_TIMEOUT);
+        return false;
+      }
+    }
   }
-  if (abort_flag != nullptr) *abort_flag = 1;
-  if (status != nullptr) atomicExch(status, SA_DEV_WAIT_TIMEOUT);
-  return false;
+}
+
+// Time-bounded wait that ignores abort requests: used to drain this CTA's own
+// asynchronous copies / MMAs (which complete on their own) before exit.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitNs) return false;
+  }
 }
 
 // TMA: 4-D tiled load global -> shared, completion counted on `bar` (bytes).
@@ -188,6 +216,19 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Make later uses of registers filled by tcgen05.ld depend on the preceding
+// tcgen05.wait::ld (volatile asm statements keep their relative order).
+__device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+  asm volatile(""
+               : "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]),
+                 "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
