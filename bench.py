@@ -419,6 +419,37 @@ def run_ours(args):
     return 0
 
 
+def run_case(args):
+    """Small single-GPU cases for profiler captures (inputs larger than L2,
+    a few hundred MB on the device): one warm-up launch, then `--steps`
+    launches of the named kernel chain."""
+    from sinkattn_b200 import ops
+    from tests.gen import cfg1_mask, wan_qk
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.case == "attn-small":
+        q, k, v = wan_qk(seed=0, B=1, H=6, dtype=torch.bfloat16, device=dev)
+        mask = cfg1_mask(6, NB, NB, seed=1).unsqueeze(0).to(dev)
+        fn = lambda: ops.bsattn_fwd(q, k, v, mask)  # noqa: E731
+    elif args.case == "calib-small":
+        q, k, _ = wan_qk(seed=0, B=2, H=4, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(ops.pool_scores_workspace_size(2, 4, S, D), dtype=torch.uint8, device=dev)
+
+        def fn():
+            _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
+            ops.coverage_mask(bm, force_sink_col=True)
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    fn()
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, "ok": True}))
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -426,7 +457,11 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    ap.add_argument("--case", choices=["attn-small", "calib-small"], default=None,
+                    help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
