@@ -123,6 +123,26 @@ SA_API int sa_pool_scores(const void* q, const void* k, const int64_t q_strides[
                    void* workspace, size_t ws_bytes, cudaStream_t stream);
 
 /*
+ * sa_pool_scores without a workspace argument. It has no counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when
+ * they call in (a C/FFI host with no device allocator, or a server that
+ * reserved all GPU memory at start-up and may not cudaMalloc while serving).
+ * The scratch is a 16 MiB device array inside the library, held by every GPU
+ * that loads it until the process exits; shapes needing more than 16 MiB
+ * (see sa_pool_scores_workspace_size) return SA_EINVAL. The first call on a
+ * device resolves the array's address with cudaGetSymbolAddress, so make it
+ * before any stream capture. All calls share the array: calls that overlap on
+ * the GPU race and must be serialised by the caller. Arguments and results
+ * are those of sa_pool_scores.
+ */
+SA_API int sa_pool_scores_noalloc(const void* q, const void* k,
+                                  const int64_t q_strides[4],
+                                  const int64_t k_strides[4], int B, int H,
+                                  int S, int D, int block, float scale,
+                                  float* scores, float* batch_mean,
+                                  cudaStream_t stream);
+
+/*
  * Running score statistics of one layer.
  * Replaces: SinkMaskCalibrator._accumulate_score (sparse_attention.py:537-549)
  *   on a device-resident accumulator: sum += x, sumsq += x*x, where x is an

@@ -51,6 +51,10 @@ _SIGNATURES = {
         _i,
         [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, ctypes.c_size_t, _vp],
     ),
+    "sa_pool_scores_noalloc": (
+        _i,
+        [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp],
+    ),
     "sa_score_accumulate": (_i, [_vp, ctypes.c_int64, _vp, _vp, _i, _vp]),
     "sa_score_finalize": (_i, [_vp, _vp, _vp, _f, ctypes.c_int64, _vp, _vp, _vp]),
     "sa_coverage_mask": (

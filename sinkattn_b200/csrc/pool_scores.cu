@@ -265,3 +265,112 @@ extern "C" int sa_pool_scores(const void* q, const void* k, const int64_t q_stri
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
+
+// ---------------------------------------------------------------------------
+// sa_pool_scores_noalloc: the same computation with library-owned scratch.
+//
+// Some callers cannot hand this library a workspace: a plain C or FFI host
+// that binds the .so without any device allocator of its own, or a serving
+// loop that reserved all device memory when it started and may not call
+// cudaMalloc on its hot path (cudaMalloc can synchronise the device and can
+// fail once memory is committed). For them the pooled Q/K and logits live in
+// one file-scope device array of kNoAllocScratchBytes (16 MiB), which every
+// GPU that loads this module keeps until the process exits. That covers the
+// Wan calibration shape (B=2, H=12, S=32768, D=128 needs 12.6 MB); larger
+// requests are rejected with SA_EINVAL.
+//
+// The first call on a device looks up the array's device address with
+// cudaGetSymbolAddress (host code only sees a host-side stand-in for the
+// symbol); make that first call before any stream capture begins. All calls
+// share the one array and it keeps the last call's contents: every byte a
+// call reads is written earlier in the same call, so nothing needs clearing,
+// but calls whose kernels overlap on the GPU (different streams, or several
+// host threads, on one device) race on it and must be serialised by the
+// caller.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace sa {
+namespace pool {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  SA_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    sa::set_error("sa_pool_scores_noalloc: device index %d out of range", dev);
+    return SA_EUNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    SA_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return SA_OK;
+}
+
+}  // namespace pool
+}  // namespace sa
+
+extern "C" int sa_pool_scores_noalloc(const void* q, const void* k, const int64_t q_strides[4],
+                                      const int64_t k_strides[4], int B, int H, int S, int D,
+                                      int block, float scale, float* scores, float* batch_mean,
+                                      cudaStream_t stream) {
+  using namespace sa::pool;
+  SA_CHECK_ARG(q && k && q_strides && k_strides, "sa_pool_scores_noalloc: null pointer argument");
+  SA_CHECK_ARG(scores || batch_mean, "sa_pool_scores_noalloc: scores and batch_mean are both NULL");
+  SA_CHECK_ARG(B >= 1 && H >= 1 && S >= 1 && block >= 1,
+               "sa_pool_scores_noalloc: B, H, S, block must be >= 1");
+  SA_CHECK_ARG(D >= 8 && D <= 256 && D % 8 == 0,
+               "sa_pool_scores_noalloc: D must be a multiple of 8 in [8,256]");
+  SA_CHECK_ARG(q_strides[3] == 1 && k_strides[3] == 1,
+               "sa_pool_scores_noalloc: stride(dim) must be 1");
+  for (int i = 0; i < 3; ++i)
+    SA_CHECK_ARG(q_strides[i] % 8 == 0 && k_strides[i] % 8 == 0,
+                 "sa_pool_scores_noalloc: strides must be multiples of 8 elements");
+  SA_CHECK_ARG(((uintptr_t)q | (uintptr_t)k) % 16 == 0,
+               "sa_pool_scores_noalloc: q/k must be 16-byte aligned");
+  SA_CHECK_ARG((int64_t)B * H <= 65535, "sa_pool_scores_noalloc: B*H too large");
+  const size_t need = sa_pool_scores_workspace_size(B, H, S, D, block);
+  SA_CHECK_ARG(need <= kNoAllocScratchBytes,
+               "sa_pool_scores_noalloc: this shape needs %zu bytes of scratch but the "
+               "built-in scratch holds %zu bytes (16 MiB); use sa_pool_scores with a "
+               "caller-provided workspace",
+               need, kNoAllocScratchBytes);
+  const int nb = (S + block - 1) / block;
+  const size_t smem = (size_t)8 * nb * sizeof(float);
+  SA_CHECK_ARG(smem <= 200 * 1024, "sa_pool_scores_noalloc: nb=%d too large", nb);
+  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
+
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != SA_OK) return rc;
+  float* qp = reinterpret_cast<float*>(scratch);
+  float* kp = qp + (size_t)B * H * nb * D;
+  float* logits = kp + (size_t)B * H * nb * D;
+
+  pool_rows_kernel<<<dim3(nb, B * H, 2), kPoolThreads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
+      q_strides[0], q_strides[1], q_strides[2], k_strides[0], k_strides[1], k_strides[2], H, S,
+      D, block, nb, qp, kp);
+  SA_CUDA_TRY(cudaGetLastError());
+  const int tiles = (nb + kT - 1) / kT;
+  pooled_logits_kernel<<<dim3(tiles, tiles, B * H), 256, 0, stream>>>(qp, kp, nb, D, scale, logits);
+  SA_CUDA_TRY(cudaGetLastError());
+  if (smem > 48 * 1024)
+    SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t rows = (int64_t)H * nb;
+  row_softmax_kernel<<<(unsigned)((rows + 7) / 8), 256, smem, stream>>>(logits, B, H, nb, scores,
+                                                                         batch_mean);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
