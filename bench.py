@@ -70,50 +70,76 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons around a region.
+
+    A reader thread timestamps every sample. __enter__ returns once the first
+    sample has arrived (so the sampler is live when timing starts); __exit__
+    waits for one more sample. summary() uses the samples taken between the
+    two."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_ms: int = 50):
         self.idx = device_index
+        self.period = period_ms
         self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, str]] = []
+        self.t_start = self.t_end = None
+
+    def _reader(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.samples.append((time.monotonic(), ln.strip()))
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.idx)],
+                 "-lms", str(self.period), "-i", str(self.idx)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return self
+        threading.Thread(target=self._reader, daemon=True).start()
+        t0 = time.monotonic()
+        while not self.samples and time.monotonic() - t0 < 10:
+            time.sleep(0.005)
+        self.t_start = time.monotonic()
         return self
 
     def __exit__(self, *exc):
+        self.t_end = time.monotonic()
         if self.proc is not None:
+            n = len(self.samples)
+            t0 = time.monotonic()
+            while len(self.samples) <= n and time.monotonic() - t0 < 2:
+                time.sleep(0.005)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
         return False
 
     def summary(self):
-        if not self.lines:
+        if not self.samples or self.t_start is None:
             return None
-        sm, mx, reasons = [], None, set()
+        window = [ln for (t, ln) in self.samples
+                  if self.t_start - self.period / 1e3 <= t <= self.t_end + self.period / 1e3]
+        sm, mx, power, reasons = [], None, [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in window:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
             try:
                 sm.append(float(parts[1]))
                 mx = float(parts[2])
+                power.append(float(parts[3]))
             except ValueError:
                 continue
             for n, val in zip(names, parts[5:9]):
@@ -122,7 +148,8 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w_max": max(power) if power else None,
+                "window_s": round(self.t_end - self.t_start, 3)}
 
 
 def dist_env():
@@ -428,6 +455,30 @@ def run_case(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.case in ("attn-wan", "calib-wan"):
+        # quick timing of one kernel chain at the full Wan shape (no e2e / CPU legs)
+        q, k, v = wan_qk(seed=0, dtype=torch.bfloat16, device=dev)
+        if args.case == "attn-wan":
+            mask = cfg1_mask(H, NB, NB, seed=1).unsqueeze(0).expand(B, -1, -1, -1).contiguous().to(dev)
+            flops = kept_flops(mask)
+            fn = lambda: ops.bsattn_fwd(q, k, v, mask)  # noqa: E731
+        else:
+            ws = torch.empty(ops.pool_scores_workspace_size(B, H, S, D), dtype=torch.uint8, device=dev)
+            flops = 0.0
+
+            def fn():
+                _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
+                ops.coverage_mask(bm, force_sink_col=True)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        total, per = time_steps(fn, args.steps, torch.cuda.current_stream(dev))
+        ms = total / args.steps
+        res = {"case": args.case, "ms": ms, "min_ms": min(per)}
+        if flops:
+            res["tflops"] = flops / (ms / 1e3) / 1e12
+        print(json.dumps(res))
+        return 0
     if args.case == "attn-small":
         q, k, v = wan_qk(seed=0, B=1, H=6, dtype=torch.bfloat16, device=dev)
         mask = cfg1_mask(6, NB, NB, seed=1).unsqueeze(0).to(dev)
@@ -453,11 +504,12 @@ def run_case(args):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
-    ap.add_argument("--case", choices=["attn-small", "calib-small"], default=None,
+    ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan"],
+                    default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)
     if args.case:

@@ -7,13 +7,13 @@
 // (sinkattention/sparse_attention.py:735-771): 128x128 blocks, no dropout,
 // not causal, scale 1/sqrt(D) by default.
 //
-// Kernel structure (one CTA per SM, 384 threads):
-//   warp 0      TMA producer: Q tiles once, then K/V tiles into a 4-slot ring
-//   warp 1      MMA issuer (one thread): S = Q K^T (SS), O += P V (TS)
-//   warp 2      TMEM allocator + kept-block list of slot 0
-//   warp 3      kept-block list of slot 1
-//   warps 4-7   softmax warpgroup of slot 0 (thread t owns query row t)
-//   warps 8-11  softmax warpgroup of slot 1
+// Kernel structure (one CTA per SM, 640 threads):
+//   warp 0       TMA producer: Q tiles once, then K/V tiles into a 4-slot ring
+//   warp 1       MMA issuer (one thread): S = Q K^T (SS), O += P V (TS)
+//   warp 2       TMEM allocator + kept-block list of slot 0
+//   warp 3       kept-block list of slot 1
+//   warps 4-11   softmax of slot 0: two warpgroups, one per 64-column half
+//   warps 12-19  softmax of slot 1 (thread pair per query row)
 // A CTA carries two query tiles ("slots") that ping-pong: while one slot's
 // softmax runs on the CUDA cores, the tensor core works on the other slot.
 //
@@ -41,7 +41,7 @@ constexpr int kBM = 128;      // query rows per tile
 constexpr int kBN = 128;      // keys per block
 constexpr int kHD = 128;      // head dim
 constexpr int kStages = 4;    // K/V ring slots
-constexpr int kThreads = 384;
+constexpr int kThreads = 640;  // 4 role warps + 4 softmax warpgroups
 constexpr int kTileBytes = kBM * kHD * 2;   // 32 KB bf16 tile
 constexpr int kBoxBytes = kTileBytes / 2;   // one 64-column box
 constexpr int kMaxBlocks = 1024;            // max key blocks per row (S <= 131072)
@@ -66,12 +66,15 @@ struct __align__(8) SmemCtl {
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t o_final[2];
+  uint64_t xbar[2];
   uint64_t mma_drain;
   uint32_t tmem_base;
   int abort_flag;
   int n_blocks[2];
   int q_tile[2];
   int16_t list[2][kMaxBlocks];
+  float xchg[2][2][kBM];  // partial row maxima (slot, half, row)
+  float xsum[2][2][kBM];  // partial row sums at the end
 };
 
 constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
@@ -123,7 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&ctl->q_full[s], 1);
       mbar_init(&ctl->s_full[s], 1);
-      mbar_init(&ctl->p_full[s], kBM);
+      mbar_init(&ctl->p_full[s], 2 * kBM);
+      mbar_init(&ctl->xbar[s], 2 * kBM);
       mbar_init(&ctl->o_final[s], 1);
     }
     for (int i = 0; i < kStages; ++i) {
@@ -177,7 +181,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n1 = ctl->n_blocks[1];
   volatile int* abort_flag = &ctl->abort_flag;
 
+  // Register split (warpgroup-wide, issued inside each role's branch so the
+  // compiler budgets every role separately): the role warps drop to 56
+  // registers and the softmax warpgroups rise to 104.
+  // 128*56 + 512*104 = 60416 <= 640*96, the registers the block launches with.
   if (warp == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       for (int s = 0; s < 2; ++s) {
@@ -208,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(kBM, kBN, 0, 0);
@@ -262,17 +272,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_drain(&ctl->mma_drain, 0);
     }
     __syncwarp();
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
     // ---------------- softmax warpgroups ----------------
-    const int s = (warp - 4) >> 2;
+    // Four warpgroups: slot s = g >> 1 and column half hh = g & 1. Thread
+    // (warp quarter wq, lane) owns query row wq*32+lane and 64 of its 128
+    // key columns; the two halves of a row exchange their partial maxima
+    // (and, at the end, partial sums) through shared memory behind the
+    // slot's `xbar` mbarrier (256 arrivals per phase, bounded waits).
+    const int g = (warp - 4) >> 2;
+    const int s = g >> 1;
+    const int hh = g & 1;
     const int wq = warp & 3;                  // TMEM lane quarter of this warp
     const int row = wq * 32 + lane;           // query row within the tile
     const int n = ctl->n_blocks[s];
     const int qt = ctl->q_tile[s];
     const int grow = qt * kBM + row;          // global query row
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + s * 128;
-    const uint32_t o_addr = tmem + lane_off + 256 + s * 128;
+    const uint32_t s_addr = tmem + lane_off + s * 128 + hh * 64;  // 64 fp32 S columns
+    const uint32_t p_addr = tmem + lane_off + s * 128 + hh * 32;  // 32 packed bf16x2 P columns
+    const uint32_t o_addr = tmem + lane_off + 256 + s * 128 + hh * 64;
+    volatile float* x_own = ctl->xchg[s][hh];
+    volatile float* x_oth = ctl->xchg[s][hh ^ 1];
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
@@ -282,27 +305,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t r[4][32];
+      uint32_t r[2][32];
       tmem_ld32(s_addr + 0, r[0]);
       tmem_ld32(s_addr + 32, r[1]);
-      tmem_ld32(s_addr + 64, r[2]);
-      tmem_ld32(s_addr + 96, r[3]);
       tmem_wait_ld();
       reg_fence32(r[0]);
       reg_fence32(r[1]);
-      reg_fence32(r[2]);
-      reg_fence32(r[3]);
       const int kb = ctl->list[s][j];
-      const int valid = min(kBN, p.Sk - kb * kBN);
-      if (valid < kBN) {
+      const int valid = min(kBN, p.Sk - kb * kBN) - hh * 64;  // valid columns of this half
+      if (valid < 64) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
+        for (int c = 0; c < 64; ++c)
           if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // Partial row maximum over 64 columns: 8 chains of 3-input max.
+      float mxp[8];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(r[c >> 5][c & 31]));
-      mx *= p.scale_log2;
+      for (int t = 0; t < 8; ++t) mxp[t] = __uint_as_float(r[0][t]);
+#pragma unroll
+      for (int c = 8; c + 16 <= 64; c += 16) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          mxp[t] = fmax3(mxp[t], __uint_as_float(r[(c + t) >> 5][(c + t) & 31]),
+                         __uint_as_float(r[(c + 8 + t) >> 5][(c + 8 + t) & 31]));
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mxp[t] = fmaxf(mxp[t], __uint_as_float(r[1][24 + t]));
+      const float mx_half = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                                  fmaxf(mxp[6], mxp[7]));
+      // Exchange with the other half of the row. Both halves have finished
+      // reading S when the phase completes, so P may overwrite it afterwards.
+      x_own[row] = mx_half;
+      mbar_arrive(&ctl->xbar[s]);
+      if (!mbar_wait(&ctl->xbar[s], (uint32_t)j & 1u, p.status, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(mx_half, x_oth[row]) * p.scale_log2;
       float alpha = 1.0f;
       const bool rescale = mx > m_used + kRescaleThreshold;
       if (rescale) {
@@ -310,26 +349,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
         m_used = mx;
       }
-      const float neg_m = -m_used;
-      // P = exp2(S*scale*log2e - m) as bf16 pairs over the first 64 columns of S.
+      // P = exp2(S*scale*log2e - m): packed f32x2 FMA for the argument, MUFU
+      // ex2 per lane, packed f32x2 adds for 4 independent partial sums.
+      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+      const uint64_t negm2 = f2_pack(-m_used, -m_used);
+      uint64_t lp2[4] = {0ull, 0ull, 0ull, 0ull};
+      uint32_t pk[32];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int c = half * 64 + 2 * e;
-          const float p0 = ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, neg_m));
-          const float p1 =
-              ex2_approx(fmaf(__uint_as_float(r[(c + 1) >> 5][(c + 1) & 31]), p.scale_log2, neg_m));
-          l += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
-        }
-        tmem_st32(s_addr + half * 32, pk);
+      for (int e = 0; e < 32; ++e) {
+        const int c = 2 * e;
+        const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(r[c >> 5][c & 31]),
+                                           __uint_as_float(r[(c + 1) >> 5][(c + 1) & 31])),
+                                   scale2, negm2);
+        float x0, x1;
+        f2_unpack(x2, x0, x1);
+        const float p0 = ex2_approx(x0);
+        const float p1 = ex2_approx(x1);
+        lp2[e & 3] = f2_add(lp2[e & 3], f2_pack(p0, p1));
+        pk[e] = pack_bf16x2(p0, p1);
+      }
+      tmem_st32(p_addr, pk);
+      {
+        const uint64_t t2 = f2_add(f2_add(lp2[0], lp2[1]), f2_add(lp2[2], lp2[3]));
+        float a0, a1;
+        f2_unpack(t2, a0, a1);
+        l += a0 + a1;
       }
       // O was complete for blocks < j when s_full(j) fired; PV(j) waits for p_full.
       if (rescale && j > 0) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld32(o_addr + c * 32, o);
           tmem_wait_ld();
@@ -343,16 +392,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&ctl->p_full[s]);
     }
-    // Epilogue: O / l -> bf16 row, natural-log LSE.
+    // Epilogue: combine the two halves' sums, O / l -> bf16, natural-log LSE.
+    float l_row = l;
+    if (ok && n > 0) {
+      ctl->xsum[s][hh][row] = l;
+      mbar_arrive(&ctl->xbar[s]);
+      ok = mbar_wait(&ctl->xbar[s], (uint32_t)n & 1u, p.status, abort_flag);
+      if (ok) l_row = l + ctl->xsum[s][hh ^ 1][row];
+    }
     if (ok && n > 0) ok = mbar_wait(&ctl->o_final[s], 0, p.status, abort_flag);
     tc_fence_after();
     if (qt < p.nq) {
       const bool write = grow < p.Sq;
-      __nv_bfloat16* orow = p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)grow * p.os2;
+      __nv_bfloat16* orow = p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 +
+                            (int64_t)grow * p.os2 + hh * 64;
       if (n > 0 && ok) {
-        const float inv_l = 1.0f / l;
+        const float inv_l = 1.0f / l_row;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld32(o_addr + c * 32, o);
           tmem_wait_ld();
@@ -370,12 +427,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (write && p.lse != nullptr)
-          p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = (m_used + __log2f(l)) * 0.69314718055994531f;
+        if (write && hh == 0 && p.lse != nullptr)
+          p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = (m_used + __log2f(l_row)) * 0.69314718055994531f;
       } else if (write) {
         uint4* dst = reinterpret_cast<uint4*>(orow);
-        for (int v = 0; v < kHD / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
-        if (p.lse != nullptr) p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = -INFINITY;
+        for (int v = 0; v < 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+        if (hh == 0 && p.lse != nullptr) p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = -INFINITY;
       }
     }
   }
