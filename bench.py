@@ -357,6 +357,26 @@ def run_ours(args):
 
     tpool, _ = time_steps(step_pool_only, args.steps, stream)
 
+    # ---- cfg3: the 30-layer calibration pass, layers pipelined on two streams
+    from tests.gen import wan_qk_layers_on_device
+
+    layers = wan_qk_layers_on_device(30, dev)
+    masks30 = torch.empty(30, H, NB, NB, dtype=torch.bool, device=dev)
+
+    def step_pass():
+        ops.calibration_pass(layers, force_sink_col=True, masks_out=masks30)
+
+    for _ in range(2):
+        step_pass()
+    torch.cuda.synchronize()
+    pass_steps = max(3, min(10, args.steps // 10))
+    tpass, _ = time_steps(step_pass, pass_steps, stream)
+    tpass = max_over_ranks(tpass, world, dev)
+    pass_ms = tpass / pass_steps
+    pass_bytes = 30 * calib_bytes
+    density30 = float(masks30.float().mean().item())
+    del layers
+
     # ---- end to end through the reference-facing API (host buffers) ---------
     qp = q_bshd.pin_memory()
     kp = k_bshd.pin_memory()
@@ -422,6 +442,15 @@ def run_ours(args):
                               "gbs": calib_bytes / (tcal / args.steps / 1e3) / 1e9,
                               "frac_of_hbm": calib_bytes / (tcal / args.steps / 1e3) / 1e9
                               / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))},
+        "calibration_pass_30_layers": {
+            "ms_per_pass": pass_ms, "ms_per_layer": pass_ms / 30,
+            "bytes_per_pass": pass_bytes, "gbs": pass_bytes / (pass_ms / 1e3) / 1e9,
+            "frac_of_hbm": pass_bytes / (pass_ms / 1e3) / 1e9
+            / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
+            "mask_density": density30,
+            "note": "cfg3: 30 layers x Q,K [2,12,32768,128] bf16 (GPU-generated, seed=layer); "
+                    "pool -> pooled softmax -> batch mean -> coverage mask (sink column "
+                    "forced); pooling of layer l+1 overlaps the scores/mask of layer l"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
                 "api": "sinkattn_b200.reference_api._block_sparse_attn"},
@@ -455,6 +484,19 @@ def run_case(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.case == "calib-pass":
+        from tests.gen import wan_qk_layers_on_device
+
+        layers = wan_qk_layers_on_device(30, dev)
+        fn = lambda: ops.calibration_pass(layers, force_sink_col=True)  # noqa: E731
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        total, per = time_steps(fn, args.steps, torch.cuda.current_stream(dev))
+        ms = total / args.steps
+        gbs = 30 * (2 * B * H * S * D * 2 + H * NB * NB) / (ms / 1e3) / 1e9
+        print(json.dumps({"case": args.case, "ms_per_pass": ms, "ms_per_layer": ms / 30, "gbs": gbs}))
+        return 0
     if args.case in ("attn-wan", "calib-wan"):
         # quick timing of one kernel chain at the full Wan shape (no e2e / CPU legs)
         q, k, v = wan_qk(seed=0, dtype=torch.bfloat16, device=dev)
@@ -508,7 +550,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
-    ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan"],
+    ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
+                                       "calib-pass"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)

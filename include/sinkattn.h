@@ -123,6 +123,23 @@ SA_API int sa_pool_scores(const void* q, const void* k, const int64_t q_strides[
                    void* workspace, size_t ws_bytes, cudaStream_t stream);
 
 /*
+ * The two halves of sa_pool_scores, for callers that pipeline layers (the
+ * HBM-bound pooling of one layer overlaps the small compute-bound score step
+ * of the previous one on another stream).
+ * sa_pool_means: block means of Q and K (sparse_attention.py:88-94 with the
+ *   replicate padding of lines 79-85), qp/kp fp32 [B,H,nb,D] contiguous.
+ * sa_pooled_softmax: softmax(qp kp^T * scale) per batch (sparse_attention.py:
+ *   140-142) into scores [B,H,nb,nb] and/or its batch mean [H,nb,nb]
+ *   (line 581); logits_ws is fp32 scratch of B*H*nb*nb elements.
+ */
+SA_API int sa_pool_means(const void* q, const void* k, const int64_t q_strides[4],
+                         const int64_t k_strides[4], int B, int H, int S, int D,
+                         int block, float* qp, float* kp, cudaStream_t stream);
+SA_API int sa_pooled_softmax(const float* qp, const float* kp, int B, int H, int nb,
+                             int D, float scale, float* scores, float* batch_mean,
+                             float* logits_ws, cudaStream_t stream);
+
+/*
  * sa_pool_scores without a workspace argument. It has no counterpart in the
  * reference: it exists for callers that cannot allocate device memory when
  * they call in (a C/FFI host with no device allocator, or a server that

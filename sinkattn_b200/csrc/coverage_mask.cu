@@ -85,15 +85,14 @@ __device__ __forceinline__ float ulp_of(float v) {
 
 template <int NPAD>
 __global__ void coverage_mask_kernel(const Params p) {
-  constexpr int E = NPAD / 32;  // sorted elements per lane (contiguous chunk)
+  constexpr int E = NPAD / 32;  // sorted positions per lane (contiguous chunk)
   extern __shared__ uint8_t smem_raw[];
   const int warps = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw) + (size_t)warp * NPAD;
-  uint8_t* keep = reinterpret_cast<uint8_t*>(reinterpret_cast<uint64_t*>(smem_raw) +
-                                             (size_t)warps * NPAD) +
-                  (size_t)warp * NPAD;
+  // per warp: sorted value keys, then the candidate value of every column
+  uint32_t* skey = reinterpret_cast<uint32_t*>(smem_raw) + (size_t)warp * 2 * NPAD;
+  float* cval = reinterpret_cast<float*>(skey + NPAD);
 
   const int64_t grow = (int64_t)blockIdx.x * warps + warp;  // (head, row) flattened
   if (grow >= (int64_t)p.H * p.nq) return;
@@ -114,27 +113,25 @@ __global__ void coverage_mask_kernel(const Params p) {
   const int c_lo = video ? T : 0;  // first column taking part in the coverage step
 
   // ---- load, required set, row sums ---------------------------------------
+  // Participating columns (j >= c_lo) get a sort key ~ordered(candidate);
+  // required columns enter as -inf (joint mode). Others get key 0xFFFFFFFF
+  // (sorted last) and candidate value NaN.
   double tot = 0.0, sel = 0.0;
-  int n_cand_local = 0;  // non-required columns taking part (candidate_counts, line 348)
+  int n_cand_local = 0;  // non-required participating columns (candidate_counts, line 348)
   for (int j = lane; j < NPAD; j += 32) {
-    uint64_t key = ~0ull;
-    uint8_t kp = 0;
-    if (j < nk) {
+    uint32_t key = 0xFFFFFFFFu;
+    float cv = __int_as_float(0x7fc00000);
+    if (j < nk && j >= c_lo) {
       const float v = s[j];
       const bool req = (j < T) || (p.force_sink && j == 0);
-      if (j >= c_lo) {
-        tot += (double)v;
-        if (!video && req) sel += (double)v;
-      }
-      kp = req ? 1 : 0;
-      if (j >= c_lo) {
-        if (video || !req) ++n_cand_local;
-        const float cand = (!video && req) ? -INFINITY : v;
-        key = ((uint64_t)(~float_to_ordered(cand)) << 32) | (uint32_t)j;
-      }
+      tot += (double)v;
+      if (!video && req) sel += (double)v;
+      if (video || !req) ++n_cand_local;
+      cv = (!video && req) ? -INFINITY : v;
+      key = ~float_to_ordered(cv);
     }
-    keys[j] = key;
-    keep[j] = kp;
+    skey[j] = key;
+    cval[j] = cv;
   }
   tot = warp_sum_f64(tot);
   sel = warp_sum_f64(sel);
@@ -144,42 +141,88 @@ __global__ void coverage_mask_kernel(const Params p) {
   const float cov = fminf(fmaxf(p.coverage, 0.f), 1.f);
   float target = __fmul_rn(cov, total);
   if (!video) target = fmaxf(__fsub_rn(target, selected), 0.f);
+  const int n_cand = __reduce_add_sync(0xffffffffu, (unsigned)n_cand_local);
   __syncwarp();
 
-  // ---- bitonic sort, ascending by key (= value descending, index ascending)
-#pragma unroll 1
-  for (int k = 2; k <= NPAD; k <<= 1) {
-#pragma unroll 1
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = lane; i < NPAD; i += 32) {
-        const int partner = i ^ j;
-        if (partner > i) {
-          const uint64_t a = keys[i], b = keys[partner];
-          const bool up = (i & k) == 0;
-          if ((a > b) == up) {
-            keys[i] = b;
-            keys[partner] = a;
+  // ---- sort the 32-bit value keys ascending (= values descending) ----------
+  // Equal values may land in any order: the cumulative sums do not depend on
+  // it, and the kept set below is chosen by value and index, not position.
+  if constexpr (NPAD <= 256) {
+    constexpr int R = NPAD / 32;
+    uint32_t reg[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) reg[i] = skey[lane + 32 * i];
+#pragma unroll
+    for (int k = 2; k <= NPAD; k <<= 1) {
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        if (j >= 32) {
+          const int js = j >> 5;
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            const int i2 = i ^ js;
+            if (i2 > i) {
+              const bool up = (((lane + 32 * i) & k) == 0);
+              const uint32_t a = reg[i], c = reg[i2];
+              const uint32_t lo = min(a, c), hi = max(a, c);
+              reg[i] = up ? lo : hi;
+              reg[i2] = up ? hi : lo;
+            }
+          }
+        } else {
+          const bool lower = (lane & j) == 0;
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            const uint32_t a = reg[i];
+            const uint32_t c = __shfl_xor_sync(0xffffffffu, a, j);
+            const bool up = (((lane + 32 * i) & k) == 0);
+            reg[i] = (lower == up) ? min(a, c) : max(a, c);
           }
         }
       }
-      __syncwarp();
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < R; ++i) skey[lane + 32 * i] = reg[i];
+    __syncwarp();
+  } else {
+#pragma unroll 1
+    for (int k = 2; k <= NPAD; k <<= 1) {
+#pragma unroll 1
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = lane; i < NPAD; i += 32) {
+          const int partner = i ^ j;
+          if (partner > i) {
+            const uint32_t a = skey[i], b = skey[partner];
+            const bool up = (i & k) == 0;
+            if ((a > b) == up) {
+              skey[i] = b;
+              skey[partner] = a;
+            }
+          }
+        }
+        __syncwarp();
+      }
     }
   }
 
-  // ---- candidates, exactness test, cumulative sums ------------------------
+  // sorted value at position r (0 for padding / non-finite, as line 345 does)
+  auto sorted_val0 = [&](int r) -> float {
+    const uint32_t key = skey[r];
+    if (key == 0xFFFFFFFFu) return 0.f;
+    const float v = ordered_to_float(~key);
+    return isfinite(v) ? v : 0.f;
+  };
+
+  // ---- exactness test, cumulative sums ---------------------------------------
   // Lane owns sorted positions [lane*E, lane*E + E).
-  const int n_cand = __reduce_add_sync(0xffffffffu, (unsigned)n_cand_local);
   int min_q = INT_MAX;
   bool nonneg = true;
   double local = 0.0;
   for (int e = 0; e < E; ++e) {
-    const uint64_t key = keys[lane * E + e];
-    const uint32_t idx = (uint32_t)key;
-    if (key == ~0ull || idx >= (uint32_t)nk) continue;
-    const float v = ordered_to_float(~(uint32_t)(key >> 32));
-    if (!isfinite(v)) continue;  // non-finite sorted scores count as 0 (line 345)
+    const float v = sorted_val0(lane * E + e);
     if (v < 0.f) nonneg = false;
-    if (v > 0.f && isfinite(v)) min_q = min(min_q, ulp_exp(v));
+    if (v > 0.f) min_q = min(min_q, ulp_exp(v));
     local += (double)v;
   }
   const bool all_nonneg = __all_sync(0xffffffffu, nonneg);
@@ -204,14 +247,7 @@ __global__ void coverage_mask_kernel(const Params p) {
     float prev_f = lane == 0 ? 0.f : (float)run;
     for (int e = 0; e < E; ++e) {
       const int r = lane * E + e;
-      const uint64_t key = keys[r];
-      const uint32_t idx = (uint32_t)key;
-      float v = 0.f;
-      if (key != ~0ull && idx < (uint32_t)nk) {
-        v = ordered_to_float(~(uint32_t)(key >> 32));
-        if (!isfinite(v)) v = 0.f;
-      }
-      run += (double)v;
+      run += (double)sorted_val0(r);
       const float cf = (float)run;
       if (cf >= target && first == INT_MAX) {
         first = r;
@@ -232,14 +268,7 @@ __global__ void coverage_mask_kernel(const Params p) {
       double run = 0.0;
       float prev_f = 0.f;
       for (int r = 0; r < NPAD; ++r) {
-        const uint64_t key = keys[r];
-        const uint32_t idx = (uint32_t)key;
-        float v = 0.f;
-        if (key != ~0ull && idx < (uint32_t)nk) {
-          v = ordered_to_float(~(uint32_t)(key >> 32));
-          if (!isfinite(v)) v = 0.f;
-        }
-        run += (double)v;
+        run += (double)sorted_val0(r);
         const float cf = (float)run;
         if (cf >= target) {
           first = r;
@@ -265,43 +294,78 @@ __global__ void coverage_mask_kernel(const Params p) {
   kcut = max(0, min(kcut, n_sortable));
 
   // ---- assemble the row ------------------------------------------------
-  for (int r = lane; r < kcut; r += 32) {
-    const uint32_t idx = (uint32_t)keys[r];
-    if (idx < (uint32_t)nk) keep[idx] = 1;
+  // The first kcut positions of the stable (value desc, index asc) order are
+  // every candidate above the cut value plus, among candidates equal to it,
+  // the lowest indices.
+  uint32_t key_cut = 0xFFFFFFFFu;
+  int m_eq = 0;
+  if (kcut > 0) {
+    key_cut = skey[kcut - 1];
+    int gt = 0;
+    for (int j = lane; j < nk; j += 32) {
+      const float cv = cval[j];
+      if (cv == cv && ~float_to_ordered(cv) < key_cut) ++gt;
+    }
+    gt = __reduce_add_sync(0xffffffffu, (unsigned)gt);
+    m_eq = kcut - gt;
   }
-  __syncwarp();
-  if (!video && p.keep_diag && row < nk && lane == 0) keep[row] = 1;
-  __syncwarp();
   int any = 0;
-  for (int j = lane; j < nk; j += 32) any |= keep[j];
+  int eq_seen = 0;
+  for (int base = 0; base < nk; base += 32) {
+    const int j = base + lane;
+    bool keep = false;
+    bool eq = false;
+    if (j < nk) {
+      const bool req = (j < T) || (!video && p.force_sink && j == 0);
+      const float cv = cval[j];
+      const bool part = (cv == cv) && cv != -INFINITY;
+      if (part && kcut > 0) {
+        const uint32_t key = ~float_to_ordered(cv);
+        eq = key == key_cut;
+        keep = key < key_cut;
+      }
+      keep = keep || req;
+      if (!video && p.keep_diag && j == row) keep = true;
+    }
+    const uint32_t bal = __ballot_sync(0xffffffffu, eq);
+    if (eq && eq_seen + __popc(bal & ((1u << lane) - 1u)) < m_eq) keep = true;
+    eq_seen += __popc(bal);
+    if (j < nk) out[j] = keep ? 1 : 0;
+    any |= keep ? 1 : 0;
+  }
   any = __any_sync(0xffffffffu, any);
   uint32_t flags = 0;
   if (!any) {
     flags |= SA_ROW_EMPTY_FALLBACK;
-    if (lane == 0) {
-      int top = -1;
-      if (video) {
-        // full-row argmax (first occurrence), line 329
-        float best = -INFINITY;
-        for (int j = 0; j < nk; ++j) {
-          const float v = s[j];
-          if (top < 0 || v > best) { best = v; top = j; }
-        }
-      } else {
-        top = (int)(uint32_t)keys[0];
-        if (top >= nk) top = 0;
+    // video mode: argmax over the full row (line 329); joint: the first entry
+    // of the candidate sort (line 373), lowest index among equal maxima.
+    float best = -INFINITY;
+    int top = INT_MAX;
+    for (int j = lane; j < nk; j += 32) {
+      const float v = video ? s[j] : cval[j];
+      if (v == v && (top == INT_MAX || v > best)) {
+        best = v;
+        top = j;
       }
-      keep[top] = 1;
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int ot = __shfl_xor_sync(0xffffffffu, top, o);
+      if (ot != INT_MAX && (top == INT_MAX || ob > best || (ob == best && ot < top))) {
+        best = ob;
+        top = ot;
+      }
+    }
+    if (top == INT_MAX) top = 0;
+    if (lane == 0) out[top] = 1;
   }
-  __syncwarp();
-  for (int j = lane; j < nk; j += 32) out[j] = keep[j];
 
   if (p.flags != nullptr && lane == 0) {
     auto sorted_val = [&](int r) -> float {
-      const uint64_t key = keys[r];
-      if (key == ~0ull || (uint32_t)key >= (uint32_t)nk) return NAN;
-      return ordered_to_float(~(uint32_t)(key >> 32));
+      const uint32_t key = skey[r];
+      if (key == 0xFFFFFFFFu) return NAN;
+      return ordered_to_float(~key);
     };
     // A tie straddling the cut (or the top-1 fallback) makes torch's order matter.
     const int cut = (flags & SA_ROW_EMPTY_FALLBACK) ? 1 : kcut;
@@ -321,7 +385,11 @@ __global__ void coverage_mask_kernel(const Params p) {
 template <int NPAD>
 int launch(const Params& p, cudaStream_t stream) {
   const int warps = NPAD <= 1024 ? 8 : (NPAD == 2048 ? 4 : 2);
-  const size_t smem = (size_t)warps * NPAD * (sizeof(uint64_t) + 1);
+  const size_t smem = (size_t)warps * NPAD * 2 * sizeof(uint32_t);
+  // max shared carveout: lets this kernel share SMs with the pooling kernel
+  SA_CUDA_TRY(cudaFuncSetAttribute(coverage_mask_kernel<NPAD>,
+                                   cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   cudaSharedmemCarveoutMaxShared));
   if (smem > 48 * 1024) {
     SA_CUDA_TRY(cudaFuncSetAttribute(coverage_mask_kernel<NPAD>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -110,6 +110,84 @@ __global__ void __launch_bounds__(kPoolThreads)
   }
 }
 
+// TMA-staged variant of pool_rows for D == 128, block == 128 (the
+// calibration shape). Persistent: one CTA per SM, 3 warps; each warp owns two
+// 32 KB shared-memory stages and streams its own sequence of (tensor, b, h,
+// block) items through them: the TMA load of item k+1 is in flight while the
+// warp sums item k. Lane l sums columns 4l..4l+3 over the block's 128 rows
+// (rows past S arrive zero-filled and the final token is added for them,
+// the replicate padding of sparse_attention.py:79-85).
+constexpr int kTmaWarps = 3;
+constexpr int kTmaStageBytes = 128 * 128 * 2;
+constexpr size_t kTmaSmem = 1024 + (size_t)kTmaWarps * 2 * kTmaStageBytes + 64;
+
+__global__ void __launch_bounds__(kTmaWarps * 32, 1)
+    pool_rows_tma_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k, int BH, int H, int S, int nb,
+                         float* __restrict__ qp, float* __restrict__ kp) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* stage0 = smem + (size_t)warp * 2 * kTmaStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kTmaWarps * 2 * kTmaStageBytes) +
+                   warp * 2;
+  if (lane == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  const int64_t n_items = 2LL * BH * nb;
+  const int64_t stride = (int64_t)gridDim.x * kTmaWarps;
+  int64_t item = (int64_t)blockIdx.x * kTmaWarps + warp;
+  auto issue = [&](int64_t it, int st) {
+    const int t = (int)(it / ((int64_t)BH * nb));
+    const int rem = (int)(it - (int64_t)t * BH * nb);
+    const int bh = rem / nb, j = rem - (rem / nb) * nb;
+    mbar_arrive_expect_tx(&full[st], kTmaStageBytes);
+    tma_load_4d(t ? &tm_k : &tm_q, &full[st], stage0 + (size_t)st * kTmaStageBytes, 0, j * 128,
+                bh % H, bh / H);
+  };
+  if (lane == 0 && item < n_items) issue(item, 0);
+  for (int k = 0; item < n_items; ++k, item += stride) {
+    const int st = k & 1;
+    const int64_t next = item + stride;
+    if (lane == 0 && next < n_items) {
+      fence_proxy_async_smem();
+      issue(next, st ^ 1);
+    }
+    if (!mbar_wait_drain(&full[st], (uint32_t)(k >> 1) & 1u)) break;
+    const uint8_t* tile = stage0 + (size_t)st * kTmaStageBytes + lane * 8;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < 128; r += 2) {
+      const uint2 u = *reinterpret_cast<const uint2*>(tile + r * 256);
+      const uint2 w = *reinterpret_cast<const uint2*>(tile + (r + 1) * 256);
+      a0 += __uint_as_float(u.x << 16); a1 += __uint_as_float(u.x & 0xffff0000u);
+      a2 += __uint_as_float(u.y << 16); a3 += __uint_as_float(u.y & 0xffff0000u);
+      b0 += __uint_as_float(w.x << 16); b1 += __uint_as_float(w.x & 0xffff0000u);
+      b2 += __uint_as_float(w.y << 16); b3 += __uint_as_float(w.y & 0xffff0000u);
+    }
+    a0 += b0; a1 += b1; a2 += b2; a3 += b3;
+    const int t = (int)(item / ((int64_t)BH * nb));
+    const int rem = (int)(item - (int64_t)t * BH * nb);
+    const int j = rem % nb;
+    const int valid = min(128, S - j * 128);
+    if (valid < 128) {
+      const uint2 u = *reinterpret_cast<const uint2*>(tile + (valid - 1) * 256);
+      const float wgt = (float)(128 - valid);
+      a0 += wgt * __uint_as_float(u.x << 16); a1 += wgt * __uint_as_float(u.x & 0xffff0000u);
+      a2 += wgt * __uint_as_float(u.y << 16); a3 += wgt * __uint_as_float(u.y & 0xffff0000u);
+    }
+    const float inv = 1.0f / 128.0f;
+    float* outp = (t ? kp : qp) + (int64_t)rem * 128 + lane * 4;
+    *reinterpret_cast<float4*>(outp) = make_float4(a0 * inv, a1 * inv, a2 * inv, a3 * inv);
+    __syncwarp();
+  }
+}
+
 // logits[bh, i, j] = scale * sum_d qp[bh, i, d] * kp[bh, j, d]
 // grid: (ceil(nb/64), ceil(nb/64), B*H); block 256 = 16x16 threads, 4x4 each.
 constexpr int kT = 64, kKC = 32;
@@ -211,6 +289,91 @@ __global__ void row_softmax_kernel(const float* __restrict__ logits, int B, int 
 }  // namespace pool
 }  // namespace sa
 
+
+namespace sa {
+namespace pool {
+
+// All calibration kernels prefer the maximum shared-memory carveout, so the
+// small score kernels of one layer can share SMs with the pooling kernel of
+// the next layer (launched on another stream) instead of waiting for a
+// carveout change.
+int prefer_max_shared_carveout() {
+  int dev = 0;
+  SA_CUDA_TRY(cudaGetDevice(&dev));
+  static bool done[64] = {};
+  if (dev >= 0 && dev < 64 && done[dev]) return SA_OK;
+  SA_CUDA_TRY(cudaFuncSetAttribute(pool_rows_tma_kernel,
+                                   cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   cudaSharedmemCarveoutMaxShared));
+  SA_CUDA_TRY(cudaFuncSetAttribute(pooled_logits_kernel,
+                                   cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   cudaSharedmemCarveoutMaxShared));
+  SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
+                                   cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   cudaSharedmemCarveoutMaxShared));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return SA_OK;
+}
+
+// Pools Q and K into qp / kp, through TMA staging when the shape allows.
+int launch_pool_rows(const void* q, const void* k, const int64_t q_strides[4],
+                     const int64_t k_strides[4], int B, int H, int S, int D, int block, int nb,
+                     float* qp, float* kp, cudaStream_t stream) {
+  const bool tma_ok = D == 128 && block == 128 && ((uintptr_t)q % 16 == 0) &&
+                      ((uintptr_t)k % 16 == 0);
+  if (int rc0 = prefer_max_shared_carveout(); rc0 != SA_OK) return rc0;
+  if (tma_ok) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (enc == nullptr) return SA_ECUDA;
+    CUtensorMap maps[2];
+    const void* bases[2] = {q, k};
+    const int64_t* strides[2] = {q_strides, k_strides};
+    for (int t = 0; t < 2; ++t) {
+      cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+      cuuint64_t gst[3] = {(cuuint64_t)strides[t][2] * 2, (cuuint64_t)strides[t][1] * 2,
+                           (cuuint64_t)strides[t][0] * 2};
+      cuuint32_t box[4] = {128, 128, 1, 1};
+      cuuint32_t estr[4] = {1, 1, 1, 1};
+      CUresult r = enc(&maps[t], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(bases[t]),
+                       dims, gst, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (pool) failed (CUresult %d)", (int)r);
+        return SA_ECUDA;
+      }
+    }
+    int dev = 0;
+    SA_CUDA_TRY(cudaGetDevice(&dev));
+    static bool attr_set[64] = {};
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      SA_CUDA_TRY(cudaFuncSetAttribute(pool_rows_tma_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kTmaSmem));
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const int64_t items = 2LL * B * H * nb;
+    const int sms = sm_count_current_device();
+    const int64_t warps_needed = (items + 0) / 1;
+    int grid = (int)((warps_needed + kTmaWarps - 1) / kTmaWarps);
+    if (grid > sms) grid = sms;
+    if (grid < 1) grid = 1;
+    pool_rows_tma_kernel<<<grid, kTmaWarps * 32, kTmaSmem, stream>>>(maps[0], maps[1], B * H, H, S,
+                                                                     nb, qp, kp);
+    SA_CUDA_TRY(cudaGetLastError());
+    return SA_OK;
+  }
+  pool_rows_kernel<<<dim3(nb, B * H, 2), kPoolThreads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
+      q_strides[0], q_strides[1], q_strides[2], k_strides[0], k_strides[1], k_strides[2], H, S, D,
+      block, nb, qp, kp);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+}  // namespace pool
+}  // namespace sa
+
 extern "C" size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int block) {
   if (B < 1 || H < 1 || S < 1 || D < 1 || block < 1) return 0;
   const size_t nb = (size_t)((S + block - 1) / block);
@@ -244,11 +407,8 @@ extern "C" int sa_pool_scores(const void* q, const void* k, const int64_t q_stri
   float* kp = qp + (size_t)B * H * nb * D;
   float* logits = kp + (size_t)B * H * nb * D;
 
-  pool_rows_kernel<<<dim3(nb, B * H, 2), kPoolThreads, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
-      q_strides[0], q_strides[1], q_strides[2], k_strides[0], k_strides[1], k_strides[2], H, S,
-      D, block, nb, qp, kp);
-  SA_CUDA_TRY(cudaGetLastError());
+  int rc = launch_pool_rows(q, k, q_strides, k_strides, B, H, S, D, block, nb, qp, kp, stream);
+  if (rc != SA_OK) return rc;
   const int tiles = (nb + kT - 1) / kT;
   pooled_logits_kernel<<<dim3(tiles, tiles, B * H), 256, 0, stream>>>(qp, kp, nb, D, scale, logits);
   SA_CUDA_TRY(cudaGetLastError());
@@ -262,6 +422,52 @@ extern "C" int sa_pool_scores(const void* q, const void* k, const int64_t q_stri
   const int64_t rows = (int64_t)H * nb;
   row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
       logits, B, H, nb, scores, batch_mean);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_pool_means(const void* q, const void* k, const int64_t q_strides[4],
+                             const int64_t k_strides[4], int B, int H, int S, int D, int block,
+                             float* qp, float* kp, cudaStream_t stream) {
+  using namespace sa::pool;
+  SA_CHECK_ARG(q && k && q_strides && k_strides && qp && kp, "sa_pool_means: null pointer argument");
+  SA_CHECK_ARG(B >= 1 && H >= 1 && S >= 1 && block >= 1, "sa_pool_means: B, H, S, block must be >= 1");
+  SA_CHECK_ARG(D >= 8 && D <= 256 && D % 8 == 0, "sa_pool_means: D must be a multiple of 8 in [8,256]");
+  SA_CHECK_ARG(q_strides[3] == 1 && k_strides[3] == 1, "sa_pool_means: stride(dim) must be 1");
+  for (int i = 0; i < 3; ++i)
+    SA_CHECK_ARG(q_strides[i] % 8 == 0 && k_strides[i] % 8 == 0,
+                 "sa_pool_means: strides must be multiples of 8 elements (16-byte loads)");
+  SA_CHECK_ARG(((uintptr_t)q | (uintptr_t)k) % 16 == 0, "sa_pool_means: q/k must be 16-byte aligned");
+  SA_CHECK_ARG(((uintptr_t)qp | (uintptr_t)kp) % 16 == 0, "sa_pool_means: qp/kp must be 16-byte aligned");
+  SA_CHECK_ARG((int64_t)B * H <= 65535, "sa_pool_means: B*H too large");
+  const int nb = (S + block - 1) / block;
+  return launch_pool_rows(q, k, q_strides, k_strides, B, H, S, D, block, nb, qp, kp, stream);
+}
+
+extern "C" int sa_pooled_softmax(const float* qp, const float* kp, int B, int H, int nb, int D,
+                                 float scale, float* scores, float* batch_mean, float* logits_ws,
+                                 cudaStream_t stream) {
+  using namespace sa::pool;
+  SA_CHECK_ARG(qp && kp && logits_ws, "sa_pooled_softmax: null pointer argument");
+  SA_CHECK_ARG(scores || batch_mean, "sa_pooled_softmax: scores and batch_mean are both NULL");
+  SA_CHECK_ARG(B >= 1 && H >= 1 && nb >= 1, "sa_pooled_softmax: B, H, nb must be >= 1");
+  SA_CHECK_ARG(D >= 8 && D <= 256 && D % 8 == 0, "sa_pooled_softmax: D must be a multiple of 8 in [8,256]");
+  SA_CHECK_ARG((int64_t)B * H <= 65535, "sa_pooled_softmax: B*H too large");
+  SA_CHECK_ARG(((uintptr_t)qp | (uintptr_t)kp) % 16 == 0, "sa_pooled_softmax: qp/kp must be 16-byte aligned");
+  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
+  if (int rc0 = prefer_max_shared_carveout(); rc0 != SA_OK) return rc0;
+  const int tiles = (nb + kT - 1) / kT;
+  pooled_logits_kernel<<<dim3(tiles, tiles, B * H), 256, 0, stream>>>(qp, kp, nb, D, scale, logits_ws);
+  SA_CUDA_TRY(cudaGetLastError());
+  const int warps = 8;
+  const size_t smem = (size_t)warps * nb * sizeof(float);
+  SA_CHECK_ARG(smem <= 200 * 1024, "sa_pooled_softmax: nb=%d too large", nb);
+  if (smem > 48 * 1024)
+    SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t rows = (int64_t)H * nb;
+  row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
+      logits_ws, B, H, nb, scores, batch_mean);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }

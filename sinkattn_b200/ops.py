@@ -196,6 +196,127 @@ def pool_scores(
     return scores, bmean
 
 
+def pool_means(q: torch.Tensor, k: torch.Tensor, block: int = BLOCK,
+               qp: Optional[torch.Tensor] = None, kp: Optional[torch.Tensor] = None):
+    """Block means of bf16 q, k [B,H,S,D] -> fp32 [B,H,nb,D] each (first half
+    of pool_scores)."""
+    dev = _require_cuda(q, k)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or q.shape != k.shape:
+        raise RuntimeError("pool_means expects bf16 q, k of equal shape [B,H,S,D]")
+    B, H, S, D = q.shape
+    nb = math.ceil(S / block)
+    q, k = _as_kernel_layout(q), _as_kernel_layout(k)
+    if qp is None:
+        qp = torch.empty((B, H, nb, D), dtype=torch.float32, device=dev)
+    if kp is None:
+        kp = torch.empty((B, H, nb, D), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_pool_means(q.data_ptr(), k.data_ptr(), _lib.strides4(q), _lib.strides4(k),
+                               B, H, S, D, block, qp.data_ptr(), kp.data_ptr(), _stream(dev))
+    _lib.check(rc, "sa_pool_means")
+    return qp, kp
+
+
+def pooled_softmax(qp: torch.Tensor, kp: torch.Tensor, scale: Optional[float] = None,
+                   want_scores: bool = True, want_batch_mean: bool = False,
+                   logits_ws: Optional[torch.Tensor] = None,
+                   batch_mean_out: Optional[torch.Tensor] = None):
+    """softmax(qp kp^T * scale) per batch from fp32 block means [B,H,nb,D]
+    (second half of pool_scores). Returns (scores or None, batch_mean or None)."""
+    dev = _require_cuda(qp, kp)
+    B, H, nb, D = qp.shape
+    if logits_ws is None or logits_ws.numel() < B * H * nb * nb:
+        logits_ws = torch.empty(B * H * nb * nb, dtype=torch.float32, device=dev)
+    scores = torch.empty((B, H, nb, nb), dtype=torch.float32, device=dev) if want_scores else None
+    bmean = batch_mean_out
+    if want_batch_mean and bmean is None:
+        bmean = torch.empty((H, nb, nb), dtype=torch.float32, device=dev)
+    sc = -1.0 if scale is None else float(scale)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_pooled_softmax(qp.data_ptr(), kp.data_ptr(), B, H, nb, D, sc, _ptr(scores),
+                                   _ptr(bmean) if want_batch_mean else None, logits_ws.data_ptr(),
+                                   _stream(dev))
+    _lib.check(rc, "sa_pooled_softmax")
+    return scores, (bmean if want_batch_mean else None)
+
+
+_PASS_STREAMS: dict[int, tuple] = {}
+
+
+def calibration_pass(
+    layers,
+    block: int = BLOCK,
+    coverage: float = 0.85,
+    keep_diagonal: bool = True,
+    text_blocks: int = 0,
+    mode: str = "joint",
+    force_sink_col: bool = False,
+    want_batch_mean: bool = False,
+    masks_out: Optional[torch.Tensor] = None,
+):
+    """Pooling + pooled softmax + batch mean + coverage mask for a sequence of
+    layers, each given as a (q, k) pair of bf16 [B,H,S,D] CUDA tensors.
+
+    Two side streams pipeline the layers: the HBM-bound pooling of layer l+1
+    runs while the compute-bound score softmax and mask of layer l run, with
+    double-buffered pooled means. The result is ordered on the caller's
+    current stream. Returns (masks bool [L,H,nb,nb], batch means fp32
+    [L,H,nb,nb] or None)."""
+    layers = list(layers)
+    if not layers:
+        raise ValueError("calibration_pass needs at least one layer")
+    q0, _ = layers[0]
+    dev = _require_cuda(q0)
+    B, H, S, D = q0.shape
+    nb = math.ceil(S / block)
+    L = len(layers)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _PASS_STREAMS:
+        _PASS_STREAMS[idx] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    sp, sc = _PASS_STREAMS[idx]
+    cur = torch.cuda.current_stream(dev)
+    masks = masks_out if masks_out is not None else torch.empty(
+        (L, H, nb, nb), dtype=torch.bool, device=dev)
+    bmeans = torch.empty((L, H, nb, nb), dtype=torch.float32, device=dev) if want_batch_mean \
+        else torch.empty((2, H, nb, nb), dtype=torch.float32, device=dev)
+    qp = [torch.empty((B, H, nb, D), dtype=torch.float32, device=dev) for _ in range(2)]
+    kp = [torch.empty((B, H, nb, D), dtype=torch.float32, device=dev) for _ in range(2)]
+    logits = torch.empty(B * H * nb * nb, dtype=torch.float32, device=dev)
+    pooled = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    sp.wait_stream(cur)
+    sc.wait_stream(cur)
+    for l, (q, k) in enumerate(layers):
+        if q.shape != (B, H, S, D) or k.shape != (B, H, S, D):
+            raise ValueError("all layers must share one [B,H,S,D] shape")
+        buf = l % 2
+        with torch.cuda.stream(sp):
+            if l >= 2:
+                sp.wait_event(consumed[buf])
+            pool_means(q, k, block, qp=qp[buf], kp=kp[buf])
+            pooled[buf].record(sp)
+        with torch.cuda.stream(sc):
+            sc.wait_event(pooled[buf])
+            bm = bmeans[l] if want_batch_mean else bmeans[buf]
+            pooled_softmax(qp[buf], kp[buf], want_scores=False, want_batch_mean=True,
+                           logits_ws=logits, batch_mean_out=bm)
+            consumed[buf].record(sc)
+            coverage_mask(bm, coverage=coverage, keep_diagonal=keep_diagonal,
+                          text_blocks=text_blocks, mode=mode, force_sink_col=force_sink_col,
+                          out=masks[l])
+    cur.wait_stream(sp)
+    cur.wait_stream(sc)
+    for t in (*qp, *kp, logits, bmeans, masks):
+        t.record_stream(sp)
+        t.record_stream(sc)
+    for q, k in layers:
+        q.record_stream(sp)
+        k.record_stream(sp)
+    return masks, (bmeans if want_batch_mean else None)
+
+
 def coverage_mask(
     scores: torch.Tensor,
     coverage: float = 0.85,
@@ -206,10 +327,12 @@ def coverage_mask(
     row_total: Optional[torch.Tensor] = None,
     row_selected: Optional[torch.Tensor] = None,
     want_flags: bool = False,
+    out: Optional[torch.Tensor] = None,
 ):
     """Per-row minimal-coverage block mask from fp32 scores [H,nq,nk] (CUDA).
 
-    Returns (mask bool [H,nq,nk], flags int32 [H,nq] or None)."""
+    Returns (mask bool [H,nq,nk], flags int32 [H,nq] or None). `out`, when
+    given, is a contiguous bool [H,nq,nk] tensor the mask is written into."""
     dev = _require_cuda(scores, row_total, row_selected)
     if scores.dim() != 3:
         raise ValueError(f"Expected [heads, blocks_q, blocks_k] scores, got {tuple(scores.shape)}")
@@ -226,7 +349,12 @@ def coverage_mask(
             raise ValueError(f"{name} must be fp32 [H, nq]")
     row_total = None if row_total is None else row_total.contiguous()
     row_selected = None if row_selected is None else row_selected.contiguous()
-    mask = torch.empty((H, nq, nk), dtype=torch.bool, device=dev)
+    if out is not None:
+        if out.shape != (H, nq, nk) or out.dtype != torch.bool or not out.is_contiguous():
+            raise ValueError("out must be a contiguous bool [H, nq, nk] tensor")
+        mask = out
+    else:
+        mask = torch.empty((H, nq, nk), dtype=torch.bool, device=dev)
     flags = torch.empty((H, nq), dtype=torch.int32, device=dev) if want_flags else None
     lib = _lib.load()
     with torch.cuda.device(dev):

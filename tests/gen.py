@@ -100,6 +100,24 @@ def wan_qk(seed: int = 0, B: int = 2, H: int = 12, S: int = WAN_S_PADDED, D: int
             v.to(device=device, dtype=dtype))
 
 
+def wan_qk_layers_on_device(n_layers: int, device, B: int = 2, H: int = 12,
+                            S: int = WAN_S_PADDED, D: int = 128, amp: float = 0.5):
+    """cfg3 timing inputs: Q, K per layer generated directly on the GPU with a
+    CUDA generator seeded by the layer index (fast; a different random stream
+    from the CPU generator used for the parity fixtures)."""
+    pe = torch.zeros(S, D)
+    n = min(S, WAN_TOKENS)
+    pe[:n] = pe3d()[:n]
+    pe = (amp * pe).to(device)
+    out = []
+    for layer in range(n_layers):
+        g = torch.Generator(device=device).manual_seed(layer)
+        q = torch.randn(B, H, S, D, generator=g, device=device).add_(pe).bfloat16()
+        k = torch.randn(B, H, S, D, generator=g, device=device).add_(pe).bfloat16()
+        out.append((q, k))
+    return out
+
+
 def zimg_qkv(seed: int = 0, H: int = 30, D: int = 128, amp: float = 0.5, device="cpu",
              dtype=torch.bfloat16):
     g = torch.Generator(device="cpu").manual_seed(int(seed))

@@ -195,3 +195,24 @@ def test_mix_outputs(oracle):
     torch.cuda.synchronize()
     ref = oracle.mix_outputs(os_.float().numpy(), ls.numpy(), od.float().numpy(), ld.numpy(), 30)
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+
+
+def test_calibration_pass_matches_serial_chain():
+    """The two-stream pipelined pass over layers gives exactly the per-layer
+    serial results (same kernels, only the scheduling differs)."""
+    from sinkattn_b200 import ops
+
+    g = torch.Generator().manual_seed(8)
+    layers = []
+    for _ in range(5):
+        q = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
+        k = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
+        layers.append((q, k))
+    masks, bms = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True)
+    torch.cuda.synchronize()
+    for l, (q, k) in enumerate(layers):
+        _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True)
+        m, _ = ops.coverage_mask(bm, force_sink_col=True)
+        torch.cuda.synchronize()
+        assert torch.equal(bm, bms[l])
+        assert torch.equal(m, masks[l])
