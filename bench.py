@@ -152,6 +152,16 @@ class ClockSampler:
                 "window_s": round(self.t_end - self.t_start, 3)}
 
 
+_TRACE = os.environ.get("SINKATTN_BENCH_TRACE") == "1"
+
+
+def trace(msg: str) -> None:
+    """Timestamped progress line on stderr (SINKATTN_BENCH_TRACE=1)."""
+    if _TRACE:
+        print(f"[bench {time.strftime('%H:%M:%S')} rank {os.environ.get('RANK', '0')}] {msg}",
+              file=sys.stderr, flush=True)
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -159,13 +169,14 @@ def dist_env():
     return world, rank, local
 
 
-def init_dist(world: int, backend: str):
+def init_dist(world: int, backend: str, device=None):
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
-        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=300))
+        kw = {"device_id": device} if (backend == "nccl" and device is not None) else {}
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120), **kw)
 
 
 def max_over_ranks(x: float, world: int, device) -> float:
@@ -280,7 +291,9 @@ def run_ours(args):
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    init_dist(world, "nccl")
+    init_dist(world, "nccl", dev)
+    barrier(world)
+    trace("process group up")
     from sinkattn_b200 import _lib, ops
     from sinkattn_b200.reference_api import _block_sparse_attn
     from tests.gen import cfg1_mask, wan_qk
@@ -290,7 +303,9 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
 
     # inputs: Wan layout (BSHD memory viewed as BHSD), seed = rank
+    trace("generating inputs")
     qh, kh, vh = wan_qk(seed=rank, dtype=torch.bfloat16)  # [B,H,S,D] on CPU
+    trace("inputs generated")
     q_bshd = qh.permute(0, 2, 1, 3).contiguous()
     k_bshd = kh.permute(0, 2, 1, 3).contiguous()
     v_bshd = vh.permute(0, 2, 1, 3).contiguous()
@@ -316,6 +331,7 @@ def run_ours(args):
 
     step_calib()
     torch.cuda.synchronize()
+    trace("first calibration step done")
     mask83 = calib["mask"].unsqueeze(0).expand(B, -1, -1, -1).contiguous()
     density83 = float(mask83.float().mean().item())
     flops83 = kept_flops(mask83)
@@ -323,12 +339,16 @@ def run_ours(args):
     def step83():
         ops.bsattn_fwd(q, k, v, mask83, out=out, lse=lse)
 
-    for _ in range(max(3, args.warmup)):
-        step20()
-        step83()
-        step_calib()
+    for i in range(max(3, args.warmup)):
+        for name, fn in (("attn rho21", step20), ("attn coverage-mask", step83),
+                         ("calibration", step_calib)):
+            fn()
+            if _TRACE:
+                torch.cuda.synchronize()
+                trace(f"warm-up {i} {name} done")
     torch.cuda.synchronize()
 
+    trace("warm-up done")
     # ---- headline: rho ~ 0.21 -------------------------------------------
     barrier(world)
     torch.cuda.synchronize()
@@ -342,6 +362,7 @@ def run_ours(args):
     avg_launch_ms = statistics.mean(per_ms)
     achieved = flops20 / (avg_launch_ms / 1e3) / 1e12
 
+    trace("headline timed")
     # ---- coverage-rule mask (rho ~ 0.83) ----------------------------------
     barrier(world)
     t83, per83 = time_steps(step83, args.steps, stream)
@@ -357,6 +378,7 @@ def run_ours(args):
 
     tpool, _ = time_steps(step_pool_only, args.steps, stream)
 
+    trace("calibration layer timed")
     # ---- cfg3: the 30-layer calibration pass, layers pipelined on two streams
     from tests.gen import wan_qk_layers_on_device
 
@@ -377,6 +399,7 @@ def run_ours(args):
     density30 = float(masks30.float().mean().item())
     del layers
 
+    trace("calibration pass timed")
     # ---- end to end through the reference-facing API (host buffers) ---------
     qp = q_bshd.pin_memory()
     kp = k_bshd.pin_memory()
@@ -407,6 +430,7 @@ def run_ours(args):
     h2d = 3 * B * S * H * D * 2
     d2h = B * S * H * D * 2 + B * H * S * 2
 
+    trace("e2e timed")
     # ---- CPU baseline (rank 0, N=1 only) ------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -543,6 +567,26 @@ def run_case(args):
     return 0
 
 
+# Multi-GPU runs of the attention kernel are held back: on a 2-GPU box the
+# second rank's first full-size attention launch did not complete (twice);
+# the cause is not yet identified, so N > 1 reports unavailable instead of
+# launching the kernel again.
+MULTI_GPU_HOLD = ("multi-GPU attention runs held back: the second rank's first full-size "
+                  "attention launch did not complete on a 2-GPU box (cause not yet found)")
+
+
+def run_multi_gpu_held(args):
+    world, rank, _ = dist_env()
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "value": None, "unit": UNIT, "n_gpus": args.gpus,
+                          "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic", "unavailable": MULTI_GPU_HOLD,
+                          "config": {"workload": "wan_sink_attention_layer",
+                                     "parallelism": f"(b,h)-units x{world}"}}), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -559,6 +603,8 @@ def main(argv=None):
         return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
+    if max(args.gpus, dist_env()[0]) > 1:
+        return run_multi_gpu_held(args)
     return run_ours(args)
 
 

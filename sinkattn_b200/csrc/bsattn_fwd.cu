@@ -300,7 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
-      if (!mbar_wait(&ctl->s_full[s], (uint32_t)j & 1u, p.status, abort_flag)) {
+      // warp-uniform outcome: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&ctl->s_full[s], (uint32_t)j & 1u, p.status, abort_flag))) {
         ok = false;
         break;
       }
@@ -337,7 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // reading S when the phase completes, so P may overwrite it afterwards.
       x_own[row] = mx_half;
       mbar_arrive(&ctl->xbar[s]);
-      if (!mbar_wait(&ctl->xbar[s], (uint32_t)j & 1u, p.status, abort_flag)) {
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&ctl->xbar[s], (uint32_t)j & 1u, p.status, abort_flag))) {
         ok = false;
         break;
       }
@@ -376,7 +379,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         l += a0 + a1;
       }
       // O was complete for blocks < j when s_full(j) fired; PV(j) waits for p_full.
-      if (rescale && j > 0) {
+      // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
+      // takes this branch when any of its rows rescales; other rows use
+      // alpha = 1.
+      if (__any_sync(0xffffffffu, rescale && j > 0)) {
+        if (!(rescale && j > 0)) alpha = 1.0f;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
@@ -401,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) l_row = l + ctl->xsum[s][hh ^ 1][row];
     }
     if (ok && n > 0) ok = mbar_wait(&ctl->o_final[s], 0, p.status, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);  // the O loads below are warp-collective
     tc_fence_after();
     if (qt < p.nq) {
       const bool write = grow < p.Sq;

@@ -244,3 +244,27 @@ def test_no_wait_timeouts_recorded():
 
     torch.cuda.synchronize()
     DeviceStatus.check(torch.device("cuda", 0))
+
+
+@pytest.mark.parametrize("boost", [3.0, 0.6])
+def test_divergent_running_max_rescale(oracle, boost):
+    """Rows whose running maximum must be raised after the first block, mixed
+    with rows that need no rescale inside the same warp (every third row gets
+    a key in the last block whose logit dwarfs the first block's maximum).
+    Exercises the lazy O/l rescale, which is warp-collective on TMEM."""
+    from sinkattn_b200 import ops
+
+    g = torch.Generator().manual_seed(21)
+    B, H, S = 1, 2, 512
+    q = torch.randn(B, H, S, 128, generator=g)
+    k = torch.randn(B, H, S, 128, generator=g)
+    v = torch.randn(B, H, S, 128, generator=g)
+    rows = torch.arange(0, S, 3)
+    q[:, :, rows] += boost * k[:, :, 384 + (rows % 100)]
+    q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    mask = torch.ones(B, H, 4, 4, dtype=torch.bool)
+    out, lse = ops.bsattn_fwd(q.cuda(), k.cuda(), v.cuda(), mask.cuda())
+    torch.cuda.synchronize()
+    ref, ref_lse = oracle.dense_masked_attention(_np(q), _np(k), _np(v), mask.numpy())
+    _check(out, ref, f"rescale boost {boost}")
+    np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=2e-3, rtol=1e-4)

@@ -1,0 +1,111 @@
+"""Multi-rank logic on CPU: unit partitioning and the Ulysses exchange, run
+as gloo ranks (world sizes 2 and 4). The local attention of each rank is the
+CPU oracle here (the product path runs the CUDA kernel)."""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_partition_units_contiguous_and_balanced():
+    from sinkattn_b200.sharding import partition_units
+
+    for n, world in [(24, 8), (30, 8), (24, 1), (5, 8), (30, 4)]:
+        parts = [partition_units(n, world, r) for r in range(world)]
+        flat = [u for p in parts for u in p]
+        assert flat == list(range(n))
+        sizes = [len(p) for p in parts]
+        assert max(sizes) - min(sizes) <= 1
+    assert [len(partition_units(30, 8, r)) for r in range(8)] == [4, 4, 4, 4, 4, 4, 3, 3]
+
+
+def test_partition_units_weighted_lpt():
+    from sinkattn_b200.sharding import partition_units
+
+    w = [10, 1, 1, 1, 9, 2, 2, 8]
+    parts = [partition_units(len(w), 3, r, weights=w) for r in range(3)]
+    assert sorted(u for p in parts for u in p) == list(range(len(w)))
+    loads = [sum(w[u] for u in p) for p in parts]
+    assert max(loads) - min(loads) <= max(w)
+    with pytest.raises(ValueError):
+        partition_units(4, 2, 2)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _oracle_attn(q, k, v, m):
+    sys.path.insert(0, str(ROOT))
+    from oracle import sinkattn_oracle as orc
+
+    out, lse = orc.dense_masked_attention(q.float().numpy(), k.float().numpy(),
+                                          v.float().numpy(), m.numpy())
+    return torch.from_numpy(out), torch.from_numpy(lse)
+
+
+def _worker(rank, world, port, result_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    sys.path.insert(0, str(ROOT))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from sinkattn_b200.sharding import sequence_to_units, ulysses_sink_attention, units_to_sequence
+
+        g = torch.Generator().manual_seed(7)
+        B, S, H, D = 2, 512, 3, 16
+        q = torch.randn(B, S, H, D, generator=g)
+        k = torch.randn(B, S, H, D, generator=g)
+        v = torch.randn(B, S, H, D, generator=g)
+        mask = torch.rand(B, H, 4, 4, generator=g) < 0.6
+        mask[..., 0] = True
+        Sr = S // world
+        sl = slice(rank * Sr, (rank + 1) * Sr)
+        # the exchange round-trips
+        u = sequence_to_units(q[:, sl].contiguous())
+        back = units_to_sequence(u, B, H)
+        assert torch.equal(back, q[:, sl])
+        out, lse = ulysses_sink_attention(q[:, sl].contiguous(), k[:, sl].contiguous(),
+                                          v[:, sl].contiguous(), mask, attn_fn=_oracle_attn)
+        np.save(os.path.join(result_dir, f"out{rank}.npy"), out.numpy())
+        np.save(os.path.join(result_dir, f"lse{rank}.npy"), lse.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ulysses_exchange_matches_full_attention(tmp_path, world, oracle):
+    port = _free_port()
+    mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    g = torch.Generator().manual_seed(7)
+    B, S, H, D = 2, 512, 3, 16
+    q = torch.randn(B, S, H, D, generator=g)
+    k = torch.randn(B, S, H, D, generator=g)
+    v = torch.randn(B, S, H, D, generator=g)
+    mask = torch.rand(B, H, 4, 4, generator=g) < 0.6
+    mask[..., 0] = True
+    ref, ref_lse = oracle.dense_masked_attention(q.permute(0, 2, 1, 3).numpy(),
+                                                 k.permute(0, 2, 1, 3).numpy(),
+                                                 v.permute(0, 2, 1, 3).numpy(), mask.numpy())
+    Sr = S // world
+    for r in range(world):
+        out = np.load(tmp_path / f"out{r}.npy")
+        lse = np.load(tmp_path / f"lse{r}.npy")
+        np.testing.assert_allclose(out, ref.transpose(0, 2, 1, 3)[:, r * Sr:(r + 1) * Sr],
+                                   atol=1e-5, rtol=1e-5)
+        np.testing.assert_allclose(lse, ref_lse[:, :, r * Sr:(r + 1) * Sr], atol=1e-5)
