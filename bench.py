@@ -508,6 +508,45 @@ def run_case(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.case == "wan-runtime":
+        # Wan runtime inner attention: sink mask | band 1, pooled K/V gap 30, adaptive mix
+        from sinkattn_b200 import reference_api as ra
+
+        q, k, v = wan_qk(seed=0, dtype=torch.bfloat16, device=dev)
+        m = cfg1_mask(H, NB, NB, seed=1)
+        ii = torch.arange(NB)
+        m = m | ((ii[:, None] - ii[None, :]).abs() <= 1)
+        mask = m.unsqueeze(0).expand(B, -1, -1, -1).contiguous().to(dev)
+
+        class Cfg:
+            mixing_mode = "adaptive"
+            sample_gap = 30
+
+        def fused():
+            kp = ops.mean_pool_seq(k, 30)
+            vp = ops.mean_pool_seq(v, 30)
+            return ops.sink_dynamic_attn(q, k, v, mask, kp, vp, 30)
+
+        def unfused():
+            o_s, l_s = ra._block_sparse_attn(q, k, v, mask, return_lse=True)
+            kp = ops.mean_pool_seq(k, 30)
+            vp = ops.mean_pool_seq(v, 30)
+            dm = torch.ones(B, H, NB, math.ceil(kp.shape[2] / 128), dtype=torch.bool, device=dev)
+            o_d, l_d = ra._block_sparse_attn(q, kp, vp, dm, return_lse=True)
+            return ra._mix_attention_outputs(o_s, l_s, o_d, l_d, Cfg, 30)
+
+        res = {"case": args.case}
+        skp = math.ceil(S / 30)
+        flops = kept_flops(mask) + 4.0 * D * S * skp * B * H
+        for name, fn in (("fused", fused), ("unfused", unfused)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            total, _ = time_steps(fn, args.steps, torch.cuda.current_stream(dev))
+            res[name + "_ms"] = total / args.steps
+            res[name + "_tflops"] = flops / (total / args.steps / 1e3) / 1e12
+        print(json.dumps(res))
+        return 0
     if args.case == "calib-pass":
         from tests.gen import wan_qk_layers_on_device
 
@@ -595,7 +634,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
-                                       "calib-pass"],
+                                       "calib-pass", "wan-runtime"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)

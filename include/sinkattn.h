@@ -97,6 +97,29 @@ SA_API int sa_bsattn_fwd(const void* q, const void* k, const void* v,
                   int32_t* status, cudaStream_t stream);
 
 /*
+ * Sink attention fused with the pooled-K/V dynamic branch.
+ * Replaces, in one pass, the two _block_sparse_attn calls of
+ * WanSinkSparseInnerAttention.forward (wanx/runtime/sink_sparse_wan.py:210-256)
+ * and their adaptive mix _mix_attention_outputs (sinkattention/sparse_attention.py:
+ * 898-919): with w_s = lse_s and w_d = lse_d + ln(gap), the mix equals one
+ * softmax over the kept sink keys together with every pooled key, the pooled
+ * keys' logits raised by ln(gap). That softmax is computed exactly (fp32
+ * accumulation), without the mix's bf16-rounded LSEs.
+ * Arguments are those of sa_bsattn_fwd plus the pooled keys/values k_pool,
+ * v_pool [B,H,Sk_pool,D] (e.g. from sa_mean_pool_seq with pool = gap) and
+ * log_gap = ln(gap). lse (nullable) is the natural-log LSE of the combined
+ * softmax. Requires ceil(Sk/128) + ceil(Sk_pool/128) <= 1024.
+ */
+SA_API int sa_sink_dynamic_attn_fwd(
+    const void* q, const void* k, const void* v, const int64_t q_strides[4],
+    const int64_t k_strides[4], const int64_t v_strides[4], int B, int H, int Sq, int Sk,
+    int D, const uint8_t* block_mask, const int64_t m_strides[4], int Hm,
+    const int32_t* head_mask_type, const void* k_pool, const void* v_pool,
+    const int64_t kp_strides[4], const int64_t vp_strides[4], int Sk_pool, float log_gap,
+    float softmax_scale, void* out, const int64_t o_strides[4], float* lse, int32_t* status,
+    cudaStream_t stream);
+
+/*
  * Scratch bytes sa_pool_scores needs: pooled Q and K in fp32 plus the fp32
  * pooled logits, 4 * B * H * nb * (2 * D + nb) bytes with nb = ceil(S/block).
  */

@@ -355,3 +355,35 @@ def kept_block_flops(block_mask: np.ndarray, B: int, H: int, Sq: int, Sk: int, D
                 bm = np.ones_like(mb[0])
             total += int((area * bm[:nq, :nk]).sum())
     return 4.0 * D * total
+
+
+def sink_dynamic_attention(q, k, v, block_mask, k_pool, v_pool, sample_gap: int,
+                           scale: float | None = None, block: int = 128):
+    """The Wan runtime's sink + pooled-K/V adaptive mix as one softmax
+    (wanx/runtime/sink_sparse_wan.py:210-265 with _mix_attention_outputs,
+    sparse_attention.py:898-919): per row, keys = kept sink keys plus every
+    pooled key, pooled logits raised by ln(sample_gap). Exact algebra of
+    alpha*o_s + (1-alpha)*o_d with alpha = e^{lse_s}/(e^{lse_s}+gap*e^{lse_d}).
+    Returns (out [B,H,Sq,D], lse [B,H,Sq])."""
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    lg = math.log(float(max(1, int(sample_gap))))
+    out = np.zeros((B, H, Sq, D), dtype=np.float32)
+    lse = np.zeros((B, H, Sq), dtype=np.float32)
+    for b in range(B):
+        mb = block_mask[b if block_mask.shape[0] > 1 else 0]
+        for h in range(H):
+            tok = np.repeat(np.repeat(mb[h], block, axis=0), block, axis=1)[:Sq, :Sk]
+            s1 = (q[b, h].astype(np.float64) @ k[b, h].astype(np.float64).T) * scale
+            s1 = np.where(tok, s1, -np.inf)
+            s2 = (q[b, h].astype(np.float64) @ k_pool[b, h].astype(np.float64).T) * scale + lg
+            s = np.concatenate([s1, s2], axis=1)
+            m = s.max(axis=1, keepdims=True)
+            p = np.exp(s - m)
+            l = p.sum(axis=1, keepdims=True)
+            vv = np.concatenate([v[b, h], v_pool[b, h]], axis=0).astype(np.float64)
+            out[b, h] = (p @ vv / l).astype(np.float32)
+            lse[b, h] = (np.log(l[:, 0]) + m[:, 0]).astype(np.float32)
+    return out, lse

@@ -46,6 +46,11 @@ _SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _vp, _f, _vp, _vp,
          _vp, _vp, _vp],
     ),
+    "sa_sink_dynamic_attn_fwd": (
+        _i,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp,
+         _i, _f, _f, _vp, _vp, _vp, _vp, _vp],
+    ),
     "sa_pool_scores_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i, _i]),
     "sa_pool_scores": (
         _i,

@@ -49,6 +49,8 @@ constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
 struct Params {
   int B, H, Sq, Sk, nq, nk;
+  int Sk2, nk2;      // pooled (dynamic-branch) keys appended to every row; 0 if none
+  float bias_log2;   // logit bias of the pooled keys, log2 units (ln(gap) * log2(e))
   const uint8_t* mask;
   int64_t ms0, ms1, ms2, ms3;
   const int32_t* head_mask_type;
@@ -72,7 +74,7 @@ struct __align__(8) SmemCtl {
   int abort_flag;
   int n_blocks[2];
   int q_tile[2];
-  int16_t list[2][kMaxBlocks];
+  uint16_t list[2][kMaxBlocks];  // key blocks; bit 15 marks a pooled-key block
   float xchg[2][2][kBM];  // partial row maxima (slot, half, row)
   float xsum[2][2][kBM];  // partial row sums at the end
 };
@@ -108,7 +110,9 @@ __device__ __forceinline__ void for_each_item(const int n0, const int n1, F&& f)
 __global__ void __launch_bounds__(kThreads, 1)
     bsattn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                      const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_k2,
+                      const __grid_constant__ CUtensorMap tm_v2, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -142,6 +146,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
+    if (p.nk2 > 0) {
+      prefetch_tensormap(&tm_k2);
+      prefetch_tensormap(&tm_v2);
+    }
   }
   if (warp == 2) {
     tmem_alloc(&ctl->tmem_base, 512);
@@ -163,9 +171,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c = c0 + lane;
         const bool keep = c < p.nk && (dense || row[(int64_t)c * p.ms3] != 0);
         const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-        if (keep) ctl->list[s][count + __popc(bal & ((1u << lane) - 1u))] = (int16_t)c;
+        if (keep) ctl->list[s][count + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)c;
         count += __popc(bal);
       }
+      // the dynamic branch: every pooled-key block, after the kept sink blocks
+      for (int t = lane; t < p.nk2; t += 32) ctl->list[s][count + t] = (uint16_t)(0x8000u | t);
+      count += p.nk2;
     }
     if (lane == 0) {
       ctl->n_blocks[s] = count;
@@ -203,8 +214,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t phase = (uint32_t)(it / kStages) & 1u;
         if (!mbar_wait(&ctl->kv_empty[stage], phase ^ 1u, p.status, abort_flag)) return false;
         uint8_t* dst = ring + stage * kTileBytes;
-        const int kb = ctl->list[item.slot][item.j];
-        const CUtensorMap* map = item.is_v ? &tm_v : &tm_k;
+        const uint32_t ent = ctl->list[item.slot][item.j];
+        const int kb = (int)(ent & 0x7fffu);
+        const bool pooled = (ent & 0x8000u) != 0;
+        const CUtensorMap* map = item.is_v ? (pooled ? &tm_v2 : &tm_v) : (pooled ? &tm_k2 : &tm_k);
         mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
         tma_load_4d(map, &ctl->kv_full[stage], dst, 0, kb * kBN, h, b);
         tma_load_4d(map, &ctl->kv_full[stage], dst + kBoxBytes, 64, kb * kBN, h, b);
@@ -313,8 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       reg_fence32(r[0]);
       reg_fence32(r[1]);
-      const int kb = ctl->list[s][j];
-      const int valid = min(kBN, p.Sk - kb * kBN) - hh * 64;  // valid columns of this half
+      const uint32_t ent = ctl->list[s][j];
+      const int kb = (int)(ent & 0x7fffu);
+      const bool pooled = (ent & 0x8000u) != 0;
+      const int valid = min(kBN, (pooled ? p.Sk2 : p.Sk) - kb * kBN) - hh * 64;  // valid columns here
+      const float bias = pooled ? p.bias_log2 : 0.f;
       if (valid < 64) {
 #pragma unroll
         for (int c = 0; c < 64; ++c)
@@ -344,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      const float mx = fmaxf(mx_half, x_oth[row]) * p.scale_log2;
+      const float mx = fmaf(fmaxf(mx_half, x_oth[row]), p.scale_log2, bias);
       float alpha = 1.0f;
       const bool rescale = mx > m_used + kRescaleThreshold;
       if (rescale) {
@@ -355,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = exp2(S*scale*log2e - m): packed f32x2 FMA for the argument, MUFU
       // ex2 per lane, packed f32x2 adds for 4 independent partial sums.
       const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
-      const uint64_t negm2 = f2_pack(-m_used, -m_used);
+      const uint64_t negm2 = f2_pack(bias - m_used, bias - m_used);
       uint64_t lp2[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t pk[32];
 #pragma unroll
@@ -487,42 +503,62 @@ bool strides_ok(const int64_t st[4]) {
 
 }  // namespace
 
-extern "C" int sa_bsattn_fwd(const void* q, const void* k, const void* v,
-                             const int64_t q_strides[4], const int64_t k_strides[4],
-                             const int64_t v_strides[4], int B, int H, int Sq, int Sk, int D,
-                             const uint8_t* block_mask, const int64_t m_strides[4], int Hm,
-                             const int32_t* head_mask_type, float softmax_scale, void* out,
-                             const int64_t o_strides[4], float* lse, int32_t* status,
-                             cudaStream_t stream) {
+namespace {
+
+// Shared by sa_bsattn_fwd (k2 == nullptr) and sa_sink_dynamic_attn_fwd.
+int launch_attention(const char* fn, const void* q, const void* k, const void* v,
+                     const int64_t q_strides[4], const int64_t k_strides[4],
+                     const int64_t v_strides[4], int B, int H, int Sq, int Sk, int D,
+                     const uint8_t* block_mask, const int64_t m_strides[4], int Hm,
+                     const int32_t* head_mask_type, const void* k2, const void* v2,
+                     const int64_t* k2_strides, const int64_t* v2_strides, int Sk2,
+                     float log_bias, float softmax_scale, void* out, const int64_t o_strides[4],
+                     float* lse, int32_t* status, cudaStream_t stream) {
   using namespace sa::attn;
-  SA_CHECK_ARG(q && k && v && out && block_mask, "sa_bsattn_fwd: null tensor pointer");
+  SA_CHECK_ARG(q && k && v && out && block_mask, "%s: null tensor pointer", fn);
   SA_CHECK_ARG(q_strides && k_strides && v_strides && o_strides && m_strides,
-               "sa_bsattn_fwd: null stride array");
-  SA_CHECK_ARG(D == kHD, "sa_bsattn_fwd: head dim must be 128, got %d", D);
+               "%s: null stride array", fn);
+  SA_CHECK_ARG(D == kHD, "%s: head dim must be 128, got %d", fn, D);
   SA_CHECK_ARG(B >= 1 && H >= 1 && Sq >= 1 && Sk >= 1,
-               "sa_bsattn_fwd: B, H, Sq, Sk must be >= 1 (got %d, %d, %d, %d)", B, H, Sq, Sk);
+               "%s: B, H, Sq, Sk must be >= 1 (got %d, %d, %d, %d)", fn, B, H, Sq, Sk);
   const int nq = (Sq + kBM - 1) / kBM;
   const int nk = (Sk + kBN - 1) / kBN;
-  SA_CHECK_ARG(nk <= kMaxBlocks, "sa_bsattn_fwd: Sk=%d exceeds %d key blocks", Sk, kMaxBlocks);
-  SA_CHECK_ARG(B <= 65535 && H <= 65535, "sa_bsattn_fwd: B/H too large");
+  const bool dual = k2 != nullptr;
+  const int nk2 = dual ? (Sk2 + kBN - 1) / kBN : 0;
+  SA_CHECK_ARG(!dual || (v2 && k2_strides && v2_strides && Sk2 >= 1),
+               "%s: pooled keys need k2, v2, their strides and Sk2 >= 1", fn);
+  SA_CHECK_ARG(nk + nk2 <= kMaxBlocks && nk2 < 0x8000,
+               "%s: %d + %d key blocks exceed %d", fn, nk, nk2, kMaxBlocks);
+  SA_CHECK_ARG(B <= 65535 && H <= 65535, "%s: B/H too large", fn);
   SA_CHECK_ARG(strides_ok(q_strides) && strides_ok(k_strides) && strides_ok(v_strides) &&
-                   strides_ok(o_strides),
-               "sa_bsattn_fwd: q/k/v/out need stride(dim)=1 and other strides multiple of 8 "
-               "elements (16 bytes)");
-  SA_CHECK_ARG(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) % 16 == 0,
-               "sa_bsattn_fwd: q/k/v/out base pointers must be 16-byte aligned");
+                   strides_ok(o_strides) && (!dual || (strides_ok(k2_strides) && strides_ok(v2_strides))),
+               "%s: q/k/v/out need stride(dim)=1 and other strides multiple of 8 "
+               "elements (16 bytes)", fn);
+  SA_CHECK_ARG(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out |
+                (uintptr_t)(dual ? k2 : q) | (uintptr_t)(dual ? v2 : q)) % 16 == 0,
+               "%s: tensor base pointers must be 16-byte aligned", fn);
   SA_CHECK_ARG(head_mask_type != nullptr || Hm == H,
-               "sa_bsattn_fwd: mask has %d heads but H=%d and no head_mask_type", Hm, H);
-  SA_CHECK_ARG(Hm >= 1, "sa_bsattn_fwd: mask heads must be >= 1");
+               "%s: mask has %d heads but H=%d and no head_mask_type", fn, Hm, H);
+  SA_CHECK_ARG(Hm >= 1, "%s: mask heads must be >= 1", fn);
 
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tk2, tv2;
   int rc;
   if ((rc = make_map_bshd(&tq, q, q_strides, B, H, Sq, D)) != SA_OK) return rc;
   if ((rc = make_map_bshd(&tk, k, k_strides, B, H, Sk, D)) != SA_OK) return rc;
   if ((rc = make_map_bshd(&tv, v, v_strides, B, H, Sk, D)) != SA_OK) return rc;
+  if (dual) {
+    if ((rc = make_map_bshd(&tk2, k2, k2_strides, B, H, Sk2, D)) != SA_OK) return rc;
+    if ((rc = make_map_bshd(&tv2, v2, v2_strides, B, H, Sk2, D)) != SA_OK) return rc;
+  } else {
+    tk2 = tk;  // unused
+    tv2 = tv;
+  }
 
   Params p;
   p.B = B; p.H = H; p.Sq = Sq; p.Sk = Sk; p.nq = nq; p.nk = nk;
+  p.Sk2 = dual ? Sk2 : 0;
+  p.nk2 = nk2;
+  p.bias_log2 = dual ? log_bias * 1.4426950408889634f : 0.f;
   p.mask = block_mask;
   p.ms0 = m_strides[0]; p.ms1 = m_strides[1]; p.ms2 = m_strides[2]; p.ms3 = m_strides[3];
   p.head_mask_type = head_mask_type;
@@ -543,7 +579,39 @@ extern "C" int sa_bsattn_fwd(const void* q, const void* k, const void* v,
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   dim3 grid((nq + 1) / 2, H, B);
-  bsattn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
+  bsattn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, tk2, tv2, p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
+}
+
+}  // namespace
+
+extern "C" int sa_bsattn_fwd(const void* q, const void* k, const void* v,
+                             const int64_t q_strides[4], const int64_t k_strides[4],
+                             const int64_t v_strides[4], int B, int H, int Sq, int Sk, int D,
+                             const uint8_t* block_mask, const int64_t m_strides[4], int Hm,
+                             const int32_t* head_mask_type, float softmax_scale, void* out,
+                             const int64_t o_strides[4], float* lse, int32_t* status,
+                             cudaStream_t stream) {
+  return launch_attention("sa_bsattn_fwd", q, k, v, q_strides, k_strides, v_strides, B, H, Sq,
+                          Sk, D, block_mask, m_strides, Hm, head_mask_type, nullptr, nullptr,
+                          nullptr, nullptr, 0, 0.f, softmax_scale, out, o_strides, lse, status,
+                          stream);
+}
+
+extern "C" int sa_sink_dynamic_attn_fwd(
+    const void* q, const void* k, const void* v, const int64_t q_strides[4],
+    const int64_t k_strides[4], const int64_t v_strides[4], int B, int H, int Sq, int Sk, int D,
+    const uint8_t* block_mask, const int64_t m_strides[4], int Hm, const int32_t* head_mask_type,
+    const void* k_pool, const void* v_pool, const int64_t kp_strides[4],
+    const int64_t vp_strides[4], int Sk_pool, float log_gap, float softmax_scale, void* out,
+    const int64_t o_strides[4], float* lse, int32_t* status, cudaStream_t stream) {
+  if (k_pool == nullptr || v_pool == nullptr) {
+    sa::set_error("sa_sink_dynamic_attn_fwd: k_pool and v_pool are required");
+    return SA_EINVAL;
+  }
+  return launch_attention("sa_sink_dynamic_attn_fwd", q, k, v, q_strides, k_strides, v_strides,
+                          B, H, Sq, Sk, D, block_mask, m_strides, Hm, head_mask_type, k_pool,
+                          v_pool, kp_strides, vp_strides, Sk_pool, log_gap, softmax_scale, out,
+                          o_strides, lse, status, stream);
 }

@@ -153,6 +153,62 @@ def bsattn_fwd(
     return out, (lse if return_lse else None)
 
 
+def sink_dynamic_attn(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    block_mask: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    sample_gap: int,
+    softmax_scale: Optional[float] = None,
+    head_mask_type: Optional[torch.Tensor] = None,
+    return_lse: bool = False,
+    out: Optional[torch.Tensor] = None,
+):
+    """Sink attention over the kept blocks of `block_mask` fused with dense
+    attention over pooled keys/values (logits raised by ln(sample_gap)): the
+    adaptive mix of the Wan runtime in one kernel. Shapes as bsattn_fwd;
+    k_pool/v_pool [B,H,Sk_pool,D] bf16. Returns (out, lse or None)."""
+    dev = _require_cuda(q, k, v, block_mask, k_pool, v_pool, head_mask_type)
+    for t in (q, k, v, k_pool, v_pool):
+        if t.dtype != torch.bfloat16 or t.dim() != 4:
+            raise RuntimeError("sink_dynamic_attn expects 4-D bf16 tensors")
+    B, H, Sq, D = q.shape
+    Sk, Skp = k.shape[2], k_pool.shape[2]
+    if k_pool.shape != (B, H, Skp, D) or v_pool.shape != (B, H, Skp, D):
+        raise RuntimeError("k_pool / v_pool must be [B,H,Sk_pool,D]")
+    nq, nk = math.ceil(Sq / BLOCK), math.ceil(Sk / BLOCK)
+    if block_mask.dim() != 4 or block_mask.shape[-2:] != (nq, nk) or block_mask.shape[0] not in (1, B):
+        raise RuntimeError(f"block_mask must be [B|1, Hm, {nq}, {nk}], got {tuple(block_mask.shape)}")
+    if head_mask_type is not None:
+        head_mask_type = head_mask_type.to(torch.int32).contiguous()
+    q, k, v = _as_kernel_layout(q), _as_kernel_layout(k), _as_kernel_layout(v)
+    k_pool, v_pool = _as_kernel_layout(k_pool), _as_kernel_layout(v_pool)
+    if out is None:
+        out = torch.empty((B, Sq, H, D), dtype=q.dtype, device=dev).permute(0, 2, 1, 3)
+    lse = torch.empty((B, H, Sq), dtype=torch.float32, device=dev) if return_lse else None
+    ms = list(block_mask.stride())
+    if block_mask.shape[0] == 1:
+        ms[0] = 0
+    mstr = (_lib.ctypes.c_int64 * 4)(*ms)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_sink_dynamic_attn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            _lib.strides4(q), _lib.strides4(k), _lib.strides4(v),
+            B, H, Sq, Sk, D, block_mask.data_ptr(), mstr, block_mask.shape[1],
+            _ptr(head_mask_type), k_pool.data_ptr(), v_pool.data_ptr(),
+            _lib.strides4(k_pool), _lib.strides4(v_pool), Skp,
+            math.log(float(max(1, int(sample_gap)))),
+            -1.0 if softmax_scale is None else float(softmax_scale),
+            out.data_ptr(), _lib.strides4(out), _ptr(lse),
+            DeviceStatus.get(dev).data_ptr(), _stream(dev),
+        )
+    _lib.check(rc, "sa_sink_dynamic_attn_fwd")
+    return out, lse
+
+
 def pool_scores_workspace_size(B: int, H: int, S: int, D: int, block: int = BLOCK) -> int:
     return int(_lib.load().sa_pool_scores_workspace_size(B, H, S, D, block))
 

@@ -245,6 +245,51 @@ def _mix_attention_outputs(sink_out, sink_lse, dynamic_out, dynamic_lse, config,
     return ops.mix_outputs(sink_out, sink_lse, dynamic_out, dynamic_lse, gap)
 
 
+def fused_wan_inner_forward(self, q, k, v):
+    """WanSinkSparseInnerAttention.forward (wanx/runtime/sink_sparse_wan.py:181-282)
+    with the sink call, the pooled K/V dynamic call and the adaptive mix fused
+    into one kernel (sa_sink_dynamic_attn_fwd).
+
+    The runtime mask, timing sections and mask statistics are the reference
+    method's own. Configurations other than the Wan default (dynamic_mode
+    pooled_kv, adaptive mixing, block-sparse dynamic kernel) run the
+    reference's unfused method, which uses the other drop-in functions.
+    """
+    from contextlib import nullcontext
+
+    cfg = self.config
+    mode, gap = self._resolve_dynamic_plan()
+    fusable = (mode == "pooled_kv" and cfg.mixing_mode == "adaptive"
+               and str(cfg.dynamic_kernel) in {"block_sparse", "auto"})
+    if not fusable:
+        return _UNFUSED_WAN_FORWARD[0](self, q, k, v)
+    time_section = self.runtime_state.time_section if self.runtime_state is not None else None
+    with (time_section("inner_total") if time_section is not None else nullcontext()):
+        with (time_section("mask_prepare") if time_section is not None else nullcontext()):
+            sink_mask_tag = "__base__"
+            base_runtime_mask = self._get_runtime_mask(
+                sink_mask=self.sink_mask, mask_tag=sink_mask_tag, batch_size=q.size(0),
+                num_heads=q.size(1), seq_len_q=q.size(2), seq_len_k=k.size(2), device=q.device)
+        with (time_section("comp_pool") if time_section is not None else nullcontext()):
+            prefix_tokens = max(int(cfg.text_length), 0)
+            k_dyn = _mean_pool_sequence_preserve_prefix(k, gap, prefix_tokens=prefix_tokens)
+            v_dyn = _mean_pool_sequence_preserve_prefix(v, gap, prefix_tokens=prefix_tokens)
+            dynamic_seq_len_k = int(k_dyn.size(2))
+        with (time_section("sparse_main") if time_section is not None else nullcontext()):
+            mixed_out, _ = ops.sink_dynamic_attn(q, k, v, base_runtime_mask, k_dyn, v_dyn, gap)
+        if self.runtime_state is not None:
+            with self.runtime_state.time_section("stats"):
+                self.runtime_state.record_mask_stats(
+                    layer_idx=self.layer_idx, sink_mask_tag=sink_mask_tag, dynamic_mode=mode,
+                    dynamic_sample_gap=gap, base_runtime_mask=base_runtime_mask,
+                    topup_mask=None, dynamic_seq_len_k=dynamic_seq_len_k,
+                    total_seq_len_k=int(k.size(2)))
+        return mixed_out
+
+
+_UNFUSED_WAN_FORWARD: list = []
+
+
 _PATCHES = {
     "sinkattention.sparse_attention": {
         "block_sparse_attn_func": block_sparse_attn_func,
@@ -269,10 +314,12 @@ _PATCHES = {
 }
 
 
-def install(modules: Optional[list[str]] = None) -> list[str]:
+def install(modules: Optional[list[str]] = None, fused_dynamic: bool = True) -> list[str]:
     """Bind the replacements into the reference's modules (importing them if
     needed). Returns the list of patched module names; modules that cannot be
-    imported are skipped."""
+    imported are skipped. With fused_dynamic, WanSinkSparseInnerAttention.forward
+    is replaced by fused_wan_inner_forward (one kernel for the sink branch, the
+    pooled dynamic branch and their mix)."""
     import importlib
 
     patched = []
@@ -285,5 +332,11 @@ def install(modules: Optional[list[str]] = None) -> list[str]:
             continue
         for attr, val in attrs.items():
             setattr(mod, attr, val)
+        if fused_dynamic and name == "wanx.runtime.sink_sparse_wan":
+            cls = getattr(mod, "WanSinkSparseInnerAttention", None)
+            if cls is not None and cls.forward is not fused_wan_inner_forward:
+                if not _UNFUSED_WAN_FORWARD:
+                    _UNFUSED_WAN_FORWARD.append(cls.forward)
+                cls.forward = fused_wan_inner_forward
         patched.append(name)
     return patched

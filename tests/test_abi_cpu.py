@@ -147,3 +147,47 @@ def test_ops_reject_cpu_tensors():
         ops.pool_scores(q, q)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.coverage_mask(torch.rand(1, 4, 4))
+
+
+def test_install_binds_dropins_into_reference(monkeypatch):
+    """With the reference checkout importable, install() rebinds its hot-path
+    names (including the fused Wan inner forward); the rebound functions
+    refuse CPU tensors (no CPU fallback)."""
+    import sys
+
+    import torch
+
+    from tests.conftest import REFERENCE_DIR
+
+    if not (REFERENCE_DIR / "sinkattention").exists():
+        pytest.skip("reference checkout not available")
+    monkeypatch.syspath_prepend(str(REFERENCE_DIR))
+    import sinkattention.sparse_attention as sa
+    import wanx.runtime.sink_sparse_wan as wan
+
+    from sinkattn_b200 import reference_api as ra
+
+    orig_forward = wan.WanSinkSparseInnerAttention.forward
+    orig = {n: getattr(sa, n) for n in ("block_sparse_attn_func", "_block_sparse_attn",
+                                        "_compute_pooled_qk_block_scores",
+                                        "_build_direct_mean_coverage_mask")}
+    try:
+        patched = ra.install()
+        assert "sinkattention.sparse_attention" in patched
+        assert sa.block_sparse_attn_func is ra.block_sparse_attn_func
+        assert sa._HAS_BLOCK_SPARSE is True
+        assert wan._block_sparse_attn is ra._block_sparse_attn
+        assert wan.WanSinkSparseInnerAttention.forward is ra.fused_wan_inner_forward
+        cfg = sa.SinkSparseConfig().merged({"dynamic_mode": "pooled_kv", "dynamic_kernel": "block_sparse",
+                                            "sample_gap": 30, "runtime_diagonal_band_width": 1})
+        inner = wan.WanSinkSparseInnerAttention(0, torch.ones(2, 2, 2, dtype=torch.bool), cfg)
+        x = torch.zeros(1, 2, 256, 128, dtype=torch.bfloat16)
+        with pytest.raises(RuntimeError, match="CUDA"):
+            inner(x, x, x)
+    finally:
+        wan.WanSinkSparseInnerAttention.forward = orig_forward
+        for n, f in orig.items():
+            setattr(sa, n, f)
+        sa._HAS_BLOCK_SPARSE = orig["block_sparse_attn_func"] is not None
+        for m in [m for m in list(sys.modules) if m.startswith(("wanx", "zimg", "sinkattention"))]:
+            sys.modules.pop(m, None)

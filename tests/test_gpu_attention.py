@@ -268,3 +268,48 @@ def test_divergent_running_max_rescale(oracle, boost):
     ref, ref_lse = oracle.dense_masked_attention(_np(q), _np(k), _np(v), mask.numpy())
     _check(out, ref, f"rescale boost {boost}")
     np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=2e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("S,gap,prefix", [(1000, 30, 0), (777, 7, 0), (1100, 30, 77)])
+def test_fused_sink_dynamic_vs_oracle(oracle, S, gap, prefix):
+    """One kernel for the sink branch + pooled dynamic branch + adaptive mix
+    equals the exact union softmax with the ln(gap) logit bias."""
+    from sinkattn_b200 import ops
+
+    g = torch.Generator().manual_seed(S + gap)
+    B, H = 2, 2
+    q = torch.randn(B, H, S, 128, generator=g).bfloat16().cuda()
+    k = torch.randn(B, H, S, 128, generator=g).bfloat16().cuda()
+    v = torch.randn(B, H, S, 128, generator=g).bfloat16().cuda()
+    nb = math.ceil(S / 128)
+    mask = torch.rand(B, H, nb, nb, generator=g) < 0.3
+    mask[..., 0] = True
+    kp = ops.mean_pool_seq(k, gap, prefix)
+    vp = ops.mean_pool_seq(v, gap, prefix)
+    out, lse = ops.sink_dynamic_attn(q, k, v, mask.cuda(), kp, vp, gap, return_lse=True)
+    torch.cuda.synchronize()
+    ref, ref_lse = oracle.sink_dynamic_attention(_np(q), _np(k), _np(v), mask.numpy(), _np(kp),
+                                                 _np(vp), gap)
+    _check(out, ref, f"fused S={S} gap={gap}")
+    np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=2e-3, rtol=1e-4)
+
+
+def test_fused_sink_dynamic_vs_reference_wan_inner(golden):
+    """Against the reference's own WanSinkSparseInnerAttention run (two
+    attention calls + bf16-LSE mix), within the attention tolerance."""
+    from sinkattn_b200 import ops
+
+    q = regen_input(golden, "attn_sparse", "q").cuda()
+    k = regen_input(golden, "attn_sparse", "k").cuda()
+    v = regen_input(golden, "attn_sparse", "v").cuda()
+    gap = int(golden["wan_inner/sample_gap"])
+    band = int(golden["wan_inner/band"])
+    mask = torch.from_numpy(golden["attn_sparse/mask"]).cuda()
+    nq = mask.shape[-2]
+    ii = torch.arange(nq, device="cuda")
+    mask = mask | ((ii[:, None] - ii[None, :]).abs() <= band)
+    kp = ops.mean_pool_seq(k, gap, 0)
+    vp = ops.mean_pool_seq(v, gap, 0)
+    out, _ = ops.sink_dynamic_attn(q, k, v, mask, kp, vp, gap)
+    torch.cuda.synchronize()
+    _check(out, from_bits(golden["wan_inner/out"]), "fused vs reference wan inner")
