@@ -15,14 +15,16 @@ __global__ void accumulate_kernel(const float* __restrict__ x, int64_t n, float*
                                   float* __restrict__ sumsq, int first) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
+    // separate roundings (no FMA contraction), as the reference's
+    // `sums += scores; sq_sums += scores.square()` on fp32 tensors
     const float v = x[i];
-    const float sq = v * v;
+    const float sq = __fmul_rn(v, v);
     if (first) {
       sum[i] = v;
       sumsq[i] = sq;
     } else {
-      sum[i] += v;
-      sumsq[i] += sq;
+      sum[i] = __fadd_rn(sum[i], v);
+      sumsq[i] = __fadd_rn(sumsq[i], sq);
     }
   }
 }
@@ -35,11 +37,12 @@ __global__ void finalize_kernel(const float* __restrict__ sum, const float* __re
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float c = count != nullptr ? count[i] : scalar_count;
-    const float m = sum[i] / c;
+    // IEEE division and separate roundings, as the reference's CPU tensors
+    const float m = __fdiv_rn(sum[i], c);
     mean[i] = m;
     if (std_out != nullptr) {
-      const float second = sumsq[i] / c;
-      std_out[i] = sqrtf(fmaxf(second - m * m, 0.f));
+      const float second = __fdiv_rn(sumsq[i], c);
+      std_out[i] = __fsqrt_rn(fmaxf(__fsub_rn(second, __fmul_rn(m, m)), 0.f));
     }
   }
 }
