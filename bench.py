@@ -560,6 +560,25 @@ def run_case(args):
         gbs = 30 * (2 * B * H * S * D * 2 + H * NB * NB) / (ms / 1e3) / 1e9
         print(json.dumps({"case": args.case, "ms_per_pass": ms, "ms_per_layer": ms / 30, "gbs": gbs}))
         return 0
+    if args.case in ("stats-wan", "stats-small"):
+        # the exact and max block-statistics modes (dense Q K^T on the tensor cores)
+        Bc, Hc = (B, H) if args.case == "stats-wan" else (1, 2)
+        q, k, _ = wan_qk(seed=0, B=Bc, H=Hc, dtype=torch.bfloat16, device=dev)
+        res = {"case": args.case, "B": Bc, "H": Hc, "S": S}
+        for mode, sweeps in (("exact", 2), ("max", 1)):
+            ws = torch.empty(max(1, ops._lib.load().sa_block_stats_workspace_size(
+                Bc, Hc, S, ops._STATS_MODES[mode])), dtype=torch.uint8, device=dev)
+            out = torch.empty(Bc, Hc, NB, NB, dtype=torch.float32, device=dev)
+            fn = lambda: ops.block_stats(q, k, mode=mode, workspace=ws, out=out)  # noqa: E731
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            total, _ = time_steps(fn, args.steps, torch.cuda.current_stream(dev))
+            ms = total / args.steps
+            res[mode + "_ms"] = ms
+            res[mode + "_mma_tflops"] = sweeps * 2.0 * S * S * D * Bc * Hc / (ms / 1e3) / 1e12
+        print(json.dumps(res))
+        return 0
     if args.case in ("attn-wan", "calib-wan"):
         # quick timing of one kernel chain at the full Wan shape (no e2e / CPU legs)
         q, k, v = wan_qk(seed=0, dtype=torch.bfloat16, device=dev)
@@ -634,7 +653,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
-                                       "calib-pass", "wan-runtime"],
+                                       "calib-pass", "wan-runtime", "stats-wan", "stats-small"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)

@@ -183,6 +183,30 @@ SA_API int sa_pool_scores_noalloc(const void* q, const void* k,
                                   cudaStream_t stream);
 
 /*
+ * Block statistics of dense Q K^T for the two other calibration score modes.
+ * mode SA_STATS_EXACT replaces _compute_exact_block_mass_scores
+ *   (sinkattention/sparse_attention.py:145-227): scores[b,h,qb,kb] = mean over
+ *   the valid rows of query block qb of the softmax mass of key block kb.
+ * mode SA_STATS_MAX replaces the Triton kernel attn_with_pooling
+ *   (sinkattention/pooling_kernel.py:194-248, selected by pooling_mode "triton"
+ *   at sparse_attention.py:124-134): per row the bf16 maxima of the scaled
+ *   logits of every key block, Po = bf16(max over the block's rows of
+ *   exp2(R - row max)), then Po / sum(Po) rounded like bf16 tensors. S must be
+ *   a multiple of 128 in this mode.
+ * q, k: bf16 [B,H,S,D] strided, D = 128. scores: fp32 [B,H,nb,nb] contiguous.
+ * workspace: sa_block_stats_workspace_size() bytes (MAX mode only; NULL/0
+ * otherwise). softmax_scale <= 0 selects 1/sqrt(D). status: as sa_bsattn_fwd.
+ */
+#define SA_STATS_EXACT 0
+#define SA_STATS_MAX 1
+SA_API size_t sa_block_stats_workspace_size(int B, int H, int S, int mode);
+SA_API int sa_block_stats(const void* q, const void* k, const int64_t q_strides[4],
+                          const int64_t k_strides[4], int B, int H, int S, int D,
+                          int mode, float softmax_scale, float* scores,
+                          void* workspace, size_t ws_bytes, int32_t* status,
+                          cudaStream_t stream);
+
+/*
  * Running score statistics of one layer.
  * Replaces: SinkMaskCalibrator._accumulate_score (sparse_attention.py:537-549)
  *   on a device-resident accumulator: sum += x, sumsq += x*x, where x is an

@@ -387,3 +387,61 @@ def sink_dynamic_attention(q, k, v, block_mask, k_pool, v_pool, sample_gap: int,
             out[b, h] = (p @ vv / l).astype(np.float32)
             lse[b, h] = (np.log(l[:, 0]) + m[:, 0]).astype(np.float32)
     return out, lse
+
+
+def exact_block_mass_scores(q: np.ndarray, k: np.ndarray, block: int = 128) -> np.ndarray:
+    """_compute_exact_block_mass_scores (sinkattention/sparse_attention.py:145-227):
+    per query block, the mean over its rows of each key block's share of the
+    row's softmax mass; row sums clamped at 1e-6 (line 224). [B,H,nq,nk]."""
+    B, H, S, D = q.shape
+    Sk = k.shape[2]
+    scale = 1.0 / math.sqrt(D)
+    nq, nk = -(-S // block), -(-Sk // block)
+    out = np.zeros((B, H, nq, nk), dtype=np.float32)
+    for b in range(B):
+        for h in range(H):
+            s = (q[b, h].astype(np.float64) @ k[b, h].astype(np.float64).T) * scale
+            m = s.max(axis=1, keepdims=True)
+            e = np.exp(s - m)
+            rs = np.maximum(e.sum(axis=1, keepdims=True), 1e-6)
+            pad = nk * block - Sk
+            if pad:
+                e = np.concatenate([e, np.zeros((S, pad))], axis=1)
+            mass = e.reshape(S, nk, block).sum(axis=2) / rs
+            for i in range(nq):
+                out[b, h, i] = mass[i * block:min(S, (i + 1) * block)].mean(axis=0)
+    return out
+
+
+def triton_max_pool_scores(q: np.ndarray, k: np.ndarray, block: int = 128) -> np.ndarray:
+    """The statistics of the Triton kernel attn_with_pooling
+    (sinkattention/pooling_kernel.py:11-248):
+      R[r,kb]  = bf16(max_{n in kb} (q_r . k_n) * qk_scale),
+                 qk_scale = fp32(sm_scale) * fp32(1.44269504)   (lines 45-48, 161-162)
+      m_r      = max over kb of the unrounded values             (line 46)
+      Po[i,kb] = bf16(max_{r in block i} exp2(R[r,kb] - m_r))   (lines 65-75, l_i = 1)
+      scores   = Po / sum(Po, -1) with bf16 tensors              (lines 243-244).
+    Keys past S in the last block are masked (lines 34-41). For S not a
+    multiple of `block` the Triton kernel also reads query rows past the end
+    of the head; here those rows take no part in the column maxima."""
+    B, H, S, D = q.shape
+    nb = -(-S // block)
+    pad = nb * block - S
+    qk_scale = np.float32(np.float32(1.0 / math.sqrt(D)) * np.float32(1.44269504))
+    out = np.zeros((B, H, nb, nb), dtype=np.float32)
+    for b in range(B):
+        for h in range(H):
+            s = (q[b, h].astype(np.float64) @ k[b, h].astype(np.float64).T).astype(np.float32)
+            if pad:
+                s = np.concatenate([s, np.full((S, pad), -np.inf, np.float32)], axis=1)
+            bmax = s.reshape(S, nb, block).max(axis=2)
+            R = (bmax * qk_scale).astype(np.float32)
+            m = R.max(axis=1, keepdims=True)
+            Rb = bf16_round(R)
+            x = np.exp2((Rb - m).astype(np.float64)).astype(np.float32)
+            if pad:
+                x = np.concatenate([x, np.zeros((pad, nb), np.float32)], axis=0)
+            po = bf16_round(x.reshape(nb, block, nb).max(axis=1))
+            tot = bf16_round(po.astype(np.float64).sum(axis=1, keepdims=True).astype(np.float32))
+            out[b, h] = bf16_round((po / tot).astype(np.float32))
+    return out

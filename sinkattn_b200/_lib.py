@@ -26,6 +26,9 @@ SA_DEV_BAD_INDEX = 2
 SA_COVERAGE_JOINT = 0
 SA_COVERAGE_VIDEO_RESIDUAL = 1
 
+SA_STATS_EXACT = 0
+SA_STATS_MAX = 1
+
 SA_ROW_TIE_AT_CUT = 1
 SA_ROW_NEAR_TARGET = 2
 SA_ROW_EMPTY_FALLBACK = 4
@@ -61,6 +64,11 @@ _SIGNATURES = {
     "sa_pool_scores_noalloc": (
         _i,
         [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp],
+    ),
+    "sa_block_stats_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i]),
+    "sa_block_stats": (
+        _i,
+        [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, ctypes.c_size_t, _vp, _vp],
     ),
     "sa_score_accumulate": (_i, [_vp, ctypes.c_int64, _vp, _vp, _i, _vp]),
     "sa_score_finalize": (_i, [_vp, _vp, _vp, _f, ctypes.c_int64, _vp, _vp, _vp]),

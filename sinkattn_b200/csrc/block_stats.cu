@@ -1,0 +1,376 @@
+// block_stats.cu — dense per-(query row, key block) statistics of Q K^T on
+// tcgen05 tensor cores, for the two other calibration score modes:
+//
+//   EXACT  _compute_exact_block_mass_scores (sinkattention/sparse_attention.py:145-227)
+//          score[qb, kb] = mean over the query rows r of block qb of
+//            sum_{n in kb} exp(s_rn - m_r) / max(sum_n exp(s_rn - m_r), 1e-6),
+//          s = q k^T / sqrt(D), m_r the row maximum over all keys.
+//          Two sweeps over the keys: the first builds m_r and the normaliser
+//          online, the second accumulates the normalised block masses.
+//   MAX    the Triton pooling kernel attn_with_pooling (sinkattention/pooling_kernel.py:
+//          11-248), whose statistics are maxima (the "pooled" name notwithstanding):
+//            R[r, kb] = bf16( max_{n in kb} s_rn * log2(e) )         (line 45-48)
+//            m_r      = max_kb of the unrounded values                  (line 46)
+//            Po[qb,kb]= bf16( max_{r in qb} exp2(R[r,kb] - m_r) )      (lines 65-75)
+//          and the row normalisation Po / sum(Po) in bf16 (lines 243-244).
+//          For S not a multiple of 128 the Triton kernel reads query rows past
+//          the end of the head (its block pointers carry no boundary check);
+//          here rows past S take no part in the column maxima and keys past S
+//          are masked, as the Triton kernel masks its last key block.
+//
+// One CTA per 128-row query tile; 256 threads:
+//   warp 0      TMA producer: the Q tile once, then K tiles (4-slot ring)
+//   warp 1      MMA issuer: S = Q K^T into one of 4 TMEM buffers
+//   warp 2      TMEM allocator
+//   warps 4-7   statistics, thread t owns query row t
+// With no PV step the tensor core runs up to 4 key blocks ahead of the
+// statistics warps (S buffers double as the pipeline depth).
+
+#include <math.h>
+
+#include "sa_common.cuh"
+
+namespace sa {
+namespace stats {
+
+constexpr int kBM = 128, kBN = 128, kHD = 128;
+constexpr int kStages = 4;
+constexpr int kSBuf = 4;
+constexpr int kThreads = 256;
+constexpr int kTileBytes = kBM * kHD * 2;
+constexpr int kBoxBytes = kTileBytes / 2;
+constexpr int kMaxNB = 1024;
+
+enum Mode { kExact = 0, kMax = 1 };
+
+struct Params {
+  int B, H, S, nq, nk, mode;
+  float scale_log2;
+  float* scores;          // [B,H,nq,nk] fp32
+  __nv_bfloat16* rbuf;    // MAX: [B,H,nk,S] bf16 block maxima (rows contiguous per block)
+  int32_t* status;
+};
+
+struct __align__(8) SmemCtl {
+  uint64_t q_full;
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[kSBuf];
+  uint64_t s_empty[kSBuf];
+  uint64_t mma_drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  float red[4][kMaxNB];   // per-warp column partials
+  float po[kMaxNB];       // MAX: bf16 column maxima before normalisation
+  float psum[4];
+};
+
+constexpr size_t kSmemBytes = 1024 + kTileBytes + kStages * kTileBytes + sizeof(SmemCtl);
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ void stats_bar_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    block_stats_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_k, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* q_smem = smem;
+  uint8_t* ring = smem + kTileBytes;
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(ring + kStages * kTileBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int passes = p.mode == kExact ? 2 : 1;
+  const int items = passes * p.nk;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&ctl->q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&ctl->kv_full[i], 1);
+      mbar_init(&ctl->kv_empty[i], 1);
+    }
+    for (int i = 0; i < kSBuf; ++i) {
+      mbar_init(&ctl->s_full[i], 1);
+      mbar_init(&ctl->s_empty[i], kBM);
+    }
+    mbar_init(&ctl->mma_drain, 1);
+    ctl->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+  }
+  if (warp == 2) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&ctl->q_full, kTileBytes);
+      tma_load_4d(&tm_q, &ctl->q_full, q_smem, 0, qb * kBM, h, b);
+      tma_load_4d(&tm_q, &ctl->q_full, q_smem + kBoxBytes, 64, qb * kBM, h, b);
+      int it = 0;
+      for (; it < items; ++it) {
+        const int stage = it % kStages;
+        if (!mbar_wait(&ctl->kv_empty[stage], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.status,
+                       abort_flag))
+          break;
+        const int j = it % p.nk;
+        uint8_t* dst = ring + stage * kTileBytes;
+        mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
+        tma_load_4d(&tm_k, &ctl->kv_full[stage], dst, 0, j * kBN, h, b);
+        tma_load_4d(&tm_k, &ctl->kv_full[stage], dst + kBoxBytes, 64, j * kBN, h, b);
+      }
+      for (int k = (it > kStages ? it - kStages : 0); k < it; ++k)
+        mbar_wait_drain(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u);
+      mbar_wait_drain(&ctl->q_full, 0);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, kBN, 0, 0);
+      bool ok = mbar_wait(&ctl->q_full, 0, p.status, abort_flag);
+      tc_fence_after();
+      const uint32_t qa = smem_u32(q_smem);
+      const uint32_t ring_base = smem_u32(ring);
+      for (int it = 0; ok && it < items; ++it) {
+        const int stage = it % kStages, buf = it % kSBuf;
+        if (!mbar_wait(&ctl->kv_full[stage], (uint32_t)(it / kStages) & 1u, p.status, abort_flag))
+          break;
+        if (!mbar_wait(&ctl->s_empty[buf], ((uint32_t)(it / kSBuf) & 1u) ^ 1u, p.status,
+                       abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t tile = ring_base + stage * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+          mma_ss(tmem + buf * 128, make_sdesc_sw128(qa + off, 16, 1024),
+                 make_sdesc_sw128(tile + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&ctl->kv_empty[stage]);
+        mma_commit(&ctl->s_full[buf]);
+      }
+      mma_commit(&ctl->mma_drain);
+      mbar_wait_drain(&ctl->mma_drain, 0);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int grow = qb * kBM + row;
+    const bool row_valid = grow < p.S;
+    const int rows_valid = min(kBM, p.S - qb * kBM);
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const int64_t bh = (int64_t)b * p.H + h;
+    __nv_bfloat16* rrow = p.rbuf != nullptr ? p.rbuf + bh * p.nk * p.S + grow : nullptr;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int it = 0; it < items; ++it) {
+      const int buf = it % kSBuf;
+      const int pass = it / p.nk, j = it % p.nk;
+      if (ok)
+        ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf], (uint32_t)(it / kSBuf) & 1u,
+                                                 p.status, abort_flag));
+      if (!ok) continue;
+      tc_fence_after();
+      uint32_t r[4][32];
+      const uint32_t s_addr = tmem + lane_off + buf * 128;
+      tmem_ld32(s_addr + 0, r[0]);
+      tmem_ld32(s_addr + 32, r[1]);
+      tmem_ld32(s_addr + 64, r[2]);
+      tmem_ld32(s_addr + 96, r[3]);
+      tmem_wait_ld();
+      reg_fence32(r[0]);
+      reg_fence32(r[1]);
+      reg_fence32(r[2]);
+      reg_fence32(r[3]);
+      tc_fence_before();
+      mbar_arrive(&ctl->s_empty[buf]);  // S copied out: the buffer may be refilled
+      const int valid = min(kBN, p.S - j * kBN);
+      if (valid < kBN) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+      }
+      float mxp[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mxp[t] = __uint_as_float(r[0][t]);
+#pragma unroll
+      for (int c = 8; c < 128; c += 16) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          mxp[t] = fmax3(mxp[t], __uint_as_float(r[(c + t) >> 5][(c + t) & 31]),
+                         __uint_as_float(r[(c + 8 + t) >> 5][(c + 8 + t) & 31]));
+      }
+      const float bmax = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                               fmaxf(mxp[6], mxp[7]));
+      if (p.mode == kMax) {
+        // block maximum of the scaled logits (pooling_kernel.py:45-48)
+        const float R = bmax * p.scale_log2;
+        m = fmaxf(m, R);
+        if (row_valid) rrow[(int64_t)j * p.S] = __float2bfloat16_rn(R);
+        continue;
+      }
+      if (pass == 0) {
+        const float mx = bmax * p.scale_log2;
+        if (mx > m) {
+          l *= ex2_approx(m - mx);  // 0 when m = -inf
+          m = mx;
+        }
+      }
+      const float negm = -m;
+      float sp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 128; ++c)
+        sp[c & 3] += ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, negm));
+      const float mass = (sp[0] + sp[1]) + (sp[2] + sp[3]);
+      if (pass == 0) {
+        l += mass;
+      } else {
+        // this row's share of block j, normalised (sparse_attention.py:224),
+        // summed over the warp's rows
+        float v = row_valid ? mass / fmaxf(l, 1e-6f) : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) ctl->red[wq][j] = v;
+      }
+    }
+    if (p.mode == kExact) {
+      stats_bar_sync();
+      const float inv_rows = 1.0f / (float)rows_valid;
+      float* out = p.scores + (bh * p.nq + qb) * p.nk;
+      for (int j = row; j < p.nk; j += kBM)
+        out[j] = ((ctl->red[0][j] + ctl->red[1][j]) + (ctl->red[2][j] + ctl->red[3][j])) * inv_rows;
+    } else {
+      // Po[qb, kb] = bf16(max over the tile's rows of exp2(R - m_r)); l_i = 1
+      // in the Triton kernel, so there is no division (pooling_kernel.py:65-75).
+      __syncwarp();
+      for (int j = 0; j < p.nk; ++j) {
+        float x = row_valid ? ex2_approx(__bfloat162float(rrow[(int64_t)j * p.S]) - m) : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+        if (lane == 0) ctl->red[wq][j] = x;
+      }
+      stats_bar_sync();
+      float part = 0.f;
+      for (int j = row; j < p.nk; j += kBM) {
+        const float po = bf16_round(fmaxf(fmaxf(ctl->red[0][j], ctl->red[1][j]),
+                                          fmaxf(ctl->red[2][j], ctl->red[3][j])));
+        ctl->po[j] = po;
+        part += po;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0) ctl->psum[wq] = part;
+      stats_bar_sync();
+      // Po / sum(Po) with bf16 tensors (pooling_kernel.py:243-244): the sum is
+      // accumulated in fp32 and rounded to bf16, the quotient rounded to bf16.
+      const float sum = bf16_round((ctl->psum[0] + ctl->psum[1]) + (ctl->psum[2] + ctl->psum[3]));
+      float* out = p.scores + (bh * p.nq + qb) * p.nk;
+      for (int j = row; j < p.nk; j += kBM) out[j] = bf16_round(__fdiv_rn(ctl->po[j], sum));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace stats
+}  // namespace sa
+
+namespace {
+
+int make_map_bhsd(CUtensorMap* map, const void* base, const int64_t st[4], int B, int H, int S,
+                  int D) {
+  sa::EncodeTiledFn enc = sa::encode_tiled_fn();
+  if (enc == nullptr) return SA_ECUDA;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    sa::set_error("cuTensorMapEncodeTiled (block stats) failed (CUresult %d)", (int)r);
+    return SA_ECUDA;
+  }
+  return SA_OK;
+}
+
+bool stats_strides_ok(const int64_t st[4]) {
+  if (st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] < 0 || st[i] % 8 != 0) return false;
+  return true;
+}
+
+}  // namespace
+
+extern "C" size_t sa_block_stats_workspace_size(int B, int H, int S, int mode) {
+  if (B < 1 || H < 1 || S < 1) return 0;
+  if (mode != sa::stats::kMax) return 0;
+  const size_t nk = (size_t)((S + 127) / 128);
+  return (size_t)B * H * S * nk * 2;
+}
+
+extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_strides[4],
+                              const int64_t k_strides[4], int B, int H, int S, int D, int mode,
+                              float softmax_scale, float* scores, void* workspace, size_t ws_bytes,
+                              int32_t* status, cudaStream_t stream) {
+  using namespace sa::stats;
+  SA_CHECK_ARG(q && k && q_strides && k_strides && scores, "sa_block_stats: null pointer argument");
+  SA_CHECK_ARG(mode == kExact || mode == kMax, "sa_block_stats: unknown mode %d", mode);
+  SA_CHECK_ARG(D == kHD, "sa_block_stats: head dim must be 128, got %d", D);
+  SA_CHECK_ARG(B >= 1 && H >= 1 && S >= 1, "sa_block_stats: B, H, S must be >= 1");
+  SA_CHECK_ARG(B <= 65535 && H <= 65535, "sa_block_stats: B/H too large");
+  const int nq = (S + kBM - 1) / kBM, nk = nq;
+  SA_CHECK_ARG(nk <= kMaxNB, "sa_block_stats: S=%d exceeds %d blocks", S, kMaxNB);
+  SA_CHECK_ARG(stats_strides_ok(q_strides) && stats_strides_ok(k_strides),
+               "sa_block_stats: q/k need stride(dim)=1 and strides multiple of 8 elements");
+  SA_CHECK_ARG(((uintptr_t)q | (uintptr_t)k) % 16 == 0, "sa_block_stats: q/k must be 16-byte aligned");
+  const size_t need = sa_block_stats_workspace_size(B, H, S, mode);
+  SA_CHECK_ARG(need == 0 || (workspace != nullptr && ws_bytes >= need),
+               "sa_block_stats: workspace of %zu bytes required, got %zu", need, ws_bytes);
+
+  CUtensorMap tq, tk;
+  int rc;
+  if ((rc = make_map_bhsd(&tq, q, q_strides, B, H, S, D)) != SA_OK) return rc;
+  if ((rc = make_map_bhsd(&tk, k, k_strides, B, H, S, D)) != SA_OK) return rc;
+  Params p;
+  p.B = B; p.H = H; p.S = S; p.nq = nq; p.nk = nk; p.mode = mode;
+  // 1/sqrt(D) in double then fp32, as a Python float passed to fp32 math
+  const float scale = softmax_scale > 0.f ? softmax_scale : (float)(1.0 / sqrt((double)D));
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.scores = scores;
+  p.rbuf = reinterpret_cast<__nv_bfloat16*>(workspace);
+  p.status = status;
+  int dev = 0;
+  SA_CUDA_TRY(cudaGetDevice(&dev));
+  static bool attr_set[64] = {};
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    SA_CUDA_TRY(cudaFuncSetAttribute(block_stats_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  block_stats_kernel<<<dim3(nq, H, B), kThreads, kSmemBytes, stream>>>(tq, tk, p);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}

@@ -298,6 +298,48 @@ def pooled_softmax(qp: torch.Tensor, kp: torch.Tensor, scale: Optional[float] = 
     return scores, (bmean if want_batch_mean else None)
 
 
+_STATS_MODES = {"exact": _lib.SA_STATS_EXACT, "max": _lib.SA_STATS_MAX}
+
+
+def block_stats(q: torch.Tensor, k: torch.Tensor, mode: str = "exact",
+                scale: Optional[float] = None, workspace: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Block statistics of the full q k^T on the tensor cores, fp32 [B,H,nb,nb].
+
+    mode "exact": mean over each query block's rows of the softmax mass each
+    key block receives (the reference's exact pooling mode).
+    mode "max": the block-maximum statistics of the reference's Triton
+    pooling kernel, row-normalised with its bf16 rounding.
+    q, k: bf16 [B,H,S,128] of equal shape (any strides with stride(-1)=1).
+    """
+    dev = _require_cuda(q, k)
+    if mode not in _STATS_MODES:
+        raise ValueError(f"block_stats mode must be one of {sorted(_STATS_MODES)}, got {mode!r}")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise RuntimeError("block_stats expects bf16 q/k")
+    if q.shape != k.shape or q.dim() != 4:
+        raise RuntimeError("block_stats expects q, k of equal shape [B,H,S,D]")
+    B, H, S, D = q.shape
+    nb = math.ceil(S / BLOCK)
+    q, k = _as_kernel_layout(q), _as_kernel_layout(k)
+    m = _STATS_MODES[mode]
+    lib = _lib.load()
+    need = int(lib.sa_block_stats_workspace_size(B, H, S, m))
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    if out is None:
+        out = torch.empty((B, H, nb, nb), dtype=torch.float32, device=dev)
+    sc = -1.0 if scale is None else float(scale)
+    ws_bytes = 0 if not need else workspace.numel() * workspace.element_size()
+    with torch.cuda.device(dev):
+        rc = lib.sa_block_stats(q.data_ptr(), k.data_ptr(), _lib.strides4(q), _lib.strides4(k),
+                                B, H, S, D, m, sc, out.data_ptr(),
+                                workspace.data_ptr() if need else None, ws_bytes,
+                                DeviceStatus.get(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "sa_block_stats")
+    return out
+
+
 _PASS_STREAMS: dict[int, tuple] = {}
 
 

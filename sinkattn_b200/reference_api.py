@@ -9,6 +9,7 @@ reference's modules so the Wan and Z-Image processors run unchanged:
       external Block-Sparse-Attention forward (sparse_attention.py:22-28, 735-771)
   sinkattention.sparse_attention._block_sparse_attn            (lines 710-776)
   sinkattention.sparse_attention._compute_pooled_qk_block_scores (lines 118-142)
+  sinkattention.sparse_attention._compute_exact_block_mass_scores (lines 145-227)
   sinkattention.sparse_attention._build_direct_mean_coverage_mask (lines 268-376)
   sinkattention.sparse_attention._mean_pool_sequence_preserve_prefix (lines 97-115)
   sinkattention.sparse_attention._mix_attention_outputs        (lines 898-919)
@@ -164,16 +165,40 @@ def _block_sparse_attn(
     return out, lse.unsqueeze(-1).to(device=q.device, dtype=q.dtype)
 
 
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
+
+
 def _compute_pooled_qk_block_scores(q, k, v, config) -> torch.Tensor:
-    """sparse_attention.py:118-142: block scores softmax(pool(q) pool(k)^T /
-    sqrt(D)) per batch, [B,H,nb,nb] fp32. pooling_mode "mean" is the kernel's
-    rule; "triton" gets the same rule, as the reference itself does whenever
-    its Triton kernel is unavailable or fails (lines 124-137)."""
+    """sparse_attention.py:118-142, [B,H,nb,nb] fp32.
+
+    pooling_mode "triton" (compared case-sensitively, as line 124 does) runs
+    the block-maximum statistics of the reference's Triton kernel
+    (pooling_kernel.py:11-248) on the tensor cores; any other mode gets the
+    mean rule softmax(pool(q) pool(k)^T / sqrt(D)) of lines 138-142."""
+    if config.pooling_mode == "triton":
+        if int(config.block_size) != _BLOCK:
+            raise NotImplementedError(
+                f"triton pooling runs with block_size {_BLOCK} only, got {config.block_size}")
+        return ops.block_stats(_bf16(q), _bf16(k), mode="max", scale=1.0 / math.sqrt(q.size(-1)))
     block = int(config.block_size)
-    scores, _ = ops.pool_scores(q.to(torch.bfloat16) if q.dtype != torch.bfloat16 else q,
-                                k.to(torch.bfloat16) if k.dtype != torch.bfloat16 else k,
-                                block=block, scale=1.0 / math.sqrt(q.size(-1)))
+    scores, _ = ops.pool_scores(_bf16(q), _bf16(k), block=block, scale=1.0 / math.sqrt(q.size(-1)))
     return scores
+
+
+def _compute_exact_block_mass_scores(q, k, config) -> torch.Tensor:
+    """sparse_attention.py:145-227: per query block, the mean over its rows of
+    each key block's share of the row's softmax mass, [B,H,nq,nk] fp32, from
+    one tensor-core pass per query tile instead of two chunked fp32 matmul
+    sweeps per query block."""
+    if int(config.block_size) != _BLOCK:
+        raise NotImplementedError(
+            f"exact block-mass scores run with block_size {_BLOCK} only, got {config.block_size}")
+    if q.shape != k.shape:
+        raise NotImplementedError(
+            f"exact block-mass scores need q and k of one shape, got {tuple(q.shape)} and "
+            f"{tuple(k.shape)}")
+    return ops.block_stats(_bf16(q), _bf16(k), mode="exact", scale=1.0 / math.sqrt(q.size(-1)))
 
 
 def _ceil_div(a: int, b: int) -> int:
@@ -296,6 +321,7 @@ _PATCHES = {
         "_HAS_BLOCK_SPARSE": True,
         "_block_sparse_attn": _block_sparse_attn,
         "_compute_pooled_qk_block_scores": _compute_pooled_qk_block_scores,
+        "_compute_exact_block_mass_scores": _compute_exact_block_mass_scores,
         "_build_direct_mean_coverage_mask": _build_direct_mean_coverage_mask,
         "_mean_pool_sequence_preserve_prefix": _mean_pool_sequence_preserve_prefix,
         "_mix_attention_outputs": _mix_attention_outputs,

@@ -100,6 +100,19 @@ def main() -> int:
         g[f"{name}/block"] = np.array(c["block"])
         g[f"{name}/scores"] = out.numpy().astype(np.float32)
 
+    # ---- exact block-mass scores (sparse_attention.py:145-227) --------------
+    exact_cases = {
+        "exact_a": dict(B=1, H=2, S=600, seed=51),
+        "exact_b": dict(B=2, H=1, S=512, seed=52),
+    }
+    for name, c in exact_cases.items():
+        q = seeded_bf16((c["B"], c["H"], c["S"], 128), c["seed"])
+        k = seeded_bf16((c["B"], c["H"], c["S"], 128), c["seed"] + 100)
+        cfg = SinkSparseConfig(pooling_mode="exact")
+        out = sa._compute_exact_block_mass_scores(q.float(), k.float(), cfg)
+        pin_inputs(g, name, q=(q, c["seed"]), k=(k, c["seed"] + 100))
+        g[f"{name}/scores"] = out.numpy().astype(np.float32)
+
     # ---- coverage masks (sparse_attention.py:268-376) ---------------------
     def softmax_scores(H, nq, nk, seed, temp):
         gen = torch.Generator().manual_seed(seed)

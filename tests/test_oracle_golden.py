@@ -138,3 +138,25 @@ def test_kept_block_flops_counts_valid_area(oracle):
     mask[0, 0, 1, 2] = True  # last row block (rows 128..199) x last col block (256..299)
     f = oracle.kept_block_flops(mask, 1, 1, 200, 300)
     assert f == 4 * 128 * (72 * 44)
+
+
+@pytest.mark.parametrize("case", ["exact_a", "exact_b"])
+def test_exact_block_mass_matches_reference(golden, oracle, case):
+    q = regen_input(golden, case, "q").float().numpy()
+    k = regen_input(golden, case, "k").float().numpy()
+    got = oracle.exact_block_mass_scores(q, k)
+    np.testing.assert_allclose(got, golden[f"{case}/scores"], rtol=1e-4, atol=1e-7)
+
+
+def test_triton_max_pool_restatement_properties(oracle):
+    """The Triton max statistics (unpinned: the kernel needs a GPU and Triton):
+    rows are normalised (bf16 rounding aside), entries lie in [0, 1] and the
+    diagonal-heavy input peaks on the diagonal."""
+    rng = np.random.default_rng(0)
+    q = oracle.bf16_round(rng.standard_normal((1, 1, 512, 128)).astype(np.float32))
+    k = q.copy()
+    s = oracle.triton_max_pool_scores(q, k)
+    assert s.shape == (1, 1, 4, 4)
+    assert np.all(s >= 0) and np.all(s <= 1)
+    np.testing.assert_allclose(s.sum(-1), 1.0, atol=2e-2)
+    assert np.all(np.argmax(s[0, 0], axis=1) == np.arange(4))
