@@ -5,6 +5,7 @@ These pin the oracle before it is trusted as the GPU parity checker.
 from __future__ import annotations
 
 import math
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -148,10 +149,20 @@ def test_exact_block_mass_matches_reference(golden, oracle, case):
     np.testing.assert_allclose(got, golden[f"{case}/scores"], rtol=1e-4, atol=1e-7)
 
 
+@pytest.mark.parametrize("case", ["tri_a", "tri_b", "tri_c"])
+def test_triton_max_restatement_matches_reference_kernel(oracle, case):
+    """Pinned against outputs of the reference's Triton kernel run on a B200
+    (tests/golden/make_golden_triton.py): bit-identical on these cases."""
+    g = dict(np.load(Path(__file__).resolve().parent / "golden" / "triton_max.npz"))
+    q = regen_input(g, case, "q").float().numpy()
+    k = regen_input(g, case, "k").float().numpy()
+    got = oracle.triton_max_pool_scores(q, k)
+    np.testing.assert_array_equal(got, g[f"{case}/scores"])
+
+
 def test_triton_max_pool_restatement_properties(oracle):
-    """The Triton max statistics (unpinned: the kernel needs a GPU and Triton):
-    rows are normalised (bf16 rounding aside), entries lie in [0, 1] and the
-    diagonal-heavy input peaks on the diagonal."""
+    """Rows are normalised (bf16 rounding aside), entries lie in [0, 1] and
+    the diagonal-heavy input peaks on the diagonal."""
     rng = np.random.default_rng(0)
     q = oracle.bf16_round(rng.standard_normal((1, 1, 512, 128)).astype(np.float32))
     k = q.copy()
