@@ -377,6 +377,7 @@ def run_ours(args):
         ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
 
     tpool, _ = time_steps(step_pool_only, args.steps, stream)
+    tpool = max_over_ranks(tpool, world, dev)
 
     trace("calibration layer timed")
     # ---- cfg3: the 30-layer calibration pass, layers pipelined on two streams
@@ -427,8 +428,8 @@ def run_ours(args):
     barrier(world)
     te2e = max_over_ranks(te2e, world, dev)
     e2e_value = flops20 * world * args.steps / (te2e / 1e3) / 1e12
-    h2d = 3 * B * S * H * D * 2
-    d2h = B * S * H * D * 2 + B * H * S * 2
+    h2d = 3 * B * S * H * D * 2 * world
+    d2h = (B * S * H * D * 2 + B * H * S * 2) * world
 
     trace("e2e timed")
     # ---- CPU baseline (rank 0, N=1 only) ------------------------------------
@@ -462,13 +463,15 @@ def run_ours(args):
                                "unit": UNIT},
         "calibration_layer": {"ms_per_layer": tcal / args.steps,
                               "pool_scores_ms": tpool / args.steps,
-                              "bytes": calib_bytes,
-                              "gbs": calib_bytes / (tcal / args.steps / 1e3) / 1e9,
+                              "bytes": calib_bytes * world,
+                              "gbs": calib_bytes * world / (tcal / args.steps / 1e3) / 1e9,
                               "frac_of_hbm": calib_bytes / (tcal / args.steps / 1e3) / 1e9
-                              / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))},
+                              / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
+                              "note": "one layer per rank; bytes and gbs whole-job, frac per GPU"},
         "calibration_pass_30_layers": {
             "ms_per_pass": pass_ms, "ms_per_layer": pass_ms / 30,
-            "bytes_per_pass": pass_bytes, "gbs": pass_bytes / (pass_ms / 1e3) / 1e9,
+            "bytes_per_pass": pass_bytes * world,
+            "gbs": pass_bytes * world / (pass_ms / 1e3) / 1e9,
             "frac_of_hbm": pass_bytes / (pass_ms / 1e3) / 1e9
             / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
             "mask_density": density30,
@@ -483,7 +486,7 @@ def run_ours(args):
                      "kernel": "sa::attn::bsattn_fwd_kernel",
                      "peak_kind": f"bf16_tflops ({peak_kind}, burst)",
                      "algorithmic_flops_per_launch": flops20},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * world,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
@@ -625,26 +628,6 @@ def run_case(args):
     return 0
 
 
-# Multi-GPU runs of the attention kernel are held back: on a 2-GPU box the
-# second rank's first full-size attention launch did not complete (twice);
-# the cause is not yet identified, so N > 1 reports unavailable instead of
-# launching the kernel again.
-MULTI_GPU_HOLD = ("multi-GPU attention runs held back: the second rank's first full-size "
-                  "attention launch did not complete on a 2-GPU box (cause not yet found)")
-
-
-def run_multi_gpu_held(args):
-    world, rank, _ = dist_env()
-    if rank == 0:
-        print(json.dumps({"metric": METRIC, "value": None, "unit": UNIT, "n_gpus": args.gpus,
-                          "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                          "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                          "data": "synthetic", "unavailable": MULTI_GPU_HOLD,
-                          "config": {"workload": "wan_sink_attention_layer",
-                                     "parallelism": f"(b,h)-units x{world}"}}), flush=True)
-    return 0
-
-
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -661,8 +644,6 @@ def main(argv=None):
         return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
-    if max(args.gpus, dist_env()[0]) > 1:
-        return run_multi_gpu_held(args)
     return run_ours(args)
 
 

@@ -270,6 +270,42 @@ def test_divergent_running_max_rescale(oracle, boost):
     np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, atol=2e-3, rtol=1e-4)
 
 
+def test_wan_seed1_single_rescale_row(oracle):
+    """Full Wan-shape inputs from generator seed 1 with the cfg1-style mask
+    hold exactly one row whose running maximum is raised after its first
+    kept block: unit (b=1, h=7), row 3671, at key block 86, by 8.98 in log2
+    units, inside a warp whose other rows need no rescale. (These are the
+    multi-GPU bench's rank-1 inputs; seed 0 has no such row.) The query block
+    holding that row matches the oracle and every output is finite."""
+    from sinkattn_b200 import ops
+    from tests.gen import cfg1_mask, wan_qk
+
+    q, k, v = wan_qk(seed=1, device="cuda")
+    mask = cfg1_mask(12, 256, 256, seed=1).unsqueeze(0).expand(2, -1, -1, -1).contiguous()
+    out, lse = ops.bsattn_fwd(q, k, v, mask.cuda())
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all() and torch.isfinite(lse).all()
+    b, h, qb = 1, 7, 3671 // 128
+    # the row's scaled block maxima in log2 units; the kernel walks kept blocks
+    # in ascending order and raises its running maximum by more than 8 once
+    srow = (q[b, h, 3671].float() @ k[b, h].float().T).cpu() / math.sqrt(128) / math.log(2)
+    bmax = srow.view(256, 128).amax(-1)
+    kept = torch.nonzero(mask[b, h, qb]).flatten().tolist()
+    run, raised = float(bmax[kept[0]]), []
+    for j in kept[1:]:
+        if float(bmax[j]) > run + 8.0:
+            raised.append(j)
+            run = float(bmax[j])
+    assert raised == [86]
+    rows = slice(qb * 128, qb * 128 + 128)
+    ref, ref_lse = oracle.dense_masked_attention(
+        q[b:b + 1, h:h + 1, rows].float().cpu().numpy(), k[b:b + 1, h:h + 1].float().cpu().numpy(),
+        v[b:b + 1, h:h + 1].float().cpu().numpy(),
+        mask[b:b + 1, h:h + 1, qb:qb + 1].numpy())
+    _check(out[b:b + 1, h:h + 1, rows], ref, "seed-1 rescale row block")
+    np.testing.assert_allclose(lse[b, h, rows].cpu().numpy(), ref_lse[0, 0], atol=2e-3, rtol=1e-4)
+
+
 @pytest.mark.parametrize("S,gap,prefix", [(1000, 30, 0), (777, 7, 0), (1100, 30, 77)])
 def test_fused_sink_dynamic_vs_oracle(oracle, S, gap, prefix):
     """One kernel for the sink branch + pooled dynamic branch + adaptive mix
