@@ -563,6 +563,27 @@ def run_case(args):
         gbs = 30 * (2 * B * H * S * D * 2 + H * NB * NB) / (ms / 1e3) / 1e9
         print(json.dumps({"case": args.case, "ms_per_pass": ms, "ms_per_layer": ms / 30, "gbs": gbs}))
         return 0
+    if args.case == "qkrope-wan":
+        # the Q/K producer (RMSNorm + rotary) at the Wan shape: B=2, 32760 tokens, 12 x 128
+        tokens, hidden = 32760, H * D
+        g = torch.Generator(device=dev).manual_seed(0)
+        qa = torch.randn(B, tokens, hidden, generator=g, device=dev).bfloat16()
+        ka = torch.randn(B, tokens, hidden, generator=g, device=dev).bfloat16()
+        wq = torch.ones(hidden, device=dev).bfloat16()
+        ang = torch.outer(torch.arange(tokens, device=dev, dtype=torch.float32),
+                          torch.linspace(0, 1, D // 2, device=dev))
+        cos, sin = torch.cos(ang), torch.sin(ang)
+        qo, ko = torch.empty_like(qa), torch.empty_like(ka)
+        fn = lambda: ops.qk_norm_rope(qa, ka, D, 1e-6, wq, wq, cos, sin, out_q=qo, out_k=ko)  # noqa: E731
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        total, _ = time_steps(fn, args.steps, torch.cuda.current_stream(dev))
+        ms = total / args.steps
+        nbytes = 4 * B * tokens * hidden * 2
+        print(json.dumps({"case": args.case, "ms": ms, "bytes": nbytes,
+                          "gbs": nbytes / (ms / 1e3) / 1e9}))
+        return 0
     if args.case in ("stats-wan", "stats-small"):
         # the exact and max block-statistics modes (dense Q K^T on the tensor cores)
         Bc, Hc = (B, H) if args.case == "stats-wan" else (1, 2)
@@ -636,7 +657,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
-                                       "calib-pass", "wan-runtime", "stats-wan", "stats-small"],
+                                       "calib-pass", "wan-runtime", "stats-wan", "stats-small",
+                                       "qkrope-wan"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)

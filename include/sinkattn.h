@@ -219,13 +219,65 @@ SA_API int sa_score_accumulate(const float* x, int64_t n, float* sum, float* sum
 /*
  * mean = sum / count; std = sqrt(clamp_min(sumsq / count - mean^2, 0)).
  * Replaces: SinkMaskCalibrator._build_mean_and_masks (sparse_attention.py:563-566).
- * `count` is a device fp32 tensor [n] (presence-weighted, as in Z-Image,
- * zimg/runtime/sink_sparse_zimage.py:330-334) or NULL with a scalar
- * `scalar_count`. std is nullable.
+ * `count` is a device fp32 tensor [n] of per-element counts, used as given,
+ * or NULL with a scalar `scalar_count`. std is nullable. With emit_variance
+ * != 0, std_out receives the clamped variance instead (no square root): the
+ * reference takes that root with torch.sqrt on the CPU, which is not
+ * correctly rounded in every case, so a host that wants its bits applies the
+ * same operation itself.
  */
 SA_API int sa_score_finalize(const float* sum, const float* sumsq, const float* count,
                       float scalar_count, int64_t n, float* mean, float* std_out,
-                      cudaStream_t stream);
+                      int emit_variance, cudaStream_t stream);
+
+/*
+ * Z-Image calibration: one sample's block scores [H, n_blocks, n_blocks]
+ * (n_blocks = image_blocks + text_blocks) placed into the fixed
+ * [H, total_blocks, total_blocks] layout (image blocks first, the sample's
+ * text blocks at the end) and accumulated: sum += s, sumsq += s*s,
+ * presence += 1 where a score landed (0 elsewhere). `first` overwrites.
+ * Replaces: _align_scores_image_text_suffix, _alignment_presence_mask and
+ *   ZImageSinkMaskCalibrator._accumulate / record
+ *   (zimg/runtime/sink_sparse_zimage.py:140-186, 262-278, 300-319).
+ */
+SA_API int sa_score_accumulate_aligned(const float* scores, int H, int n_blocks,
+                                       int image_blocks, int text_blocks, int total_blocks,
+                                       float* sum, float* sumsq, float* presence, int first,
+                                       cudaStream_t stream);
+
+/*
+ * Presence-weighted mean and std: presence is raised to >= 1 in place, then
+ * mean = sum / presence, std = sqrt(clamp_min(sumsq / presence - mean^2, 0)).
+ * Replaces: ZImageSinkMaskCalibrator.build_package statistics
+ *   (zimg/runtime/sink_sparse_zimage.py:330-334). std is nullable;
+ *   emit_variance as for sa_score_finalize.
+ */
+SA_API int sa_score_finalize_presence(const float* sum, const float* sumsq, float* presence,
+                                      int64_t n, float* mean, float* std_out,
+                                      int emit_variance, cudaStream_t stream);
+
+/*
+ * Q/K producer of the sink attention: RMSNorm over the hidden dimension, then
+ * the rotary embedding, for Q and K in one pass.
+ *   y = bf16((x * rstd) * w), rstd = 1 / sqrt(sum(x^2) / hidden + eps);
+ *   per head (D channels) and pair i at position s = row % S:
+ *   out[2i] = bf16(y[2i] cos[s,i] - y[2i+1] sin[s,i]),
+ *   out[2i+1] = bf16(y[2i] sin[s,i] + y[2i+1] cos[s,i]).
+ * Rows are tokens (rows = B*S), `hidden` bf16 values each, row strides in
+ * elements (multiples of 8); in place is allowed. w_q/w_k: [hidden] bf16
+ * (w_is_bf16 != 0) or fp32, both NULL for no affine weight. cos/sin: fp32
+ * [S, >= D/2] with the given row stride, both NULL for no rotation.
+ * Replaces: apply_fast_qk_norm + apply_fast_rotary_qk in the Wan attention
+ *   processor (wanx/runtime/sink_sparse_wan.py:300-315;
+ *   wanx/runtime/fast_misc.py:834-864, 216-234).
+ */
+SA_API int sa_qk_norm_rope(const void* q_in, const void* k_in, int64_t q_in_row_stride,
+                           int64_t k_in_row_stride, int rows, int S, int hidden, int D,
+                           const void* w_q, const void* w_k, int w_is_bf16, float eps,
+                           const float* cos_table, const float* sin_table,
+                           int64_t freq_row_stride, void* q_out, void* k_out,
+                           int64_t q_out_row_stride, int64_t k_out_row_stride,
+                           cudaStream_t stream);
 
 /*
  * Per-row minimal coverage block mask.

@@ -445,3 +445,34 @@ def triton_max_pool_scores(q: np.ndarray, k: np.ndarray, block: int = 128) -> np
             tot = bf16_round(po.astype(np.float64).sum(axis=1, keepdims=True).astype(np.float32))
             out[b, h] = bf16_round((po / tot).astype(np.float32))
     return out
+
+
+def qk_norm_rope(x: np.ndarray, w: np.ndarray, eps: float, cos: np.ndarray, sin: np.ndarray,
+                 heads: int) -> np.ndarray:
+    """The Wan Q/K producer (wanx/runtime/sink_sparse_wan.py:300-315): RMSNorm
+    over the hidden dimension (fast_misc.py:306-340: y = x * rstd * w,
+    rstd = 1/sqrt(mean(x^2) + eps)), rounded to bf16, split into heads, then
+    the rotary product per channel pair (fast_misc.py:173-194: out_2i =
+    y_2i cos - y_2i+1 sin, out_2i+1 = y_2i sin + y_2i+1 cos), rounded to bf16.
+    x [B,S,hidden], w [hidden], cos/sin [S, D/2]; returns [B,H,S,D]."""
+    xf = x.astype(np.float64)
+    ms = (xf * xf).mean(axis=-1, keepdims=True)
+    y = bf16_round((xf / np.sqrt(ms + eps) * w.astype(np.float64)).astype(np.float32))
+    B, S, hidden = x.shape
+    D = hidden // heads
+    y = y.reshape(B, S, heads, D).transpose(0, 2, 1, 3).astype(np.float64)
+    ye, yo = y[..., 0::2], y[..., 1::2]
+    c = cos.astype(np.float64)[None, None]
+    s = sin.astype(np.float64)[None, None]
+    out = np.empty_like(y)
+    out[..., 0::2] = ye * c - yo * s
+    out[..., 1::2] = ye * s + yo * c
+    return bf16_round(out.astype(np.float32))
+
+
+def bf16_ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in bf16 steps between arrays of bf16-representable values."""
+    def key(v):
+        u = (np.ascontiguousarray(v, dtype=np.float32).view(np.uint32) >> 16).astype(np.int64)
+        return np.where(u & 0x8000, 0x8000 - u, u)  # monotone integer order
+    return np.abs(key(a) - key(b))

@@ -71,7 +71,14 @@ _SIGNATURES = {
         [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, ctypes.c_size_t, _vp, _vp],
     ),
     "sa_score_accumulate": (_i, [_vp, ctypes.c_int64, _vp, _vp, _i, _vp]),
-    "sa_score_finalize": (_i, [_vp, _vp, _vp, _f, ctypes.c_int64, _vp, _vp, _vp]),
+    "sa_score_finalize": (_i, [_vp, _vp, _vp, _f, ctypes.c_int64, _vp, _vp, _i, _vp]),
+    "sa_score_accumulate_aligned": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp]),
+    "sa_score_finalize_presence": (_i, [_vp, _vp, _vp, ctypes.c_int64, _vp, _vp, _i, _vp]),
+    "sa_qk_norm_rope": (
+        _i,
+        [_vp, _vp, ctypes.c_int64, ctypes.c_int64, _i, _i, _i, _i, _vp, _vp, _i, _f, _vp, _vp,
+         ctypes.c_int64, _vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp],
+    ),
     "sa_coverage_mask": (
         _i,
         [_vp, _vp, _i, _i, _i, _i, _f, _i, _i, _i, _vp, _vp, _vp, _vp, _vp],

@@ -1,18 +1,20 @@
-"""Device-resident sink-mask calibrator.
+"""Device-resident sink-mask calibrators.
 
-Same interface and package format as the reference's SinkMaskCalibrator
-(sinkattention/sparse_attention.py:526-608): record(layer, q, k, v) per
+Same interfaces and package format as the reference's SinkMaskCalibrator
+(sinkattention/sparse_attention.py:526-608) and ZImageSinkMaskCalibrator
+(zimg/runtime/sink_sparse_zimage.py:248-366): record(layer, q, k, v) per
 self-attention call, then build_package() / save(). The difference is where
-the statistics live: the reference takes every layer's batch-mean scores to
-the host (`.mean(dim=0).cpu()`, line 581) and accumulates sum and
-sum-of-squares there; here the pooled scores, their batch mean and both
-running sums stay on the GPU (sa_pool_scores + sa_score_accumulate), and only
-the final mean/std/mask leave it.
+the statistics live: the reference takes every layer's scores to the host
+(`.mean(dim=0).cpu()`, sparse_attention.py:581, sink_sparse_zimage.py:303)
+and accumulates there; here the block scores, the Z-Image alignment and the
+running sums stay on the GPU (sa_pool_scores / sa_block_stats,
+sa_score_accumulate(_aligned)), and only the final mean/std/mask leave it.
 
 The mean is sum / count in fp32 on the device, the same operations in the
-same order as the reference's CPU accumulation, and masks are built by the
-drop-in _build_direct_mean_coverage_mask on the host copy of the mean, so
-they equal the reference's builder bit for bit.
+same order as the reference's CPU accumulation; the std's square root is
+taken on the host copy of the variance with torch.sqrt, the reference's own
+CPU op; and masks are built by the drop-in _build_direct_mean_coverage_mask
+on the host copy of the mean. All three equal the reference's bit for bit.
 """
 from __future__ import annotations
 
@@ -23,7 +25,7 @@ from typing import Dict, Optional
 import torch
 
 from . import ops
-from .reference_api import _build_direct_mean_coverage_mask
+from .reference_api import _build_direct_mean_coverage_mask, _compute_block_scores
 
 
 class DeviceSinkMaskCalibrator:
@@ -72,12 +74,14 @@ class DeviceSinkMaskCalibrator:
         mean_scores, std_scores, sink_masks, counts = {}, {}, {}, {}
         for layer_idx in sorted(self.score_sums.keys()):
             key = str(layer_idx)
-            mean, std = ops.score_finalize(self.score_sums[layer_idx],
+            mean, var = ops.score_finalize(self.score_sums[layer_idx],
                                            self.score_sq_sums[layer_idx],
-                                           self.score_counts[layer_idx])
+                                           self.score_counts[layer_idx], variance=True)
             mean_cpu = mean.cpu()
             mean_scores[key] = mean_cpu
-            std_scores[key] = std.cpu()
+            # the root with the reference's own CPU op (not correctly rounded
+            # in every case), so the exported std carries the reference's bits
+            std_scores[key] = torch.sqrt(var.cpu())
             sink_masks[key] = _build_direct_mean_coverage_mask(mean_cpu, config)
             counts[key] = int(self.score_counts[layer_idx])
         return mean_scores, std_scores, sink_masks, counts
@@ -94,6 +98,122 @@ class DeviceSinkMaskCalibrator:
             "sink_masks": sink_masks,
             "counts": counts,
             "meta": {"route": "wanx_direct_coverage"},
+        }
+
+    def save(self, output_path: str, include_scores: bool = True, config_override=None) -> dict:
+        package = self.build_package(include_scores=include_scores,
+                                     config_override=config_override)
+        out = Path(output_path)
+        out.parent.mkdir(parents=True, exist_ok=True)
+        torch.save(package, out)
+        return package
+
+
+def _pad_to_multiple(value: int, multiple: int = 32) -> int:
+    return -(-int(value) // multiple) * multiple
+
+
+def _zimg_config(config):
+    """build_zimg_sink_config (zimg/runtime/sink_sparse_zimage.py:54-81) when the
+    reference's Z-Image runtime is importable; otherwise the config as given,
+    which must then already be a Z-Image config."""
+    try:
+        from zimg.runtime.sink_sparse_zimage import build_zimg_sink_config
+    except ImportError:
+        return config
+    return build_zimg_sink_config(package_config=asdict(config))
+
+
+class DeviceZImageSinkMaskCalibrator:
+    """ZImageSinkMaskCalibrator with its statistics on the GPU.
+
+    Every sample's scores [H, n, n] (n = image blocks + this sample's text
+    blocks) are aligned into the fixed [H, T, T] layout, image blocks first and
+    text blocks at the end, and accumulated with a presence count
+    (sa_score_accumulate_aligned); the mean is presence-weighted
+    (sa_score_finalize_presence). The fixed layout follows
+    _fixed_block_shape: image tokens and the maximum text length are padded
+    to multiples of 32 tokens (sink_sparse_zimage.py:30-35, 123-136)."""
+
+    def __init__(self, config):
+        self.config = _zimg_config(config)
+        self.current_step = -1
+        self.score_sums: Dict[int, torch.Tensor] = {}
+        self.score_sq_sums: Dict[int, torch.Tensor] = {}
+        self.score_presence_sums: Dict[int, torch.Tensor] = {}
+        self.score_counts: Dict[int, int] = {}
+        bs = int(self.config.block_size)
+        self.image_token_count = _pad_to_multiple(
+            int(self.config.token_width) * int(self.config.token_height)
+            * int(self.config.token_depth))
+        self.image_blocks = -(-self.image_token_count // bs)
+        self.max_text_tokens = _pad_to_multiple(int(self.config.text_length))
+        self.total_blocks = self.image_blocks + -(-self.max_text_tokens // bs)
+
+    def reset_generation(self) -> None:
+        self.current_step = -1
+
+    @torch.no_grad()
+    def record(self, layer_idx: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+               text_token_count: int) -> None:
+        """ZImageSinkMaskCalibrator.record (sink_sparse_zimage.py:281-319)."""
+        if layer_idx == 0:
+            self.current_step += 1
+        if text_token_count < 0:
+            raise ValueError(f"Invalid Z-Image text token count: {text_token_count}")
+        if text_token_count > self.max_text_tokens:
+            raise ValueError(
+                "Observed Z-Image text token count exceeds calibrated maximum. "
+                f"Observed {text_token_count}, configured max {self.max_text_tokens}.")
+        if q.size(0) != 1:
+            raise ValueError("Z-Image calibration expects one sample at a time after "
+                             "valid-token slicing.")
+        scores = _compute_block_scores(q, k, v, self.config).detach().float()[0]
+        current_text_blocks = -(-int(text_token_count) // int(self.config.block_size))
+        first = layer_idx not in self.score_sums
+        if first:
+            shape = (scores.size(0), self.total_blocks, self.total_blocks)
+            self.score_sums[layer_idx] = torch.empty(shape, dtype=torch.float32, device=q.device)
+            self.score_sq_sums[layer_idx] = torch.empty_like(self.score_sums[layer_idx])
+            self.score_presence_sums[layer_idx] = torch.empty_like(self.score_sums[layer_idx])
+            self.score_counts[layer_idx] = 0
+        ops.score_accumulate_aligned(scores, self.image_blocks, current_text_blocks,
+                                     self.total_blocks, self.score_sums[layer_idx],
+                                     self.score_sq_sums[layer_idx],
+                                     self.score_presence_sums[layer_idx], first=first)
+        self.score_counts[layer_idx] += 1
+
+    @torch.no_grad()
+    def build_package(self, include_scores: bool = True, config_override=None) -> dict:
+        """build_package (sink_sparse_zimage.py:321-354): presence-weighted
+        statistics, masks from the mean, package format version 3."""
+        export_config = self.config if config_override is None else _zimg_config(config_override)
+        mean_scores, std_scores, sink_masks, counts = {}, {}, {}, {}
+        for layer_idx in sorted(self.score_sums.keys()):
+            key = str(layer_idx)
+            mean, var = ops.score_finalize_presence(self.score_sums[layer_idx],
+                                                    self.score_sq_sums[layer_idx],
+                                                    self.score_presence_sums[layer_idx],
+                                                    variance=True)
+            mean_cpu = mean.cpu()
+            mean_scores[key] = mean_cpu
+            std_scores[key] = torch.sqrt(var.cpu())
+            sink_masks[key] = _build_direct_mean_coverage_mask(mean_cpu, export_config)
+            counts[key] = int(self.score_counts[layer_idx])
+        return {
+            "version": 3,
+            "config": asdict(export_config),
+            "mean_scores": mean_scores if include_scores else {},
+            "std_scores": std_scores if include_scores else {},
+            "sink_masks": sink_masks,
+            "counts": counts,
+            "meta": {
+                "route": "zimg_static_only",
+                "text_layout": "image_prefix_text_suffix_aligned",
+                "image_token_count": self.image_token_count,
+                "max_text_token_count": self.max_text_tokens,
+                "total_blocks": self.total_blocks,
+            },
         }
 
     def save(self, output_path: str, include_scores: bool = True, config_override=None) -> dict:

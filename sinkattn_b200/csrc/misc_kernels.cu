@@ -31,18 +31,62 @@ __global__ void accumulate_kernel(const float* __restrict__ x, int64_t n, float*
 
 // SinkMaskCalibrator._build_mean_and_masks (sparse_attention.py:563-566) and the
 // presence-weighted variant of zimg/runtime/sink_sparse_zimage.py:330-334.
+// With clamp_count the per-element counts are first raised to >= 1 in place,
+// as the Z-Image calibrator's `presence_sums.clamp_min_(1.0)` does.
+// With emit_variance the second output receives the clamped variance (no
+// square root), for hosts that take the root themselves.
 __global__ void finalize_kernel(const float* __restrict__ sum, const float* __restrict__ sumsq,
-                                const float* __restrict__ count, float scalar_count, int64_t n,
-                                float* __restrict__ mean, float* __restrict__ std_out) {
+                                float* __restrict__ count, float scalar_count, int64_t n,
+                                float* __restrict__ mean, float* __restrict__ std_out,
+                                int clamp_count, int emit_variance) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const float c = count != nullptr ? count[i] : scalar_count;
+    float c = count != nullptr ? count[i] : scalar_count;
+    if (clamp_count && c < 1.0f) {
+      c = 1.0f;
+      count[i] = c;
+    }
     // IEEE division and separate roundings, as the reference's CPU tensors
     const float m = __fdiv_rn(sum[i], c);
     mean[i] = m;
     if (std_out != nullptr) {
       const float second = __fdiv_rn(sumsq[i], c);
-      std_out[i] = __fsqrt_rn(fmaxf(__fsub_rn(second, __fmul_rn(m, m)), 0.f));
+      const float var = fmaxf(__fsub_rn(second, __fmul_rn(m, m)), 0.f);
+      std_out[i] = emit_variance ? var : __fsqrt_rn(var);
+    }
+  }
+}
+
+// ZImageSinkMaskCalibrator.record's alignment and accumulation
+// (zimg/runtime/sink_sparse_zimage.py:140-186, 262-278, 300-319): the scores of
+// one sample, [H, n, n] with n = image blocks + this sample's text blocks,
+// are placed in the fixed [H, T, T] layout (image blocks first, text blocks
+// at the end), and sum, sum of squares and presence (1 where a score landed)
+// accumulate there. Absent entries add 0, as the reference's zero-filled
+// aligned tensor does. One thread per target entry.
+__global__ void accumulate_aligned_kernel(const float* __restrict__ scores, int H, int n,
+                                          int image_blocks, int text_start, int T,
+                                          float* __restrict__ sum, float* __restrict__ sumsq,
+                                          float* __restrict__ presence, int first) {
+  const int64_t total = (int64_t)H * T * T;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int h = (int)(e / ((int64_t)T * T));
+    const int ti = (int)((e / T) % T), tj = (int)(e % T);
+    const int si = ti < image_blocks ? ti : (ti >= text_start ? image_blocks + (ti - text_start) : -1);
+    const int sj = tj < image_blocks ? tj : (tj >= text_start ? image_blocks + (tj - text_start) : -1);
+    const bool present = si >= 0 && sj >= 0;
+    const float v = present ? scores[((int64_t)h * n + si) * n + sj] : 0.f;
+    const float sq = __fmul_rn(v, v);
+    const float pr = present ? 1.f : 0.f;
+    if (first) {
+      sum[e] = v;
+      sumsq[e] = sq;
+      presence[e] = pr;
+    } else {
+      sum[e] = __fadd_rn(sum[e], v);
+      sumsq[e] = __fadd_rn(sumsq[e], sq);
+      presence[e] = __fadd_rn(presence[e], pr);
     }
   }
 }
@@ -167,14 +211,50 @@ extern "C" int sa_score_accumulate(const float* x, int64_t n, float* sum, float*
 
 extern "C" int sa_score_finalize(const float* sum, const float* sumsq, const float* count,
                                  float scalar_count, int64_t n, float* mean, float* std_out,
-                                 cudaStream_t stream) {
+                                 int emit_variance, cudaStream_t stream) {
   SA_CHECK_ARG(sum && mean, "sa_score_finalize: null pointer argument");
   SA_CHECK_ARG(std_out == nullptr || sumsq != nullptr, "sa_score_finalize: std needs sumsq");
   SA_CHECK_ARG(count != nullptr || scalar_count > 0.f, "sa_score_finalize: count must be > 0");
   SA_CHECK_ARG(n >= 0, "sa_score_finalize: n must be >= 0");
   if (n == 0) return SA_OK;
   sa::misc::finalize_kernel<<<sa::misc::grid_for(n, 256), 256, 0, stream>>>(
-      sum, sumsq, count, scalar_count, n, mean, std_out);
+      sum, sumsq, const_cast<float*>(count), scalar_count, n, mean, std_out, 0, emit_variance);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_score_accumulate_aligned(const float* scores, int H, int n_blocks,
+                                           int image_blocks, int text_blocks, int total_blocks,
+                                           float* sum, float* sumsq, float* presence, int first,
+                                           cudaStream_t stream) {
+  SA_CHECK_ARG(scores && sum && sumsq && presence,
+               "sa_score_accumulate_aligned: null pointer argument");
+  SA_CHECK_ARG(H >= 1 && image_blocks >= 0 && text_blocks >= 0,
+               "sa_score_accumulate_aligned: bad sizes");
+  SA_CHECK_ARG(n_blocks == image_blocks + text_blocks,
+               "Unexpected Z-Image block score shape. Expected %dx%d, got %dx%d.",
+               image_blocks + text_blocks, image_blocks + text_blocks, n_blocks, n_blocks);
+  SA_CHECK_ARG(image_blocks + text_blocks <= total_blocks,
+               "sa_score_accumulate_aligned: %d image + %d text blocks exceed the %d-block layout",
+               image_blocks, text_blocks, total_blocks);
+  const int64_t total = (int64_t)H * total_blocks * total_blocks;
+  if (total == 0) return SA_OK;
+  sa::misc::accumulate_aligned_kernel<<<sa::misc::grid_for(total, 256), 256, 0, stream>>>(
+      scores, H, n_blocks, image_blocks, total_blocks - text_blocks, total_blocks, sum, sumsq,
+      presence, first);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_score_finalize_presence(const float* sum, const float* sumsq, float* presence,
+                                          int64_t n, float* mean, float* std_out,
+                                          int emit_variance, cudaStream_t stream) {
+  SA_CHECK_ARG(sum && sumsq && presence && mean,
+               "sa_score_finalize_presence: null pointer argument");
+  SA_CHECK_ARG(n >= 0, "sa_score_finalize_presence: n must be >= 0");
+  if (n == 0) return SA_OK;
+  sa::misc::finalize_kernel<<<sa::misc::grid_for(n, 256), 256, 0, stream>>>(
+      sum, sumsq, presence, 0.f, n, mean, std_out, 1, emit_variance);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }

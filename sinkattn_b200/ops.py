@@ -479,7 +479,11 @@ def score_accumulate(x: torch.Tensor, sum_: torch.Tensor, sumsq: torch.Tensor, f
     _lib.check(rc, "sa_score_accumulate")
 
 
-def score_finalize(sum_: torch.Tensor, sumsq: torch.Tensor, count) -> tuple[torch.Tensor, torch.Tensor]:
+def score_finalize(sum_: torch.Tensor, sumsq: torch.Tensor, count,
+                   variance: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """(mean, std) of running sums over `count` samples (a number or a per-
+    element tensor); with variance=True the second result is the clamped
+    variance instead of its square root."""
     dev = _require_cuda(sum_, sumsq)
     mean = torch.empty_like(sum_)
     std = torch.empty_like(sum_)
@@ -490,9 +494,109 @@ def score_finalize(sum_: torch.Tensor, sumsq: torch.Tensor, count) -> tuple[torc
     with torch.cuda.device(dev):
         rc = lib.sa_score_finalize(sum_.data_ptr(), sumsq.data_ptr(), _ptr(cnt_t),
                                    float(count) if cnt_t is None else 0.0, sum_.numel(),
-                                   mean.data_ptr(), std.data_ptr(), _stream(dev))
+                                   mean.data_ptr(), std.data_ptr(), int(variance), _stream(dev))
     _lib.check(rc, "sa_score_finalize")
     return mean, std
+
+
+def score_accumulate_aligned(scores: torch.Tensor, image_blocks: int, text_blocks: int,
+                             total_blocks: int, sum_: torch.Tensor, sumsq: torch.Tensor,
+                             presence: torch.Tensor, first: bool) -> None:
+    """Place one sample's fp32 scores [H, n, n] (n = image + text blocks) into
+    the fixed [H, T, T] layout and accumulate sum, sum of squares and presence
+    there (the Z-Image calibrator's alignment)."""
+    dev = _require_cuda(scores, sum_, sumsq, presence)
+    if scores.dtype != torch.float32 or scores.dim() != 3 or scores.shape[1] != scores.shape[2]:
+        raise ValueError(f"Expected [heads, blocks_q, blocks_k] scores, got {tuple(scores.shape)}")
+    H, n = scores.shape[0], scores.shape[1]
+    for t in (sum_, sumsq, presence):
+        if t.shape != (H, total_blocks, total_blocks) or t.dtype != torch.float32 \
+                or not t.is_contiguous():
+            raise RuntimeError("aligned accumulators must be contiguous fp32 [H, T, T]")
+    scores = scores.contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_score_accumulate_aligned(scores.data_ptr(), H, n, int(image_blocks),
+                                             int(text_blocks), int(total_blocks), sum_.data_ptr(),
+                                             sumsq.data_ptr(), presence.data_ptr(), int(first),
+                                             _stream(dev))
+    if rc == _lib.SA_EINVAL and "Z-Image block score shape" in lib.sa_last_error().decode():
+        raise ValueError(lib.sa_last_error().decode())
+    _lib.check(rc, "sa_score_accumulate_aligned")
+
+
+def score_finalize_presence(sum_: torch.Tensor, sumsq: torch.Tensor, presence: torch.Tensor,
+                            variance: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """Presence-weighted mean/std (or clamped variance with variance=True);
+    presence is clamped to >= 1 in place."""
+    dev = _require_cuda(sum_, sumsq, presence)
+    if not (sum_.is_contiguous() and sumsq.is_contiguous() and presence.is_contiguous()):
+        raise RuntimeError("score_finalize_presence expects contiguous tensors")
+    mean = torch.empty_like(sum_)
+    std = torch.empty_like(sum_)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_score_finalize_presence(sum_.data_ptr(), sumsq.data_ptr(), presence.data_ptr(),
+                                            sum_.numel(), mean.data_ptr(), std.data_ptr(),
+                                            int(variance), _stream(dev))
+    _lib.check(rc, "sa_score_finalize_presence")
+    return mean, std
+
+
+def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, head_dim: int, eps: float,
+                 w_q: Optional[torch.Tensor] = None, w_k: Optional[torch.Tensor] = None,
+                 cos: Optional[torch.Tensor] = None, sin: Optional[torch.Tensor] = None,
+                 out_q: Optional[torch.Tensor] = None, out_k: Optional[torch.Tensor] = None):
+    """RMSNorm over the hidden dimension + rotary embedding for Q and K.
+
+    q, k: bf16 [B, S, hidden] (the projections' outputs, stride(-1) = 1);
+    w_q, w_k: [hidden] bf16 or fp32 (or None); cos, sin: fp32 [S, head_dim/2]
+    (or None: no rotation). Returns (q, k) bf16 [B, S, hidden]; out_q/out_k
+    may alias q/k (in place).
+    """
+    dev = _require_cuda(q, k, w_q, w_k, cos, sin)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or q.dim() != 3 or q.shape != k.shape:
+        raise RuntimeError("qk_norm_rope expects bf16 q, k of one shape [B, S, hidden]")
+    B, S, hidden = q.shape
+
+    def rows_view(t):
+        if t.stride(-1) != 1 or t.stride(0) != S * t.stride(1):
+            t = t.contiguous()
+        return t
+
+    q, k = rows_view(q), rows_view(k)
+    if out_q is None:
+        out_q = torch.empty((B, S, hidden), dtype=torch.bfloat16, device=dev)
+    if out_k is None:
+        out_k = torch.empty((B, S, hidden), dtype=torch.bfloat16, device=dev)
+    for o in (out_q, out_k):
+        if o.shape != (B, S, hidden) or o.dtype != torch.bfloat16 or o.stride(-1) != 1 \
+                or o.stride(0) != S * o.stride(1):
+            raise RuntimeError("qk_norm_rope outputs must be bf16 [B, S, hidden] with uniform rows")
+    w_bf16 = 1
+    if w_q is not None:
+        if w_q.dtype == torch.bfloat16 and w_k.dtype == torch.bfloat16:
+            w_q, w_k = w_q.contiguous(), w_k.contiguous()
+        else:
+            w_q, w_k = w_q.float().contiguous(), w_k.float().contiguous()
+            w_bf16 = 0
+        if w_q.numel() != hidden or w_k.numel() != hidden:
+            raise RuntimeError(f"norm weights must have {hidden} elements")
+    fs = 0
+    if cos is not None:
+        cos, sin = cos.float().contiguous(), sin.float().contiguous()
+        if cos.shape != (S, head_dim // 2) or sin.shape != (S, head_dim // 2):
+            raise ValueError(f"Rotary frequency shape mismatch: expected {(S, head_dim // 2)}, "
+                             f"got {tuple(cos.shape)}")
+        fs = cos.stride(0)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_qk_norm_rope(q.data_ptr(), k.data_ptr(), q.stride(1), k.stride(1), B * S, S,
+                                 hidden, int(head_dim), _ptr(w_q), _ptr(w_k), w_bf16, float(eps),
+                                 _ptr(cos), _ptr(sin), fs, out_q.data_ptr(), out_k.data_ptr(),
+                                 out_q.stride(1), out_k.stride(1), _stream(dev))
+    _lib.check(rc, "sa_qk_norm_rope")
+    return out_q, out_k
 
 
 def mean_pool_seq(x: torch.Tensor, pool: int, prefix: int = 0) -> torch.Tensor:

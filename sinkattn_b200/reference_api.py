@@ -201,6 +201,18 @@ def _compute_exact_block_mass_scores(q, k, config) -> torch.Tensor:
     return ops.block_stats(_bf16(q), _bf16(k), mode="exact", scale=1.0 / math.sqrt(q.size(-1)))
 
 
+def _compute_block_scores(q, k, v, config) -> torch.Tensor:
+    """sparse_attention.py:230-238: the calibration score mode dispatch over the
+    drop-ins above."""
+    pooling_mode = str(config.pooling_mode).strip().lower()
+    if pooling_mode == "exact":
+        return _compute_exact_block_mass_scores(q, k, config)
+    if pooling_mode in {"triton", "mean"}:
+        return _compute_pooled_qk_block_scores(q, k, v, config)
+    raise ValueError(
+        f"Unsupported pooling_mode: {config.pooling_mode}. Expected one of: exact, triton, mean.")
+
+
 def _ceil_div(a: int, b: int) -> int:
     return (a + b - 1) // b
 
@@ -315,6 +327,68 @@ def fused_wan_inner_forward(self, q, k, v):
 _UNFUSED_WAN_FORWARD: list = []
 
 
+def _rotary_tables(freqs, S: int, D: int):
+    """cos/sin fp32 [S, D/2] from the rotary embedding the Wan processor gets:
+    a complex tensor [1,1,S,D/2] or [S,D/2] (wanx/runtime/fast_misc.py:711-720),
+    a (real, imag) pair of [S,D/2] tensors, or Wan's (cos, sin) pair repeated
+    per channel, [1,S,1,D], read at even and odd channels (fast_misc.py:145-170)."""
+    if isinstance(freqs, torch.Tensor) and torch.is_complex(freqs):
+        re, im = freqs.real, freqs.imag
+    elif isinstance(freqs, (tuple, list)) and len(freqs) == 2:
+        re, im = freqs
+        if re.shape[-1] == D and re.numel() == S * D:
+            re, im = re.reshape(S, D)[:, 0::2], im.reshape(S, D)[:, 1::2]
+    else:
+        raise TypeError(f"Unsupported rotary embedding type: {type(freqs)!r}")
+    return re.reshape(S, D // 2).float(), im.reshape(S, D // 2).float()
+
+
+def _rms_like(norm) -> bool:
+    # the RMSNorm test of apply_fast_qk_norm (fast_misc.py:846-852)
+    if norm is None or getattr(norm, "weight", None) is None or getattr(norm, "eps", None) is None:
+        return False
+    return "layernorm" not in norm.__class__.__name__.lower() and getattr(norm, "bias", None) is None
+
+
+def fused_prepare_attention_tensors(attn, hidden_states, encoder_hidden_states=None,
+                                    rotary_emb=None):
+    """_prepare_attention_tensors (wanx/runtime/sink_sparse_wan.py:285-315) for
+    self-attention with RMS-normalised Q/K and a rotary embedding: the Q/K
+    RMSNorm and the rotation run as one kernel (sa_qk_norm_rope) on the
+    projections' outputs. Q, K and V come back as [B,H,S,D] views of the
+    [B,S,H*D] projections, the layout the attention kernel reads. Other
+    configurations run the reference's own function."""
+    norm_q, norm_k = getattr(attn, "norm_q", None), getattr(attn, "norm_k", None)
+    fusable = (encoder_hidden_states is None and rotary_emb is not None
+               and hidden_states.is_cuda and _rms_like(norm_q) and _rms_like(norm_k))
+    if not fusable:
+        return _UNFUSED_PREPARE[0](attn, hidden_states, encoder_hidden_states, rotary_emb)
+    from contextlib import nullcontext
+
+    timing = getattr(getattr(attn, "inner_attention", None), "timing", None)
+    query = attn.to_q(hidden_states)
+    key = attn.to_k(hidden_states)
+    value = attn.to_v(hidden_states)
+    if query.dtype != torch.bfloat16:
+        return _UNFUSED_PREPARE[0](attn, hidden_states, encoder_hidden_states, rotary_emb)
+    S = query.shape[1]
+    D = query.shape[-1] // attn.heads
+    with (timing.section("qk_norm") if timing is not None and timing.is_enabled else nullcontext()):
+        cos, sin = _rotary_tables(rotary_emb, S, D)
+        in_place = not (query.requires_grad or key.requires_grad)
+        query, key = ops.qk_norm_rope(query, key, D, float(norm_q.eps), norm_q.weight,
+                                      norm_k.weight, cos.to(query.device), sin.to(query.device),
+                                      out_q=query if in_place else None,
+                                      out_k=key if in_place else None)
+    query = query.unflatten(2, (attn.heads, -1)).transpose(1, 2)
+    key = key.unflatten(2, (attn.heads, -1)).transpose(1, 2)
+    value = value.unflatten(2, (attn.heads, -1)).transpose(1, 2)
+    return query, key, value, None
+
+
+_UNFUSED_PREPARE: list = []
+
+
 _PATCHES = {
     "sinkattention.sparse_attention": {
         "block_sparse_attn_func": block_sparse_attn_func,
@@ -345,7 +419,8 @@ def install(modules: Optional[list[str]] = None, fused_dynamic: bool = True) -> 
     needed). Returns the list of patched module names; modules that cannot be
     imported are skipped. With fused_dynamic, WanSinkSparseInnerAttention.forward
     is replaced by fused_wan_inner_forward (one kernel for the sink branch, the
-    pooled dynamic branch and their mix)."""
+    pooled dynamic branch and their mix). In the Wan runtime the Q/K RMSNorm and
+    rotary embedding become one kernel (fused_prepare_attention_tensors)."""
     import importlib
 
     patched = []
@@ -358,11 +433,15 @@ def install(modules: Optional[list[str]] = None, fused_dynamic: bool = True) -> 
             continue
         for attr, val in attrs.items():
             setattr(mod, attr, val)
+        if name == "wanx.runtime.sink_sparse_wan":
+            orig = getattr(mod, "_prepare_attention_tensors", None)
+            if orig is not None and orig is not fused_prepare_attention_tensors:
+                _UNFUSED_PREPARE[:] = [orig]
+                mod._prepare_attention_tensors = fused_prepare_attention_tensors
         if fused_dynamic and name == "wanx.runtime.sink_sparse_wan":
             cls = getattr(mod, "WanSinkSparseInnerAttention", None)
             if cls is not None and cls.forward is not fused_wan_inner_forward:
-                if not _UNFUSED_WAN_FORWARD:
-                    _UNFUSED_WAN_FORWARD.append(cls.forward)
+                _UNFUSED_WAN_FORWARD[:] = [cls.forward]
                 cls.forward = fused_wan_inner_forward
         patched.append(name)
     return patched

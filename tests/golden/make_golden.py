@@ -113,6 +113,47 @@ def main() -> int:
         pin_inputs(g, name, q=(q, c["seed"]), k=(k, c["seed"] + 100))
         g[f"{name}/scores"] = out.numpy().astype(np.float32)
 
+    # ---- Q/K producer: RMSNorm + rotary (wanx/runtime/sink_sparse_wan.py:300-315)
+    # through the reference's own helpers with its default (non-Triton) path:
+    # torch RMSNorm modules and the fp64 complex rotary (fast_misc.py:173-179).
+    import wanx.runtime.fast_misc as fm
+
+    S_r, H_r, D_r = 96, 2, 128
+    hidden = H_r * D_r
+    q_lin = seeded_bf16((1, S_r, hidden), 71)
+    k_lin = seeded_bf16((1, S_r, hidden), 72)
+    gw = torch.Generator().manual_seed(73)
+    w_q = (1.0 + 0.25 * torch.randn(hidden, generator=gw)).to(torch.bfloat16)
+    w_k = (1.0 + 0.25 * torch.randn(hidden, generator=gw)).to(torch.bfloat16)
+
+    class _Attn:
+        pass
+
+    attn = _Attn()
+    attn.norm_q = torch.nn.RMSNorm(hidden, eps=1e-6, dtype=torch.bfloat16)
+    attn.norm_k = torch.nn.RMSNorm(hidden, eps=1e-6, dtype=torch.bfloat16)
+    with torch.no_grad():
+        attn.norm_q.weight.copy_(w_q)
+        attn.norm_k.weight.copy_(w_k)
+    # 1-D RoPE frequencies theta^(-2i/D), positions 0..S-1, complex64 [1,1,S,D/2]
+    inv = 1.0 / (10000.0 ** (torch.arange(0, D_r, 2, dtype=torch.float64) / D_r))
+    ang = torch.outer(torch.arange(S_r, dtype=torch.float64), inv)
+    freqs = torch.polar(torch.ones_like(ang), ang).to(torch.complex64)[None, None]
+    with torch.no_grad():
+        qn, kn = fm.apply_fast_qk_norm(attn, q_lin, k_lin)
+        qn = qn.unflatten(2, (H_r, -1)).transpose(1, 2)
+        kn = kn.unflatten(2, (H_r, -1)).transpose(1, 2)
+        qo, ko = fm.apply_fast_rotary_qk(qn, kn, freqs)
+    pin_inputs(g, "qkrope", q=(q_lin, 71), k=(k_lin, 72))
+    g["qkrope/w_q"] = bits(w_q)
+    g["qkrope/w_k"] = bits(w_k)
+    g["qkrope/eps"] = np.array(1e-6)
+    g["qkrope/heads"] = np.array(H_r)
+    g["qkrope/cos"] = freqs.real[0, 0].numpy().astype(np.float32)
+    g["qkrope/sin"] = freqs.imag[0, 0].numpy().astype(np.float32)
+    g["qkrope/q_out"] = bits(qo.contiguous())
+    g["qkrope/k_out"] = bits(ko.contiguous())
+
     # ---- coverage masks (sparse_attention.py:268-376) ---------------------
     def softmax_scores(H, nq, nk, seed, temp):
         gen = torch.Generator().manual_seed(seed)

@@ -128,7 +128,9 @@ def test_misc_validation(lib):
     from sinkattn_b200 import _lib
 
     assert lib.sa_score_accumulate(None, 4, 16, 16, 1, None) == _lib.SA_EINVAL
-    assert lib.sa_score_finalize(16, None, None, 0.0, 4, 16, None, None) == _lib.SA_EINVAL
+    assert lib.sa_score_finalize(16, None, None, 0.0, 4, 16, None, 0, None) == _lib.SA_EINVAL
+    assert lib.sa_score_finalize_presence(16, 16, None, 4, 16, None, 0, None) == _lib.SA_EINVAL
+    assert lib.sa_score_accumulate_aligned(16, 2, 5, 4, 2, 6, 16, 16, 16, 1, None) == _lib.SA_EINVAL
     st = _i64(8 * 8, 8 * 8, 8, 1)
     assert lib.sa_mean_pool_seq(16, st, 1, 1, 8, 12, 2, 0, 16, st, None) == _lib.SA_EINVAL
 
@@ -168,6 +170,7 @@ def test_install_binds_dropins_into_reference(monkeypatch):
     from sinkattn_b200 import reference_api as ra
 
     orig_forward = wan.WanSinkSparseInnerAttention.forward
+    orig_prepare = wan._prepare_attention_tensors
     orig = {n: getattr(sa, n) for n in ("block_sparse_attn_func", "_block_sparse_attn",
                                         "_compute_pooled_qk_block_scores",
                                         "_build_direct_mean_coverage_mask")}
@@ -184,7 +187,33 @@ def test_install_binds_dropins_into_reference(monkeypatch):
         x = torch.zeros(1, 2, 256, 128, dtype=torch.bfloat16)
         with pytest.raises(RuntimeError, match="CUDA"):
             inner(x, x, x)
+        # the fused Q/K producer is bound, and hands CPU inputs to the
+        # reference's own _prepare_attention_tensors unchanged
+        assert wan._prepare_attention_tensors is ra.fused_prepare_attention_tensors
+        assert ra._UNFUSED_PREPARE[0] is orig_prepare
+
+        class Attn(torch.nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.heads = 2
+                self.add_k_proj = None
+                self.to_q = torch.nn.Linear(256, 256, dtype=torch.bfloat16)
+                self.to_k = torch.nn.Linear(256, 256, dtype=torch.bfloat16)
+                self.to_v = torch.nn.Linear(256, 256, dtype=torch.bfloat16)
+                self.norm_q = torch.nn.RMSNorm(256, eps=1e-6, dtype=torch.bfloat16)
+                self.norm_k = torch.nn.RMSNorm(256, eps=1e-6, dtype=torch.bfloat16)
+
+        attn = Attn()
+        hs = torch.randn(1, 8, 256).bfloat16()
+        ang = torch.outer(torch.arange(8.0), torch.linspace(0.0, 1.0, 64))
+        freqs = torch.polar(torch.ones_like(ang), ang)[None, None]
+        with torch.no_grad():
+            got = wan._prepare_attention_tensors(attn, hs, None, freqs)
+            want = orig_prepare(attn, hs, None, freqs)
+        for a, b in zip(got[:3], want[:3]):
+            assert torch.equal(a, b)
     finally:
+        wan._prepare_attention_tensors = orig_prepare
         wan.WanSinkSparseInnerAttention.forward = orig_forward
         for n, f in orig.items():
             setattr(sa, n, f)

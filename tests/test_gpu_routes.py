@@ -95,3 +95,87 @@ def test_zimage_cfg4_attention_rows_vs_oracle(oracle):
         err = np.abs(out[:, h:h + 1, rows].float().cpu().numpy() - ref)
         assert err.max() <= 2e-2 and err.mean() / np.abs(ref).mean() <= 1e-2
         np.testing.assert_allclose(lse[0, h, rows].cpu().numpy(), ref_lse[0, 0], atol=2e-3)
+
+
+@pytest.mark.parametrize("pooling_mode", ["mean", "triton"])
+def test_device_zimage_calibrator_alignment(tmp_path, oracle, pooling_mode):
+    """Z-Image calibration with samples of different text lengths: the device
+    alignment, presence-weighted statistics and masks equal the reference's
+    CPU arithmetic (zimg/runtime/sink_sparse_zimage.py:140-186, 262-354),
+    restated here on the scores the device computed."""
+    from dataclasses import dataclass
+
+    from sinkattn_b200 import reference_api as ra
+    from sinkattn_b200.calibrator import DeviceZImageSinkMaskCalibrator
+
+    @dataclass
+    class ZCfg:
+        block_size: int = 128
+        pooling_mode: str = "mean"
+        offline_direct_coverage: float = 0.85
+        offline_text_video_coverage_mode: str = "joint"
+        force_text_global_attention: bool = True
+        text_length: int = 300
+        keep_diagonal: bool = True
+        token_width: int = 32
+        token_height: int = 32
+        token_depth: int = 1
+
+    cfg = ZCfg(pooling_mode=pooling_mode)
+    cal = DeviceZImageSinkMaskCalibrator(cfg)
+    assert (cal.image_blocks, cal.total_blocks, cal.max_text_tokens) == (8, 11, 320)
+    g = torch.Generator().manual_seed(5)
+    H, T, IB = 3, 11, 8
+    ref = {}
+    for step, text in enumerate([300, 100, 0, 250]):
+        for layer in (0, 1):
+            S = 1024 + text
+            q = torch.randn(1, H, S, 128, generator=g).bfloat16().cuda()
+            k = torch.randn(1, H, S, 128, generator=g).bfloat16().cuda()
+            cal.record(layer, q, k, k, text_token_count=text)
+            # the reference's record on the same device scores
+            sc = ra._compute_block_scores(q, k, k, cfg).float().mean(dim=0).cpu()
+            tb = -(-text // 128)
+            aligned = torch.zeros(H, T, T)
+            aligned[:, :IB, :IB] = sc[:, :IB, :IB]
+            pres = torch.zeros(H, T, T)
+            pres[:, :IB, :IB] = 1.0
+            if tb > 0:
+                t0 = T - tb
+                aligned[:, :IB, t0:] = sc[:, :IB, IB:]
+                aligned[:, t0:, :IB] = sc[:, IB:, :IB]
+                aligned[:, t0:, t0:] = sc[:, IB:, IB:]
+                pres[:, :IB, t0:] = 1.0
+                pres[:, t0:, :IB] = 1.0
+                pres[:, t0:, t0:] = 1.0
+            if layer not in ref:
+                ref[layer] = [aligned, aligned.square(), pres]
+            else:
+                ref[layer][0] += aligned
+                ref[layer][1] += aligned.square()
+                ref[layer][2] += pres
+    assert cal.current_step == 3 and cal.score_counts == {0: 4, 1: 4}
+    pkg = cal.save(str(tmp_path / "z.pt"))
+    loaded = torch.load(tmp_path / "z.pt", map_location="cpu", weights_only=True)
+    assert loaded["meta"]["route"] == "zimg_static_only" and loaded["meta"]["total_blocks"] == 11
+    for layer in (0, 1):
+        s, sq, pres = ref[layer]
+        pres = pres.clamp_min_(1.0)
+        mean = s / pres
+        std = torch.sqrt((sq / pres - mean.square()).clamp_min_(0.0))
+        assert torch.equal(pkg["mean_scores"][str(layer)], mean)
+        assert torch.equal(pkg["std_scores"][str(layer)], std)
+        assert torch.equal(cal.score_presence_sums[layer].cpu(), pres)
+        # the reference's required text blocks are the first ceil(text_length / 128)
+        # rows and columns (sparse_attention.py:250-261); fp32 sums as it takes them
+        req = torch.zeros(T, T)
+        req[:, :3] = 1.0
+        req[:3, :] = 1.0
+        res = oracle.coverage_mask(mean.numpy(), row_total=mean.sum(-1).numpy(),
+                                   row_selected=(mean * req).sum(-1).numpy(),
+                                   text_blocks=3, mode="joint", keep_diagonal=True)
+        np.testing.assert_array_equal(loaded["sink_masks"][str(layer)].numpy(), res.mask)
+    with pytest.raises(ValueError):
+        cal.record(0, q, k, k, text_token_count=400)
+    with pytest.raises(ValueError):
+        cal.record(0, q.expand(2, -1, -1, -1), k.expand(2, -1, -1, -1), k, text_token_count=250)

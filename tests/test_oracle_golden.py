@@ -171,3 +171,17 @@ def test_triton_max_pool_restatement_properties(oracle):
     assert np.all(s >= 0) and np.all(s <= 1)
     np.testing.assert_allclose(s.sum(-1), 1.0, atol=2e-2)
     assert np.all(np.argmax(s[0, 0], axis=1) == np.arange(4))
+
+
+def test_qk_norm_rope_matches_reference(golden, oracle):
+    """RMSNorm + rotary through the reference's own helpers (torch RMSNorm,
+    fp64 complex rotary): the oracle equals them bit for bit here."""
+    heads = int(golden["qkrope/heads"])
+    for t in ("q", "k"):
+        x = regen_input(golden, "qkrope", t).float().numpy()
+        w = from_bits(golden[f"qkrope/w_{t}"])
+        got = oracle.qk_norm_rope(x, w, float(golden["qkrope/eps"]), golden["qkrope/cos"],
+                                  golden["qkrope/sin"], heads)
+        want = from_bits(golden[f"qkrope/{t}_out"])
+        d = oracle.bf16_ulp_distance(got, want)
+        assert d.max() == 0, (d.max(), (d == 0).mean())
