@@ -7,23 +7,32 @@
 // (sinkattention/sparse_attention.py:735-771): 128x128 blocks, no dropout,
 // not causal, scale 1/sqrt(D) by default.
 //
-// Kernel structure (one CTA per SM, 640 threads):
-//   warp 0       TMA producer: Q tiles once, then K/V tiles into a 4-slot ring
-//   warp 1       MMA issuer (one thread): S = Q K^T (SS), O += P V (TS)
-//   warp 2       TMEM allocator + kept-block list of slot 0
-//   warp 3       kept-block list of slot 1
-//   warps 4-11   softmax of slot 0: two warpgroups, one per 64-column half
-//   warps 12-19  softmax of slot 1 (thread pair per query row)
-// A CTA carries two query tiles ("slots") that ping-pong: while one slot's
-// softmax runs on the CUDA cores, the tensor core works on the other slot.
+// Kernel structure (one CTA per query tile, 384 threads):
+//   warp 0       TMA producer: K/V tiles into a 6-slot ring
+//   warp 1       QK issuer (one thread): S = Q K^T
+//   warp 2       TMEM allocator + the tile's kept-block list
+//   warp 3       PV issuer (one thread): O[h] += P[h] V
+//   warps 4-7    softmax stream 0: keys 0-63 of every kept block
+//   warps 8-11   softmax stream 1: keys 64-127 of every kept block
+// Each kept 128-key block is split into two 64-key halves. Stream h owns half
+// h of every block with its own running maximum, row sum and O accumulator,
+// so a stream's thread holds one query row and needs no exchange with the
+// other stream until the end, where the two (max, sum, O) are merged.
 //
-// TMEM (512 columns x 128 lanes, fp32): S0 [0,128) S1 [128,256)
-// O0 [256,384) O1 [384,512). P (bf16 pairs) overwrites the first 64 columns
-// of its slot's S and is the A operand of the PV MMA straight from TMEM.
+// Q lives in TMEM (the softmax threads write it there once), so S = Q K^T is
+// a TS MMA that reads only K from shared memory, and shared memory holds
+// nothing but the K/V ring: per block the tensor core reads 64 KB of it and
+// TMA writes 64 KB. P has its own TMEM columns, and QK and PV come from two
+// issuing threads, so QK of block j+1 is issued as soon as both streams have
+// copied S of block j to registers (whatever PV is waiting for), and the next
+// S is computed while the softmax still works on the current one.
 //
-// Shared memory: Q0, Q1 (32 KB each) and a ring of 4 x 32 KB K/V tiles, all
-// in the 128-byte-swizzled layout TMA writes and UMMA reads (two 64-column
-// boxes per 128x128 tile).
+// TMEM (512 columns x 128 lanes, 32-bit):
+//   S [0,128) (stream h: columns 64h..64h+63)   P[h] [128+32h, 160+32h)
+//   Q [192,256) (bf16 pairs)   O[0] [256,384)   O[1] [384,512)
+//
+// Shared memory: a ring of 6 x 32 KB K/V tiles in the 128-byte-swizzled
+// layout TMA writes and UMMA reads (two 64-column boxes per 128x128 tile).
 //
 // Online softmax uses base-2 exponentials with a lazily updated row maximum:
 // the running maximum is only raised (and O, l rescaled) when a block's
@@ -39,13 +48,17 @@ namespace attn {
 
 constexpr int kBM = 128;      // query rows per tile
 constexpr int kBN = 128;      // keys per block
+constexpr int kHalf = 64;     // keys per stream per block
 constexpr int kHD = 128;      // head dim
-constexpr int kStages = 4;    // K/V ring slots
-constexpr int kThreads = 640;  // 4 role warps + 4 softmax warpgroups
+constexpr int kStages = 6;    // K/V ring slots
+constexpr int kThreads = 384;  // 4 role warps + 2 softmax warpgroups
 constexpr int kTileBytes = kBM * kHD * 2;   // 32 KB bf16 tile
 constexpr int kBoxBytes = kTileBytes / 2;   // one 64-column box
+constexpr int kHalfRowsBytes = kHalf * 128; // 64 rows of a box: 8 KB
 constexpr int kMaxBlocks = 1024;            // max key blocks per row (S <= 131072)
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+// TMEM columns
+constexpr uint32_t kColS = 0, kColP = 128, kColQ = 192, kColO = 256;
 
 struct Params {
   int B, H, Sq, Sk, nq, nk;
@@ -55,6 +68,8 @@ struct Params {
   int64_t ms0, ms1, ms2, ms3;
   const int32_t* head_mask_type;
   float scale_log2;  // softmax_scale * log2(e)
+  const __nv_bfloat16* q;
+  int64_t qs0, qs1, qs2;
   __nv_bfloat16* out;
   int64_t os0, os1, os2;
   float* lse;
@@ -62,88 +77,77 @@ struct Params {
 };
 
 struct __align__(8) SmemCtl {
-  uint64_t q_full[2];
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t q_ready;      // Q written to TMEM, 256 arrivals
+  uint64_t s_full;       // S of block j computed (commit)
+  uint64_t s_free;       // S of block j copied out by both streams, 256 arrivals
+  uint64_t p_full[2];    // [stream], 128 arrivals per phase
+  uint64_t pv_done[2];   // [stream], committed after each PV
   uint64_t o_final[2];
-  uint64_t xbar[2];
-  uint64_t mma_drain;
+  uint64_t xbar;         // final (max, sum) exchange, 256 arrivals
+  uint64_t mma_drain[2];  // [0] QK issuer, [1] PV issuer
   uint32_t tmem_base;
   int abort_flag;
-  int n_blocks[2];
-  int q_tile[2];
-  uint16_t list[2][kMaxBlocks];  // key blocks; bit 15 marks a pooled-key block
-  float xchg[2][2][kBM];  // partial row maxima (slot, half, row)
-  float xsum[2][2][kBM];  // partial row sums at the end
+  int n_blocks;
+  uint16_t list[kMaxBlocks];  // key blocks; bit 15 marks a pooled-key block
+  float xm[2][kBM];
+  float xl[2][kBM];
 };
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
-                              sizeof(SmemCtl);
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kTileBytes + sizeof(SmemCtl);
 
-// The deterministic order in which K/V tiles are produced and consumed:
-//   K(0,0) K(1,0) then for every j: V(0,j) K(0,j+1) V(1,j) K(1,j+1)
-// (entries whose block index is past the slot's count are skipped).
-struct SeqItem {
-  int slot, j, is_v;
-};
-
+// The order in which K/V tiles are produced and consumed:
+//   K(0), then for every j: K(j+1) (if any), V(j)
+// so QK of block j+1 is issued before PV of block j.
 template <typename F>
-__device__ __forceinline__ void for_each_item(const int n0, const int n1, F&& f) {
-  const int n[2] = {n0, n1};
-  if (n[0] > 0 && !f(SeqItem{0, 0, 0})) return;
-  if (n[1] > 0 && !f(SeqItem{1, 0, 0})) return;
-  const int nmax = n0 > n1 ? n0 : n1;
-  for (int j = 0; j < nmax; ++j) {
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      if (j < n[s]) {
-        if (!f(SeqItem{s, j, 1})) return;
-        if (j + 1 < n[s])
-          if (!f(SeqItem{s, j + 1, 0})) return;
-      }
-    }
+__device__ __forceinline__ void for_each_item(const int n, F&& f) {
+  if (n <= 0) return;
+  if (!f(0, 0)) return;
+  for (int j = 0; j < n; ++j) {
+    if (j + 1 < n && !f(j + 1, 0)) return;
+    if (!f(j, 1)) return;
   }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    bsattn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
-                      const __grid_constant__ CUtensorMap tm_k,
+    bsattn_fwd_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_k2,
                       const __grid_constant__ CUtensorMap tm_v2, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* q_smem = smem;                      // 2 tiles
-  uint8_t* ring = smem + 2 * kTileBytes;       // kStages tiles
+  uint8_t* ring = smem;
   SmemCtl* ctl = reinterpret_cast<SmemCtl*>(ring + kStages * kTileBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.z;
+  const int qt = blockIdx.x;
   const int h = blockIdx.y;
+  const int b = blockIdx.z;
 
-  // ---- set-up: barriers, TMEM, kept-block lists ---------------------------
+  // ---- set-up: barriers, TMEM, kept-block list ----------------------------
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&ctl->q_full[s], 1);
-      mbar_init(&ctl->s_full[s], 1);
-      mbar_init(&ctl->p_full[s], 2 * kBM);
-      mbar_init(&ctl->xbar[s], 2 * kBM);
-      mbar_init(&ctl->o_final[s], 1);
-    }
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&ctl->kv_full[i], 1);
       mbar_init(&ctl->kv_empty[i], 1);
     }
-    mbar_init(&ctl->mma_drain, 1);
+    mbar_init(&ctl->q_ready, 2 * kBM);
+    mbar_init(&ctl->s_full, 1);
+    mbar_init(&ctl->s_free, 2 * kBM);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(&ctl->p_full[st], kBM);
+      mbar_init(&ctl->pv_done[st], 1);
+      mbar_init(&ctl->o_final[st], 1);
+    }
+    mbar_init(&ctl->xbar, 2 * kBM);
+    mbar_init(&ctl->mma_drain[0], 1);
+    mbar_init(&ctl->mma_drain[1], 1);
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
     if (p.nk2 > 0) {
@@ -154,70 +158,47 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) {
     tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
-  }
-  if (warp == 2 || warp == 3) {
-    const int s = warp - 2;
-    const int qt = blockIdx.x * 2 + s;
+    int mh = h;
+    bool dense = false;
+    if (p.head_mask_type != nullptr) {
+      const int t = p.head_mask_type[h];
+      if (t > 0) mh = t - 1; else dense = true;
+    }
+    const uint8_t* row = p.mask + (int64_t)b * p.ms0 + (int64_t)mh * p.ms1 + (int64_t)qt * p.ms2;
     int count = 0;
-    if (qt < p.nq) {
-      int mh = h;
-      bool dense = false;
-      if (p.head_mask_type != nullptr) {
-        const int t = p.head_mask_type[h];
-        if (t > 0) mh = t - 1; else dense = true;
-      }
-      const uint8_t* row = p.mask + (int64_t)b * p.ms0 + (int64_t)mh * p.ms1 + (int64_t)qt * p.ms2;
-      for (int c0 = 0; c0 < p.nk; c0 += 32) {
-        const int c = c0 + lane;
-        const bool keep = c < p.nk && (dense || row[(int64_t)c * p.ms3] != 0);
-        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-        if (keep) ctl->list[s][count + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)c;
-        count += __popc(bal);
-      }
-      // the dynamic branch: every pooled-key block, after the kept sink blocks
-      for (int t = lane; t < p.nk2; t += 32) ctl->list[s][count + t] = (uint16_t)(0x8000u | t);
-      count += p.nk2;
+    for (int c0 = 0; c0 < p.nk; c0 += 32) {
+      const int c = c0 + lane;
+      const bool keep = c < p.nk && (dense || row[(int64_t)c * p.ms3] != 0);
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+      if (keep) ctl->list[count + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)c;
+      count += __popc(bal);
     }
-    if (lane == 0) {
-      ctl->n_blocks[s] = count;
-      ctl->q_tile[s] = qt;
-    }
+    // the dynamic branch: every pooled-key block, after the kept sink blocks
+    for (int t = lane; t < p.nk2; t += 32) ctl->list[count + t] = (uint16_t)(0x8000u | t);
+    count += p.nk2;
+    if (lane == 0) ctl->n_blocks = count;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
   const uint32_t tmem = ctl->tmem_base;
-  const int n0 = ctl->n_blocks[0];
-  const int n1 = ctl->n_blocks[1];
+  const int n = ctl->n_blocks;
   volatile int* abort_flag = &ctl->abort_flag;
 
-  // Register split (warpgroup-wide, issued inside each role's branch so the
-  // compiler budgets every role separately): the role warps drop to 56
-  // registers and the softmax warpgroups rise to 104.
-  // 128*56 + 512*104 = 60416 <= 640*96, the registers the block launches with.
   if (warp == 0) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      for (int s = 0; s < 2; ++s) {
-        if (ctl->n_blocks[s] == 0) continue;
-        uint8_t* dst = q_smem + s * kTileBytes;
-        mbar_arrive_expect_tx(&ctl->q_full[s], kTileBytes);
-        const int row0 = ctl->q_tile[s] * kBM;
-        tma_load_4d(&tm_q, &ctl->q_full[s], dst, 0, row0, h, b);
-        tma_load_4d(&tm_q, &ctl->q_full[s], dst + kBoxBytes, 64, row0, h, b);
-      }
+    if (lane == 0 && n > 0) {
       int it = 0;
-      for_each_item(n0, n1, [&](const SeqItem& item) -> bool {
+      for_each_item(n, [&](const int j, const int is_v) -> bool {
         const int stage = it % kStages;
         const uint32_t phase = (uint32_t)(it / kStages) & 1u;
         if (!mbar_wait(&ctl->kv_empty[stage], phase ^ 1u, p.status, abort_flag)) return false;
         uint8_t* dst = ring + stage * kTileBytes;
-        const uint32_t ent = ctl->list[item.slot][item.j];
+        const uint32_t ent = ctl->list[j];
         const int kb = (int)(ent & 0x7fffu);
         const bool pooled = (ent & 0x8000u) != 0;
-        const CUtensorMap* map = item.is_v ? (pooled ? &tm_v2 : &tm_v) : (pooled ? &tm_k2 : &tm_k);
+        const CUtensorMap* map = is_v ? (pooled ? &tm_v2 : &tm_v) : (pooled ? &tm_k2 : &tm_k);
         mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
         tma_load_4d(map, &ctl->kv_full[stage], dst, 0, kb * kBN, h, b);
         tma_load_4d(map, &ctl->kv_full[stage], dst + kBoxBytes, 64, kb * kBN, h, b);
@@ -229,119 +210,138 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_drain(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+  } else if (warp == 1 || warp == 3) {
+    // ---------------- MMA issuers: warp 1 QK, warp 3 PV ----------------
+    // Both walk the K/V sequence to find the ring stage of each item and
+    // take only their own kind (K tiles for QK, V tiles for PV).
+    const int role_v = warp == 3 ? 1 : 0;
+    if (lane == 0 && n > 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_bf16(kBM, kHD, 0, 1);
-      bool ok = true;
-      for (int s = 0; s < 2 && ok; ++s)
-        if (ctl->n_blocks[s] > 0) ok = mbar_wait(&ctl->q_full[s], 0, p.status, abort_flag);
+      const bool ok = mbar_wait(&ctl->q_ready, 0, p.status, abort_flag);
       tc_fence_after();
-      const uint32_t q_base = smem_u32(q_smem);
       const uint32_t ring_base = smem_u32(ring);
       int it = 0;
       if (ok) {
-        for_each_item(n0, n1, [&](const SeqItem& item) -> bool {
+        for_each_item(n, [&](const int j, const int is_v) -> bool {
+          if (is_v != role_v) {
+            ++it;
+            return true;
+          }
           const int stage = it % kStages;
           const uint32_t phase = (uint32_t)(it / kStages) & 1u;
+          if (!is_v && j > 0) {
+            // S is single-buffered: both streams have copied S(j-1) out
+            if (!mbar_wait(&ctl->s_free, (uint32_t)(j - 1) & 1u, p.status, abort_flag))
+              return false;
+          }
           if (!mbar_wait(&ctl->kv_full[stage], phase, p.status, abort_flag)) return false;
           const uint32_t tile = ring_base + stage * kTileBytes;
-          const int s = item.slot;
-          if (!item.is_v) {
+          if (!is_v) {
             tc_fence_after();
-            const uint32_t qa = q_base + s * kTileBytes;
-            const uint32_t d = tmem + s * 128;
+            // S = Q (TMEM) . K^T (shared memory), all 128 keys of the block
 #pragma unroll
             for (int kk = 0; kk < kHD / 16; ++kk) {
               const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-              const uint64_t ad = make_sdesc_sw128(qa + off, 16, 1024);
-              const uint64_t bd = make_sdesc_sw128(tile + off, 16, 1024);
-              mma_ss(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+              mma_ts(tmem + kColS, tmem + kColQ + kk * 8, make_sdesc_sw128(tile + off, 16, 1024),
+                     idesc_qk, kk > 0 ? 1u : 0u);
             }
+            mma_commit(&ctl->s_full);
             mma_commit(&ctl->kv_empty[stage]);
-            mma_commit(&ctl->s_full[s]);
           } else {
-            if (!mbar_wait(&ctl->p_full[s], (uint32_t)item.j & 1u, p.status, abort_flag))
-              return false;
-            tc_fence_after();
-            const uint32_t d = tmem + 256 + s * 128;
-            const uint32_t pa = tmem + s * 128;
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              const uint64_t bd = make_sdesc_sw128(tile + kk * 2048, kBoxBytes, 1024);
-              mma_ts(d, pa + kk * 8, bd, idesc_pv, (item.j > 0 || kk > 0) ? 1u : 0u);
+            for (int st = 0; st < 2; ++st) {
+              if (!mbar_wait(&ctl->p_full[st], (uint32_t)j & 1u, p.status, abort_flag))
+                return false;
+              tc_fence_after();
+              // O[st] += P[st] (128 x 64, bf16 in TMEM) . V[keys 64st .. 64st+63]
+#pragma unroll
+              for (int kk = 0; kk < kHalf / 16; ++kk) {
+                const uint64_t bd =
+                    make_sdesc_sw128(tile + st * kHalfRowsBytes + kk * 2048, kBoxBytes, 1024);
+                mma_ts(tmem + kColO + st * 128, tmem + kColP + st * 32 + kk * 8, bd, idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+              }
+              mma_commit(&ctl->pv_done[st]);
+              if (j == n - 1) mma_commit(&ctl->o_final[st]);
             }
             mma_commit(&ctl->kv_empty[stage]);
-            if (item.j == ctl->n_blocks[s] - 1) mma_commit(&ctl->o_final[s]);
           }
           ++it;
           return true;
         });
       }
       // Drain every MMA this thread issued before TMEM can be released.
-      mma_commit(&ctl->mma_drain);
-      mbar_wait_drain(&ctl->mma_drain, 0);
+      mma_commit(&ctl->mma_drain[role_v]);
+      mbar_wait_drain(&ctl->mma_drain[role_v], 0);
     }
     __syncwarp();
-  } else if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
-    // ---------------- softmax warpgroups ----------------
-    // Four warpgroups: slot s = g >> 1 and column half hh = g & 1. Thread
-    // (warp quarter wq, lane) owns query row wq*32+lane and 64 of its 128
-    // key columns; the two halves of a row exchange their partial maxima
-    // (and, at the end, partial sums) through shared memory behind the
-    // slot's `xbar` mbarrier (256 arrivals per phase, bounded waits).
-    const int g = (warp - 4) >> 2;
-    const int s = g >> 1;
-    const int hh = g & 1;
-    const int wq = warp & 3;                  // TMEM lane quarter of this warp
-    const int row = wq * 32 + lane;           // query row within the tile
-    const int n = ctl->n_blocks[s];
-    const int qt = ctl->q_tile[s];
-    const int grow = qt * kBM + row;          // global query row
+  } else if (warp >= 4) {
+    // ---------------- softmax streams ----------------
+    // Stream st = 0/1 (warps 4-7 / 8-11) owns keys 64st..64st+63 of every
+    // kept block. Thread (warp quarter wq, lane) owns query row wq*32+lane,
+    // which is TMEM lane wq*32+lane.
+    const int st = (warp - 4) >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int grow = qt * kBM + row;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + s * 128 + hh * 64;  // 64 fp32 S columns
-    const uint32_t p_addr = tmem + lane_off + s * 128 + hh * 32;  // 32 packed bf16x2 P columns
-    const uint32_t o_addr = tmem + lane_off + 256 + s * 128 + hh * 64;
-    volatile float* x_own = ctl->xchg[s][hh];
-    volatile float* x_oth = ctl->xchg[s][hh ^ 1];
+    bool ok = true;
+    if (n > 0) {
+      // Q row -> TMEM: stream st writes head dims 64st..64st+63 (32 columns of
+      // bf16 pairs, the A-operand layout of the QK MMA). Rows past Sq are 0.
+      uint32_t qv[32];
+      if (grow < p.Sq) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2 + st * 64);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const uint4 w = src[v];
+          qv[4 * v] = w.x; qv[4 * v + 1] = w.y; qv[4 * v + 2] = w.z; qv[4 * v + 3] = w.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) qv[e] = 0u;
+      }
+      tmem_st32(tmem + lane_off + kColQ + st * 32, qv);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&ctl->q_ready);
+    }
     float m_used = -INFINITY;
     float l = 0.f;
-    bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
       // warp-uniform outcome: the TMEM loads below are warp-collective
       if (!__all_sync(0xffffffffu,
-                      mbar_wait(&ctl->s_full[s], (uint32_t)j & 1u, p.status, abort_flag))) {
+                      mbar_wait(&ctl->s_full, (uint32_t)j & 1u, p.status, abort_flag))) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t r[2][32];
-      tmem_ld32(s_addr + 0, r[0]);
-      tmem_ld32(s_addr + 32, r[1]);
+      tmem_ld32(tmem + lane_off + kColS + st * kHalf + 0, r[0]);
+      tmem_ld32(tmem + lane_off + kColS + st * kHalf + 32, r[1]);
       tmem_wait_ld();
       reg_fence32(r[0]);
       reg_fence32(r[1]);
-      const uint32_t ent = ctl->list[s][j];
+      tc_fence_before();
+      mbar_arrive(&ctl->s_free);  // S may be overwritten by the next QK
+      const uint32_t ent = ctl->list[j];
       const int kb = (int)(ent & 0x7fffu);
       const bool pooled = (ent & 0x8000u) != 0;
-      const int valid = min(kBN, (pooled ? p.Sk2 : p.Sk) - kb * kBN) - hh * 64;  // valid columns here
+      const int valid = min(kHalf, (pooled ? p.Sk2 : p.Sk) - kb * kBN - st * kHalf);
       const float bias = pooled ? p.bias_log2 : 0.f;
-      if (valid < 64) {
+      if (valid < kHalf) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
+        for (int c = 0; c < kHalf; ++c)
           if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      // Partial row maximum over 64 columns: 8 chains of 3-input max.
+      // Row maximum over this stream's 64 columns: 8 chains of 3-input max.
       float mxp[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) mxp[t] = __uint_as_float(r[0][t]);
 #pragma unroll
-      for (int c = 8; c + 16 <= 64; c += 16) {
+      for (int c = 8; c + 16 <= kHalf; c += 16) {
 #pragma unroll
         for (int t = 0; t < 8; ++t)
           mxp[t] = fmax3(mxp[t], __uint_as_float(r[(c + t) >> 5][(c + t) & 31]),
@@ -349,18 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int t = 0; t < 8; ++t) mxp[t] = fmaxf(mxp[t], __uint_as_float(r[1][24 + t]));
-      const float mx_half = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
-                                  fmaxf(mxp[6], mxp[7]));
-      // Exchange with the other half of the row. Both halves have finished
-      // reading S when the phase completes, so P may overwrite it afterwards.
-      x_own[row] = mx_half;
-      mbar_arrive(&ctl->xbar[s]);
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait(&ctl->xbar[s], (uint32_t)j & 1u, p.status, abort_flag))) {
-        ok = false;
-        break;
-      }
-      const float mx = fmaf(fmaxf(mx_half, x_oth[row]), p.scale_log2, bias);
+      const float mx_raw = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                                 fmaxf(mxp[6], mxp[7]));
+      const float mx = fmaf(mx_raw, p.scale_log2, bias);  // -inf stays -inf
       float alpha = 1.0f;
       const bool rescale = mx > m_used + kRescaleThreshold;
       if (rescale) {
@@ -368,10 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
         m_used = mx;
       }
-      // P = exp2(S*scale*log2e - m): packed f32x2 FMA for the argument, MUFU
-      // ex2 per lane, packed f32x2 adds for 4 independent partial sums.
+      // P = exp2(S*scale*log2e + bias - m); a row that has seen no valid key
+      // yet (m = -inf) gets P = 0 from its -inf inputs.
+      const float negm = m_used == -INFINITY ? 0.f : -m_used;
       const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
-      const uint64_t negm2 = f2_pack(bias - m_used, bias - m_used);
+      const uint64_t negm2 = f2_pack(bias + negm, bias + negm);
       uint64_t lp2[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t pk[32];
 #pragma unroll
@@ -387,77 +379,100 @@ __global__ void __launch_bounds__(kThreads, 1)
         lp2[e & 3] = f2_add(lp2[e & 3], f2_pack(p0, p1));
         pk[e] = pack_bf16x2(p0, p1);
       }
-      tmem_st32(p_addr, pk);
       {
         const uint64_t t2 = f2_add(f2_add(lp2[0], lp2[1]), f2_add(lp2[2], lp2[3]));
         float a0, a1;
         f2_unpack(t2, a0, a1);
         l += a0 + a1;
       }
-      // O was complete for blocks < j when s_full(j) fired; PV(j) waits for p_full.
-      // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
-      // takes this branch when any of its rows rescales; other rows use
-      // alpha = 1.
+      // P[st] and O[st] are free once PV of block j-1 has completed.
+      if (j > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&ctl->pv_done[st], (uint32_t)(j - 1) & 1u,
+                                               p.status, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      tmem_st32(tmem + lane_off + kColP + st * 32, pk);
+      // Rescale O when the maximum moved after the first block. tcgen05.ld/st
+      // are warp-collective (.sync.aligned): the whole warp takes this branch
+      // when any of its rows rescales; other rows use alpha = 1.
       if (__any_sync(0xffffffffu, rescale && j > 0)) {
         if (!(rescale && j > 0)) alpha = 1.0f;
+        const uint32_t o_self = tmem + lane_off + kColO + st * 128;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32(o_addr + c * 32, o);
+          tmem_ld32(o_self + c * 32, o);
           tmem_wait_ld();
           reg_fence32(o);
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(o_addr + c * 32, o);
+          tmem_st32(o_self + c * 32, o);
         }
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&ctl->p_full[s]);
+      mbar_arrive(&ctl->p_full[st]);
     }
-    // Epilogue: combine the two halves' sums, O / l -> bf16, natural-log LSE.
-    float l_row = l;
+    // Epilogue: merge the two streams' (max, sum, O) for each row; stream st
+    // writes output columns 64st..64st+63, stream 0 the LSE.
+    if (ok && n > 0) ok = mbar_wait(&ctl->o_final[st], 0, p.status, abort_flag);
+    float m_oth = -INFINITY, l_oth = 0.f;
     if (ok && n > 0) {
-      ctl->xsum[s][hh][row] = l;
-      mbar_arrive(&ctl->xbar[s]);
-      ok = mbar_wait(&ctl->xbar[s], (uint32_t)n & 1u, p.status, abort_flag);
-      if (ok) l_row = l + ctl->xsum[s][hh ^ 1][row];
+      ctl->xm[st][row] = m_used;
+      ctl->xl[st][row] = l;
+      mbar_arrive(&ctl->xbar);
+      ok = mbar_wait(&ctl->xbar, 0, p.status, abort_flag);
+      if (ok) {
+        m_oth = ctl->xm[st ^ 1][row];
+        l_oth = ctl->xl[st ^ 1][row];
+      }
     }
-    if (ok && n > 0) ok = mbar_wait(&ctl->o_final[s], 0, p.status, abort_flag);
     ok = __all_sync(0xffffffffu, ok);  // the O loads below are warp-collective
     tc_fence_after();
-    if (qt < p.nq) {
-      const bool write = grow < p.Sq;
-      __nv_bfloat16* orow = p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 +
-                            (int64_t)grow * p.os2 + hh * 64;
-      if (n > 0 && ok) {
-        const float inv_l = 1.0f / l_row;
+    const bool write = grow < p.Sq;
+    __nv_bfloat16* orow = p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 +
+                          (int64_t)grow * p.os2 + st * kHalf;
+    if (n > 0 && ok) {
+      const float m = fmaxf(m_used, m_oth);
+      const float a_self = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m);
+      const float a_oth = m_oth == -INFINITY ? 0.f : ex2_approx(m_oth - m);
+      const float L = l * a_self + l_oth * a_oth;
+      const float inv_l = 1.0f / L;
+      const float w0 = (st == 0 ? a_self : a_oth) * inv_l;  // weight of O[0]
+      const float w1 = (st == 0 ? a_oth : a_self) * inv_l;  // weight of O[1]
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c * 32, o);
-          tmem_wait_ld();
-          reg_fence32(o);
-          if (write) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o0[32], o1[32];
+        tmem_ld32(tmem + lane_off + kColO + st * kHalf + c * 32, o0);
+        tmem_ld32(tmem + lane_off + kColO + 128 + st * kHalf + c * 32, o1);
+        tmem_wait_ld();
+        reg_fence32(o0);
+        reg_fence32(o1);
+        if (write) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
-              w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
-              w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
-              w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
-              dst[v] = w;
+          for (int v = 0; v < 4; ++v) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i0 = 8 * v + 2 * e;
+              w[e] = pack_bf16x2(
+                  fmaf(__uint_as_float(o0[i0]), w0, __uint_as_float(o1[i0]) * w1),
+                  fmaf(__uint_as_float(o0[i0 + 1]), w0, __uint_as_float(o1[i0 + 1]) * w1));
             }
+            dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-        if (write && hh == 0 && p.lse != nullptr)
-          p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = (m_used + __log2f(l_row)) * 0.69314718055994531f;
-      } else if (write) {
-        uint4* dst = reinterpret_cast<uint4*>(orow);
-        for (int v = 0; v < 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
-        if (hh == 0 && p.lse != nullptr) p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = -INFINITY;
       }
+      if (write && st == 0 && p.lse != nullptr)
+        p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = (m + __log2f(L)) * 0.69314718055994531f;
+    } else if (write) {
+      uint4* dst = reinterpret_cast<uint4*>(orow);
+      for (int v = 0; v < 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+      if (st == 0 && p.lse != nullptr) p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = -INFINITY;
     }
   }
 
@@ -541,9 +556,8 @@ int launch_attention(const char* fn, const void* q, const void* k, const void* v
                "%s: mask has %d heads but H=%d and no head_mask_type", fn, Hm, H);
   SA_CHECK_ARG(Hm >= 1, "%s: mask heads must be >= 1", fn);
 
-  CUtensorMap tq, tk, tv, tk2, tv2;
+  CUtensorMap tk, tv, tk2, tv2;
   int rc;
-  if ((rc = make_map_bshd(&tq, q, q_strides, B, H, Sq, D)) != SA_OK) return rc;
   if ((rc = make_map_bshd(&tk, k, k_strides, B, H, Sk, D)) != SA_OK) return rc;
   if ((rc = make_map_bshd(&tv, v, v_strides, B, H, Sk, D)) != SA_OK) return rc;
   if (dual) {
@@ -564,6 +578,8 @@ int launch_attention(const char* fn, const void* q, const void* k, const void* v
   p.head_mask_type = head_mask_type;
   const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.qs0 = q_strides[0]; p.qs1 = q_strides[1]; p.qs2 = q_strides[2];
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.os0 = o_strides[0]; p.os1 = o_strides[1]; p.os2 = o_strides[2];
   p.lse = lse;
@@ -578,8 +594,8 @@ int launch_attention(const char* fn, const void* q, const void* k, const void* v
                                      (int)kSmemBytes));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  dim3 grid((nq + 1) / 2, H, B);
-  bsattn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, tk2, tv2, p);
+  dim3 grid(nq, H, B);
+  bsattn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, tk2, tv2, p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
