@@ -163,6 +163,18 @@ SA_API int sa_pooled_softmax(const float* qp, const float* kp, int B, int H, int
                              float* logits_ws, cudaStream_t stream);
 
 /*
+ * sa_pooled_softmax over L stacked layers in two launches, for a calibration
+ * pass over many layers: qp, kp fp32 [L,B,H,nb,D] (block means), batch_means
+ * fp32 [L,H,nb,nb] (each layer's mean over its B), logits_ws fp32
+ * [L*B*H*nb*nb]. scale <= 0 means 1/sqrt(D).
+ * Replaces: the per-layer _compute_block_scores + batch mean of
+ *   SinkMaskCalibrator.record (sparse_attention.py:138-142, 575-582).
+ */
+SA_API int sa_pooled_softmax_layers(const float* qp, const float* kp, int L, int B, int H, int nb,
+                                    int D, float scale, float* batch_means, float* logits_ws,
+                                    cudaStream_t stream);
+
+/*
  * sa_pool_scores without a workspace argument. It has no counterpart in the
  * reference: it exists for callers that cannot allocate device memory when
  * they call in (a C/FFI host with no device allocator, or a server that

@@ -60,6 +60,7 @@ _SIGNATURES = {
         [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, ctypes.c_size_t, _vp],
     ),
     "sa_pool_means": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "sa_pooled_softmax_layers": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sa_pooled_softmax": (_i, [_vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),
     "sa_pool_scores_noalloc": (
         _i,

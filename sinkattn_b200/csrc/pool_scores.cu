@@ -251,18 +251,21 @@ __global__ void __launch_bounds__(256)
 
 // One warp per (h, i). For every batch b: p = exp(x - max) * (1/sum).
 // scores (nullable) [B,H,nb,nb]; batch_mean (nullable) [H,nb,nb].
-__global__ void row_softmax_kernel(const float* __restrict__ logits, int B, int H, int nb,
+// L stacked layers: logits [L,B,H,nb,nb], batch_mean [L,H,nb,nb] (per layer).
+__global__ void row_softmax_kernel(const float* __restrict__ logits, int L, int B, int H, int nb,
                                    float* __restrict__ scores, float* __restrict__ batch_mean) {
   extern __shared__ float accs[];
   const int warps = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r = (int64_t)blockIdx.x * warps + warp;  // h*nb + i
-  if (r >= (int64_t)H * nb) return;
-  const int h = (int)(r / nb), i = (int)(r % nb);
+  const int64_t r = (int64_t)blockIdx.x * warps + warp;  // (l*H + h)*nb + i
+  if (r >= (int64_t)L * H * nb) return;
+  const int l = (int)(r / ((int64_t)H * nb));
+  const int rh = (int)(r % ((int64_t)H * nb));
+  const int h = rh / nb, i = rh % nb;
   float* acc = accs + (size_t)warp * nb;
   for (int j = lane; j < nb; j += 32) acc[j] = 0.f;
   for (int b = 0; b < B; ++b) {
-    const int64_t off = (((int64_t)b * H + h) * nb + i) * nb;
+    const int64_t off = ((((int64_t)l * B + b) * H + h) * nb + i) * nb;
     const float* x = logits + off;
     float m = -INFINITY;
     for (int j = lane; j < nb; j += 32) m = fmaxf(m, x[j]);
@@ -421,7 +424,7 @@ extern "C" int sa_pool_scores(const void* q, const void* k, const int64_t q_stri
   }
   const int64_t rows = (int64_t)H * nb;
   row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
-      logits, B, H, nb, scores, batch_mean);
+      logits, 1, B, H, nb, scores, batch_mean);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
@@ -467,7 +470,41 @@ extern "C" int sa_pooled_softmax(const float* qp, const float* kp, int B, int H,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t rows = (int64_t)H * nb;
   row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
-      logits_ws, B, H, nb, scores, batch_mean);
+      logits_ws, 1, B, H, nb, scores, batch_mean);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+// Pooled softmax and per-layer batch mean of L stacked layers in two launches
+// (a calibration pass over many layers): qp, kp [L,B,H,nb,D] fp32.
+extern "C" int sa_pooled_softmax_layers(const float* qp, const float* kp, int L, int B, int H,
+                                        int nb, int D, float scale, float* batch_means,
+                                        float* logits_ws, cudaStream_t stream) {
+  using namespace sa::pool;
+  SA_CHECK_ARG(qp && kp && logits_ws && batch_means,
+               "sa_pooled_softmax_layers: null pointer argument");
+  SA_CHECK_ARG(L >= 1 && B >= 1 && H >= 1 && nb >= 1,
+               "sa_pooled_softmax_layers: L, B, H, nb must be >= 1");
+  SA_CHECK_ARG(D >= 8 && D <= 256 && D % 8 == 0,
+               "sa_pooled_softmax_layers: D must be a multiple of 8 in [8,256]");
+  SA_CHECK_ARG((int64_t)L * B * H <= 65535, "sa_pooled_softmax_layers: L*B*H too large");
+  SA_CHECK_ARG(((uintptr_t)qp | (uintptr_t)kp) % 16 == 0,
+               "sa_pooled_softmax_layers: qp/kp must be 16-byte aligned");
+  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
+  if (int rc0 = prefer_max_shared_carveout(); rc0 != SA_OK) return rc0;
+  const int tiles = (nb + kT - 1) / kT;
+  pooled_logits_kernel<<<dim3(tiles, tiles, L * B * H), 256, 0, stream>>>(qp, kp, nb, D, scale,
+                                                                          logits_ws);
+  SA_CUDA_TRY(cudaGetLastError());
+  const int warps = 8;
+  const size_t smem = (size_t)warps * nb * sizeof(float);
+  SA_CHECK_ARG(smem <= 200 * 1024, "sa_pooled_softmax_layers: nb=%d too large", nb);
+  if (smem > 48 * 1024)
+    SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t rows = (int64_t)L * H * nb;
+  row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
+      logits_ws, L, B, H, nb, nullptr, batch_means);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
@@ -575,8 +612,8 @@ extern "C" int sa_pool_scores_noalloc(const void* q, const void* k, const int64_
     SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t rows = (int64_t)H * nb;
-  row_softmax_kernel<<<(unsigned)((rows + 7) / 8), 256, smem, stream>>>(logits, B, H, nb, scores,
-                                                                         batch_mean);
+  row_softmax_kernel<<<(unsigned)((rows + 7) / 8), 256, smem, stream>>>(logits, 1, B, H, nb,
+                                                                         scores, batch_mean);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }

@@ -343,6 +343,30 @@ def block_stats(q: torch.Tensor, k: torch.Tensor, mode: str = "exact",
 _PASS_STREAMS: dict[int, tuple] = {}
 
 
+def pooled_softmax_layers(qp: torch.Tensor, kp: torch.Tensor, scale: Optional[float] = None,
+                          batch_means_out: Optional[torch.Tensor] = None,
+                          logits_ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-layer batch means of softmax(qp kp^T * scale) for L stacked layers:
+    qp, kp fp32 [L,B,H,nb,D] contiguous -> fp32 [L,H,nb,nb]."""
+    dev = _require_cuda(qp, kp)
+    L, B, H, nb, D = qp.shape
+    if kp.shape != qp.shape or not (qp.is_contiguous() and kp.is_contiguous()):
+        raise RuntimeError("pooled_softmax_layers expects contiguous qp, kp of one shape")
+    need = L * B * H * nb * nb
+    if logits_ws is None or logits_ws.numel() < need:
+        logits_ws = torch.empty(need, dtype=torch.float32, device=dev)
+    out = batch_means_out
+    if out is None:
+        out = torch.empty((L, H, nb, nb), dtype=torch.float32, device=dev)
+    sc = -1.0 if scale is None else float(scale)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_pooled_softmax_layers(qp.data_ptr(), kp.data_ptr(), L, B, H, nb, D, sc,
+                                          out.data_ptr(), logits_ws.data_ptr(), _stream(dev))
+    _lib.check(rc, "sa_pooled_softmax_layers")
+    return out
+
+
 def calibration_pass(
     layers,
     block: int = BLOCK,
@@ -353,13 +377,16 @@ def calibration_pass(
     force_sink_col: bool = False,
     want_batch_mean: bool = False,
     masks_out: Optional[torch.Tensor] = None,
+    chunk: int = 3,
 ):
     """Pooling + pooled softmax + batch mean + coverage mask for a sequence of
     layers, each given as a (q, k) pair of bf16 [B,H,S,D] CUDA tensors.
 
-    Two side streams pipeline the layers: the HBM-bound pooling of layer l+1
-    runs while the compute-bound score softmax and mask of layer l run, with
-    double-buffered pooled means. The result is ordered on the caller's
+    The layers go in chunks: every layer of a chunk is pooled back to back on
+    one side stream (HBM-bound, one persistent TMA kernel per layer), then the
+    chunk's pooled softmax and per-layer batch means (two launches for the
+    whole chunk) and its coverage masks (one launch) run on a second side
+    stream while the next chunk pools. The result is ordered on the caller's
     current stream. Returns (masks bool [L,H,nb,nb], batch means fp32
     [L,H,nb,nb] or None)."""
     layers = list(layers)
@@ -370,6 +397,7 @@ def calibration_pass(
     B, H, S, D = q0.shape
     nb = math.ceil(S / block)
     L = len(layers)
+    C = max(1, min(int(chunk), L))
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     if idx not in _PASS_STREAMS:
         _PASS_STREAMS[idx] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
@@ -378,35 +406,38 @@ def calibration_pass(
     masks = masks_out if masks_out is not None else torch.empty(
         (L, H, nb, nb), dtype=torch.bool, device=dev)
     bmeans = torch.empty((L, H, nb, nb), dtype=torch.float32, device=dev) if want_batch_mean \
-        else torch.empty((2, H, nb, nb), dtype=torch.float32, device=dev)
-    qp = [torch.empty((B, H, nb, D), dtype=torch.float32, device=dev) for _ in range(2)]
-    kp = [torch.empty((B, H, nb, D), dtype=torch.float32, device=dev) for _ in range(2)]
-    logits = torch.empty(B * H * nb * nb, dtype=torch.float32, device=dev)
+        else torch.empty((2, C, H, nb, nb), dtype=torch.float32, device=dev)
+    qp = torch.empty((2, C, B, H, nb, D), dtype=torch.float32, device=dev)
+    kp = torch.empty((2, C, B, H, nb, D), dtype=torch.float32, device=dev)
+    logits = torch.empty(C * B * H * nb * nb, dtype=torch.float32, device=dev)
     pooled = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     sp.wait_stream(cur)
     sc.wait_stream(cur)
-    for l, (q, k) in enumerate(layers):
-        if q.shape != (B, H, S, D) or k.shape != (B, H, S, D):
-            raise ValueError("all layers must share one [B,H,S,D] shape")
-        buf = l % 2
+    for ci, l0 in enumerate(range(0, L, C)):
+        l1 = min(L, l0 + C)
+        n = l1 - l0
+        buf = ci % 2
         with torch.cuda.stream(sp):
-            if l >= 2:
+            if ci >= 2:
                 sp.wait_event(consumed[buf])
-            pool_means(q, k, block, qp=qp[buf], kp=kp[buf])
+            for l in range(l0, l1):
+                q, k = layers[l]
+                if q.shape != (B, H, S, D) or k.shape != (B, H, S, D):
+                    raise ValueError("all layers must share one [B,H,S,D] shape")
+                pool_means(q, k, block, qp=qp[buf, l - l0], kp=kp[buf, l - l0])
             pooled[buf].record(sp)
         with torch.cuda.stream(sc):
             sc.wait_event(pooled[buf])
-            bm = bmeans[l] if want_batch_mean else bmeans[buf]
-            pooled_softmax(qp[buf], kp[buf], want_scores=False, want_batch_mean=True,
-                           logits_ws=logits, batch_mean_out=bm)
+            bm = bmeans[l0:l1] if want_batch_mean else bmeans[buf, :n]
+            pooled_softmax_layers(qp[buf, :n], kp[buf, :n], batch_means_out=bm, logits_ws=logits)
             consumed[buf].record(sc)
-            coverage_mask(bm, coverage=coverage, keep_diagonal=keep_diagonal,
+            coverage_mask(bm.reshape(n * H, nb, nb), coverage=coverage, keep_diagonal=keep_diagonal,
                           text_blocks=text_blocks, mode=mode, force_sink_col=force_sink_col,
-                          out=masks[l])
+                          out=masks[l0:l1].view(n * H, nb, nb))
     cur.wait_stream(sp)
     cur.wait_stream(sc)
-    for t in (*qp, *kp, logits, bmeans, masks):
+    for t in (qp, kp, logits, bmeans, masks):
         t.record_stream(sp)
         t.record_stream(sc)
     for q, k in layers:

@@ -197,9 +197,10 @@ def test_mix_outputs(oracle):
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
 
 
-def test_calibration_pass_matches_serial_chain():
-    """The two-stream pipelined pass over layers gives exactly the per-layer
-    serial results (same kernels, only the scheduling differs)."""
+@pytest.mark.parametrize("chunk", [1, 2, 10])
+def test_calibration_pass_matches_serial_chain(chunk):
+    """The chunked, two-stream pass over layers (stacked pooled softmax and one
+    mask launch per chunk) gives exactly the per-layer serial results."""
     from sinkattn_b200 import ops
 
     g = torch.Generator().manual_seed(8)
@@ -208,7 +209,8 @@ def test_calibration_pass_matches_serial_chain():
         q = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
         k = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
         layers.append((q, k))
-    masks, bms = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True)
+    masks, bms = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True,
+                                      chunk=chunk)
     torch.cuda.synchronize()
     for l, (q, k) in enumerate(layers):
         _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True)
