@@ -477,7 +477,8 @@ def run_ours(args):
             "mask_density": density30,
             "note": "cfg3: 30 layers x Q,K [2,12,32768,128] bf16 (GPU-generated, seed=layer); "
                     "pool -> pooled softmax -> batch mean -> coverage mask (sink column "
-                    "forced); pooling of layer l+1 overlaps the scores/mask of layer l"},
+                    "forced); layers in chunks of 3, the pooling of chunk c+1 overlaps the "
+                    "stacked scores and masks of chunk c"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
                 "api": "sinkattn_b200.reference_api._block_sparse_attn"},
