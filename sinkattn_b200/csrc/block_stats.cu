@@ -5,8 +5,10 @@
 //          score[qb, kb] = mean over the query rows r of block qb of
 //            sum_{n in kb} exp(s_rn - m_r) / max(sum_n exp(s_rn - m_r), 1e-6),
 //          s = q k^T / sqrt(D), m_r the row maximum over all keys.
-//          Two sweeps over the keys: the first builds m_r and the normaliser
-//          online, the second accumulates the normalised block masses.
+//          Two sweeps over the keys: the first finds m_r (maxima only, no
+//          exponentials); the second computes every block's unnormalised mass
+//          and the row sum in the same exponentials and keeps the masses in a
+//          per-CTA scratch slot, which the epilogue normalises and averages.
 //   MAX    the Triton pooling kernel attn_with_pooling (sinkattention/pooling_kernel.py:
 //          11-248), whose statistics are maxima (the "pooled" name notwithstanding):
 //            R[r, kb] = bf16( max_{n in kb} s_rn * log2(e) )         (line 45-48)
@@ -18,13 +20,17 @@
 //          here rows past S take no part in the column maxima and keys past S
 //          are masked, as the Triton kernel masks its last key block.
 //
-// One CTA per 128-row query tile; 256 threads:
-//   warp 0      TMA producer: the Q tile once, then K tiles (4-slot ring)
-//   warp 1      MMA issuer: S = Q K^T into one of 4 TMEM buffers
+// Persistent grid (one CTA per SM, looping over 128-row query tiles); 256
+// threads:
+//   warp 0      TMA producer: K tiles into a 6-slot ring
+//   warp 1      MMA issuer: S = Q K^T (Q from TMEM, K from shared memory)
+//               into one of 3 TMEM buffers, so it runs up to 3 blocks ahead
 //   warp 2      TMEM allocator
-//   warps 4-7   statistics, thread t owns query row t
-// With no PV step the tensor core runs up to 4 key blocks ahead of the
-// statistics warps (S buffers double as the pipeline depth).
+//   warps 4-7   statistics, thread t owns query row t; they also write the
+//               tile's Q into TMEM
+// TMEM: S buffers [0,384), Q [384,448) (bf16 pairs, the A-operand layout).
+// Each CTA owns one scratch slot of nk x 128 fp32 values (block masses, or
+// the bf16-rounded block maxima), written with one coalesced store per block.
 
 #include <math.h>
 
@@ -34,29 +40,32 @@ namespace sa {
 namespace stats {
 
 constexpr int kBM = 128, kBN = 128, kHD = 128;
-constexpr int kStages = 4;
-constexpr int kSBuf = 4;
+constexpr int kStages = 6;
+constexpr int kSBuf = 3;
 constexpr int kThreads = 256;
-constexpr int kTileBytes = kBM * kHD * 2;
+constexpr int kTileBytes = kBN * kHD * 2;
 constexpr int kBoxBytes = kTileBytes / 2;
 constexpr int kMaxNB = 1024;
+constexpr uint32_t kColQ = 384;
 
 enum Mode { kExact = 0, kMax = 1 };
 
 struct Params {
-  int B, H, S, nq, nk, mode;
+  int B, H, S, nq, nk, mode, tiles;
   float scale_log2;
+  const __nv_bfloat16* q;
+  int64_t qs0, qs1, qs2;
   float* scores;          // [B,H,nq,nk] fp32
-  __nv_bfloat16* rbuf;    // MAX: [B,H,nk,S] bf16 block maxima (rows contiguous per block)
+  float* scratch;         // [gridDim.x][nk][128] fp32
   int32_t* status;
 };
 
 struct __align__(8) SmemCtl {
-  uint64_t q_full;
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[kSBuf];
   uint64_t s_empty[kSBuf];
+  uint64_t q_ready;       // one phase per tile, 128 arrivals
   uint64_t mma_drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -65,7 +74,7 @@ struct __align__(8) SmemCtl {
   float psum[4];
 };
 
-constexpr size_t kSmemBytes = 1024 + kTileBytes + kStages * kTileBytes + sizeof(SmemCtl);
+constexpr size_t kSmemBytes = 1024 + kStages * kTileBytes + sizeof(SmemCtl);
 
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
@@ -75,23 +84,26 @@ __device__ __forceinline__ void stats_bar_sync() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& qb, int& h, int& b) {
+  qb = t % p.nq;
+  const int bh = t / p.nq;
+  h = bh % p.H;
+  b = bh / p.H;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-    block_stats_kernel(const __grid_constant__ CUtensorMap tm_q,
-                       const __grid_constant__ CUtensorMap tm_k, const Params p) {
+    block_stats_kernel(const __grid_constant__ CUtensorMap tm_k, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* q_smem = smem;
-  uint8_t* ring = smem + kTileBytes;
+  uint8_t* ring = smem;
   SmemCtl* ctl = reinterpret_cast<SmemCtl*>(ring + kStages * kTileBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int passes = p.mode == kExact ? 2 : 1;
-  const int items = passes * p.nk;
+  const int items = passes * p.nk;  // per tile
 
   if (threadIdx.x == 0) {
-    mbar_init(&ctl->q_full, 1);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&ctl->kv_full[i], 1);
       mbar_init(&ctl->kv_empty[i], 1);
@@ -100,14 +112,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->s_empty[i], kBM);
     }
+    mbar_init(&ctl->q_ready, kBM);
     mbar_init(&ctl->mma_drain, 1);
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) {
-    prefetch_tensormap(&tm_q);
-    prefetch_tensormap(&tm_k);
-  }
+  if (warp == 0 && lane == 0) prefetch_tensormap(&tm_k);
   if (warp == 2) {
     tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
@@ -120,50 +130,58 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(&ctl->q_full, kTileBytes);
-      tma_load_4d(&tm_q, &ctl->q_full, q_smem, 0, qb * kBM, h, b);
-      tma_load_4d(&tm_q, &ctl->q_full, q_smem + kBoxBytes, 64, qb * kBM, h, b);
-      int it = 0;
-      for (; it < items; ++it) {
-        const int stage = it % kStages;
-        if (!mbar_wait(&ctl->kv_empty[stage], ((uint32_t)(it / kStages) & 1u) ^ 1u, p.status,
-                       abort_flag))
-          break;
-        const int j = it % p.nk;
-        uint8_t* dst = ring + stage * kTileBytes;
-        mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
-        tma_load_4d(&tm_k, &ctl->kv_full[stage], dst, 0, j * kBN, h, b);
-        tma_load_4d(&tm_k, &ctl->kv_full[stage], dst + kBoxBytes, 64, j * kBN, h, b);
+      int g = 0;  // K tiles produced by this CTA
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        int qb, h, b;
+        tile_coords(p, t, qb, h, b);
+        for (int it = 0; it < items; ++it, ++g) {
+          const int stage = g % kStages;
+          if (!mbar_wait(&ctl->kv_empty[stage], ((uint32_t)(g / kStages) & 1u) ^ 1u, p.status,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int j = it % p.nk;
+          uint8_t* dst = ring + stage * kTileBytes;
+          mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
+          tma_load_4d(&tm_k, &ctl->kv_full[stage], dst, 0, j * kBN, h, b);
+          tma_load_4d(&tm_k, &ctl->kv_full[stage], dst + kBoxBytes, 64, j * kBN, h, b);
+        }
       }
-      for (int k = (it > kStages ? it - kStages : 0); k < it; ++k)
+      for (int k = (g > kStages ? g - kStages : 0); k < g; ++k)
         mbar_wait_drain(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u);
-      mbar_wait_drain(&ctl->q_full, 0);
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_bf16(kBM, kBN, 0, 0);
-      bool ok = mbar_wait(&ctl->q_full, 0, p.status, abort_flag);
-      tc_fence_after();
-      const uint32_t qa = smem_u32(q_smem);
       const uint32_t ring_base = smem_u32(ring);
-      for (int it = 0; ok && it < items; ++it) {
-        const int stage = it % kStages, buf = it % kSBuf;
-        if (!mbar_wait(&ctl->kv_full[stage], (uint32_t)(it / kStages) & 1u, p.status, abort_flag))
-          break;
-        if (!mbar_wait(&ctl->s_empty[buf], ((uint32_t)(it / kSBuf) & 1u) ^ 1u, p.status,
-                       abort_flag))
-          break;
+      int g = 0, tc = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++tc) {
+        if (!mbar_wait(&ctl->q_ready, (uint32_t)tc & 1u, p.status, abort_flag)) break;
         tc_fence_after();
-        const uint32_t tile = ring_base + stage * kTileBytes;
+        for (int it = 0; it < items; ++it, ++g) {
+          const int stage = g % kStages, buf = g % kSBuf;
+          if (!mbar_wait(&ctl->kv_full[stage], (uint32_t)(g / kStages) & 1u, p.status,
+                         abort_flag) ||
+              !mbar_wait(&ctl->s_empty[buf], ((uint32_t)(g / kSBuf) & 1u) ^ 1u, p.status,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tile = ring_base + stage * kTileBytes;
 #pragma unroll
-        for (int kk = 0; kk < kHD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-          mma_ss(tmem + buf * 128, make_sdesc_sw128(qa + off, 16, 1024),
-                 make_sdesc_sw128(tile + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kHD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+            mma_ts(tmem + buf * 128, tmem + kColQ + kk * 8, make_sdesc_sw128(tile + off, 16, 1024),
+                   idesc, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&ctl->kv_empty[stage]);
+          mma_commit(&ctl->s_full[buf]);
         }
-        mma_commit(&ctl->kv_empty[stage]);
-        mma_commit(&ctl->s_full[buf]);
       }
       mma_commit(&ctl->mma_drain);
       mbar_wait_drain(&ctl->mma_drain, 0);
@@ -172,117 +190,138 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
-    const int grow = qb * kBM + row;
-    const bool row_valid = grow < p.S;
-    const int rows_valid = min(kBM, p.S - qb * kBM);
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const int64_t bh = (int64_t)b * p.H + h;
-    __nv_bfloat16* rrow = p.rbuf != nullptr ? p.rbuf + bh * p.nk * p.S + grow : nullptr;
-    float m = -INFINITY, l = 0.f;
+    float* slot = p.scratch + (int64_t)blockIdx.x * p.nk * kBM;
     bool ok = true;
-    for (int it = 0; it < items; ++it) {
-      const int buf = it % kSBuf;
-      const int pass = it / p.nk, j = it % p.nk;
-      if (ok)
-        ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf], (uint32_t)(it / kSBuf) & 1u,
-                                                 p.status, abort_flag));
-      if (!ok) continue;
-      tc_fence_after();
-      uint32_t r[4][32];
-      const uint32_t s_addr = tmem + lane_off + buf * 128;
-      tmem_ld32(s_addr + 0, r[0]);
-      tmem_ld32(s_addr + 32, r[1]);
-      tmem_ld32(s_addr + 64, r[2]);
-      tmem_ld32(s_addr + 96, r[3]);
-      tmem_wait_ld();
-      reg_fence32(r[0]);
-      reg_fence32(r[1]);
-      reg_fence32(r[2]);
-      reg_fence32(r[3]);
-      tc_fence_before();
-      mbar_arrive(&ctl->s_empty[buf]);  // S copied out: the buffer may be refilled
-      const int valid = min(kBN, p.S - j * kBN);
-      if (valid < kBN) {
+    int g = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+      int qb, h, b;
+      tile_coords(p, t, qb, h, b);
+      const int grow = qb * kBM + row;
+      const bool row_valid = grow < p.S;
+      const int rows_valid = min(kBM, p.S - qb * kBM);
+      // Q row -> TMEM (all S of the previous tile has been read, so its QK
+      // MMAs are complete). Rows past S are zero.
+      {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t qv[32];
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            const uint4 w = row_valid ? src[half * 8 + v] : make_uint4(0, 0, 0, 0);
+            qv[4 * v] = w.x; qv[4 * v + 1] = w.y; qv[4 * v + 2] = w.z; qv[4 * v + 3] = w.w;
+          }
+          tmem_st32(tmem + lane_off + kColQ + half * 32, qv);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&ctl->q_ready);
+      }
+      float m = -INFINITY, l = 0.f;
+      for (int it = 0; it < items; ++it, ++g) {
+        const int buf = g % kSBuf;
+        const int pass = it / p.nk, j = it % p.nk;
+        if (ok)
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf], (uint32_t)(g / kSBuf) & 1u,
+                                                   p.status, abort_flag));
+        if (!ok) continue;
+        tc_fence_after();
+        uint32_t r[4][32];
+        const uint32_t s_addr = tmem + lane_off + buf * 128;
+        tmem_ld32(s_addr + 0, r[0]);
+        tmem_ld32(s_addr + 32, r[1]);
+        tmem_ld32(s_addr + 64, r[2]);
+        tmem_ld32(s_addr + 96, r[3]);
+        tmem_wait_ld();
+        reg_fence32(r[0]);
+        reg_fence32(r[1]);
+        reg_fence32(r[2]);
+        reg_fence32(r[3]);
+        tc_fence_before();
+        mbar_arrive(&ctl->s_empty[buf]);  // S copied out: the buffer may be refilled
+        const int valid = min(kBN, p.S - j * kBN);
+        if (valid < kBN) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+        }
+        if (p.mode == kMax || pass == 0) {
+          float mxp[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) mxp[u] = __uint_as_float(r[0][u]);
+#pragma unroll
+          for (int c = 8; c < 128; c += 16) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              mxp[u] = fmax3(mxp[u], __uint_as_float(r[(c + u) >> 5][(c + u) & 31]),
+                             __uint_as_float(r[(c + 8 + u) >> 5][(c + 8 + u) & 31]));
+          }
+          const float bmax = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                                   fmaxf(mxp[6], mxp[7]));
+          const float R = bmax * p.scale_log2;
+          m = fmaxf(m, R);
+          // MAX: the block maximum rounded as the Triton kernel stores it
+          // (pooling_kernel.py:45-48); EXACT keeps only the running maximum.
+          if (p.mode == kMax) slot[(int64_t)j * kBM + row] = bf16_round(R);
+          continue;
+        }
+        // EXACT, second sweep: this block's mass for the row under its final
+        // maximum m (every key of the row has been seen in the first sweep)
+        const float negm = -m;
+        float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 128; ++c)
-          if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
-      }
-      float mxp[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mxp[t] = __uint_as_float(r[0][t]);
-#pragma unroll
-      for (int c = 8; c < 128; c += 16) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-          mxp[t] = fmax3(mxp[t], __uint_as_float(r[(c + t) >> 5][(c + t) & 31]),
-                         __uint_as_float(r[(c + 8 + t) >> 5][(c + 8 + t) & 31]));
-      }
-      const float bmax = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
-                               fmaxf(mxp[6], mxp[7]));
-      if (p.mode == kMax) {
-        // block maximum of the scaled logits (pooling_kernel.py:45-48)
-        const float R = bmax * p.scale_log2;
-        m = fmaxf(m, R);
-        if (row_valid) rrow[(int64_t)j * p.S] = __float2bfloat16_rn(R);
-        continue;
-      }
-      if (pass == 0) {
-        const float mx = bmax * p.scale_log2;
-        if (mx > m) {
-          l *= ex2_approx(m - mx);  // 0 when m = -inf
-          m = mx;
-        }
-      }
-      const float negm = -m;
-      float sp[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 128; ++c)
-        sp[c & 3] += ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, negm));
-      const float mass = (sp[0] + sp[1]) + (sp[2] + sp[3]);
-      if (pass == 0) {
+          sp[c & 3] += ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, negm));
+        const float mass = (sp[0] + sp[1]) + (sp[2] + sp[3]);
         l += mass;
-      } else {
-        // this row's share of block j, normalised (sparse_attention.py:224),
-        // summed over the warp's rows
-        float v = row_valid ? mass / fmaxf(l, 1e-6f) : 0.f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) ctl->red[wq][j] = v;
+        slot[(int64_t)j * kBM + row] = mass;
       }
-    }
-    if (p.mode == kExact) {
-      stats_bar_sync();
-      const float inv_rows = 1.0f / (float)rows_valid;
-      float* out = p.scores + (bh * p.nq + qb) * p.nk;
-      for (int j = row; j < p.nk; j += kBM)
-        out[j] = ((ctl->red[0][j] + ctl->red[1][j]) + (ctl->red[2][j] + ctl->red[3][j])) * inv_rows;
-    } else {
-      // Po[qb, kb] = bf16(max over the tile's rows of exp2(R - m_r)); l_i = 1
-      // in the Triton kernel, so there is no division (pooling_kernel.py:65-75).
       __syncwarp();
-      for (int j = 0; j < p.nk; ++j) {
-        float x = row_valid ? ex2_approx(__bfloat162float(rrow[(int64_t)j * p.S]) - m) : 0.f;
+      float* out = p.scores + ((int64_t)t) * p.nk;  // tiles are ordered (b, h, qb)
+      if (p.mode == kExact) {
+        // sum over the tile's rows of mass / max(l, 1e-6) (sparse_attention.py:224),
+        // divided by the number of valid rows (the mean of line 225)
+        const float lc = fmaxf(l, 1e-6f);
+        for (int j = 0; j < p.nk; ++j) {
+          float v = row_valid ? __fdiv_rn(slot[(int64_t)j * kBM + row], lc) : 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-        if (lane == 0) ctl->red[wq][j] = x;
-      }
-      stats_bar_sync();
-      float part = 0.f;
-      for (int j = row; j < p.nk; j += kBM) {
-        const float po = bf16_round(fmaxf(fmaxf(ctl->red[0][j], ctl->red[1][j]),
-                                          fmaxf(ctl->red[2][j], ctl->red[3][j])));
-        ctl->po[j] = po;
-        part += po;
-      }
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) ctl->red[wq][j] = v;
+        }
+        stats_bar_sync();
+        const float inv_rows = 1.0f / (float)rows_valid;
+        for (int j = row; j < p.nk; j += kBM)
+          out[j] = ((ctl->red[0][j] + ctl->red[1][j]) + (ctl->red[2][j] + ctl->red[3][j])) * inv_rows;
+      } else {
+        // Po[qb, kb] = bf16(max over the tile's rows of exp2(R - m_r)); l_i = 1
+        // in the Triton kernel, so there is no division (pooling_kernel.py:65-75).
+        for (int j = 0; j < p.nk; ++j) {
+          float x = row_valid ? ex2_approx(slot[(int64_t)j * kBM + row] - m) : 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      if (lane == 0) ctl->psum[wq] = part;
-      stats_bar_sync();
-      // Po / sum(Po) with bf16 tensors (pooling_kernel.py:243-244): the sum is
-      // accumulated in fp32 and rounded to bf16, the quotient rounded to bf16.
-      const float sum = bf16_round((ctl->psum[0] + ctl->psum[1]) + (ctl->psum[2] + ctl->psum[3]));
-      float* out = p.scores + (bh * p.nq + qb) * p.nk;
-      for (int j = row; j < p.nk; j += kBM) out[j] = bf16_round(__fdiv_rn(ctl->po[j], sum));
+          for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+          if (lane == 0) ctl->red[wq][j] = x;
+        }
+        stats_bar_sync();
+        float part = 0.f;
+        for (int j = row; j < p.nk; j += kBM) {
+          const float po = bf16_round(fmaxf(fmaxf(ctl->red[0][j], ctl->red[1][j]),
+                                            fmaxf(ctl->red[2][j], ctl->red[3][j])));
+          ctl->po[j] = po;
+          part += po;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (lane == 0) ctl->psum[wq] = part;
+        stats_bar_sync();
+        // Po / sum(Po) with bf16 tensors (pooling_kernel.py:243-244): the sum is
+        // accumulated in fp32 and rounded to bf16, the quotient rounded to bf16.
+        const float sum =
+            bf16_round((ctl->psum[0] + ctl->psum[1]) + (ctl->psum[2] + ctl->psum[3]));
+        for (int j = row; j < p.nk; j += kBM) out[j] = bf16_round(__fdiv_rn(ctl->po[j], sum));
+      }
+      stats_bar_sync();  // red / po are rewritten by the next tile's epilogue
     }
   }
 
@@ -322,13 +361,20 @@ bool stats_strides_ok(const int64_t st[4]) {
   return true;
 }
 
+// CTAs of the persistent grid: one per SM, at most one per tile.
+int stats_grid(int B, int H, int S) {
+  const int64_t tiles = (int64_t)B * H * ((S + 127) / 128);
+  const int sms = sa::sm_count_current_device();
+  return (int)(tiles < sms ? tiles : sms);
+}
+
 }  // namespace
 
 extern "C" size_t sa_block_stats_workspace_size(int B, int H, int S, int mode) {
   if (B < 1 || H < 1 || S < 1) return 0;
-  if (mode != sa::stats::kMax) return 0;
+  if (mode != sa::stats::kExact && mode != sa::stats::kMax) return 0;
   const size_t nk = (size_t)((S + 127) / 128);
-  return (size_t)B * H * S * nk * 2;
+  return (size_t)stats_grid(B, H, S) * nk * 128 * sizeof(float);
 }
 
 extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_strides[4],
@@ -340,27 +386,30 @@ extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_stri
   SA_CHECK_ARG(mode == kExact || mode == kMax, "sa_block_stats: unknown mode %d", mode);
   SA_CHECK_ARG(D == kHD, "sa_block_stats: head dim must be 128, got %d", D);
   SA_CHECK_ARG(B >= 1 && H >= 1 && S >= 1, "sa_block_stats: B, H, S must be >= 1");
-  SA_CHECK_ARG(B <= 65535 && H <= 65535, "sa_block_stats: B/H too large");
   const int nq = (S + kBM - 1) / kBM, nk = nq;
   SA_CHECK_ARG(nk <= kMaxNB, "sa_block_stats: S=%d exceeds %d blocks", S, kMaxNB);
+  SA_CHECK_ARG((int64_t)B * H * nq <= 0x7fffffff, "sa_block_stats: too many query tiles");
   SA_CHECK_ARG(stats_strides_ok(q_strides) && stats_strides_ok(k_strides),
                "sa_block_stats: q/k need stride(dim)=1 and strides multiple of 8 elements");
   SA_CHECK_ARG(((uintptr_t)q | (uintptr_t)k) % 16 == 0, "sa_block_stats: q/k must be 16-byte aligned");
   const size_t need = sa_block_stats_workspace_size(B, H, S, mode);
-  SA_CHECK_ARG(need == 0 || (workspace != nullptr && ws_bytes >= need),
+  SA_CHECK_ARG(workspace != nullptr && ws_bytes >= need,
                "sa_block_stats: workspace of %zu bytes required, got %zu", need, ws_bytes);
+  SA_CHECK_ARG((uintptr_t)workspace % 16 == 0, "sa_block_stats: workspace must be 16-byte aligned");
 
-  CUtensorMap tq, tk;
+  CUtensorMap tk;
   int rc;
-  if ((rc = make_map_bhsd(&tq, q, q_strides, B, H, S, D)) != SA_OK) return rc;
   if ((rc = make_map_bhsd(&tk, k, k_strides, B, H, S, D)) != SA_OK) return rc;
   Params p;
   p.B = B; p.H = H; p.S = S; p.nq = nq; p.nk = nk; p.mode = mode;
+  p.tiles = B * H * nq;
   // 1/sqrt(D) in double then fp32, as a Python float passed to fp32 math
   const float scale = softmax_scale > 0.f ? softmax_scale : (float)(1.0 / sqrt((double)D));
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.qs0 = q_strides[0]; p.qs1 = q_strides[1]; p.qs2 = q_strides[2];
   p.scores = scores;
-  p.rbuf = reinterpret_cast<__nv_bfloat16*>(workspace);
+  p.scratch = reinterpret_cast<float*>(workspace);
   p.status = status;
   int dev = 0;
   SA_CUDA_TRY(cudaGetDevice(&dev));
@@ -370,7 +419,7 @@ extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_stri
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  block_stats_kernel<<<dim3(nq, H, B), kThreads, kSmemBytes, stream>>>(tq, tk, p);
+  block_stats_kernel<<<stats_grid(B, H, S), kThreads, kSmemBytes, stream>>>(tk, p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
