@@ -270,7 +270,7 @@ def kept_flops(mask_bhqk: torch.Tensor) -> float:
     return 4.0 * D * 128 * 128 * float(mask_bhqk.sum().item())
 
 
-def time_steps(fn, steps, stream, per_launch_events=True):
+def time_steps(fn, steps, stream):
     """Device time of `steps` calls (ms) with CUDA events on `stream`."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
