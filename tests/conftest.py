@@ -62,3 +62,12 @@ def oracle():
     from oracle import sinkattn_oracle
 
     return sinkattn_oracle
+
+
+@pytest.fixture(scope="module")
+def lib():
+    """The C-ABI library (loading needs no GPU; entry points are only called
+    with arguments they reject before any launch)."""
+    from sinkattn_b200 import _lib
+
+    return _lib.load()

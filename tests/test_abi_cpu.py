@@ -19,13 +19,6 @@ def header_symbols() -> list[str]:
     return sorted(set(re.findall(r"^SA_API\s+[\w\s\*]+?\b(sa_\w+)\s*\(", text, flags=re.M)))
 
 
-@pytest.fixture(scope="module")
-def lib():
-    from sinkattn_b200 import _lib
-
-    return _lib.load()
-
-
 def test_header_declares_symbols():
     syms = header_symbols()
     assert "sa_bsattn_fwd" in syms and "sa_coverage_mask" in syms and "sa_pool_scores" in syms
