@@ -270,6 +270,19 @@ def kept_flops(mask_bhqk: torch.Tensor) -> float:
     return 4.0 * D * 128 * 128 * float(mask_bhqk.sum().item())
 
 
+def memcpy2d_async(dst: int, dpitch: int, src: int, spitch: int, width: int, height: int,
+                   kind: str, stream) -> None:
+    """One cudaMemcpy2DAsync (pinned host <-> device) on a torch stream."""
+    from cuda.bindings import runtime as cudart
+
+    k = (cudart.cudaMemcpyKind.cudaMemcpyHostToDevice if kind == "h2d"
+         else cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+    (err,) = cudart.cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, k,
+                                      stream.cuda_stream)
+    if err != cudart.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaMemcpy2DAsync failed: {err}")
+
+
 def time_steps(fn, steps, stream):
     """Device time of `steps` calls (ms) with CUDA events on `stream`."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -411,36 +424,46 @@ def run_ours(args):
     k_d = torch.empty_like(k_bshd, device=dev)
     v_d = torch.empty_like(v_bshd, device=dev)
 
-    # The step moves each batch element separately: the host-to-device copy of
-    # element b+1 (copy engine) overlaps the attention call on element b, and
-    # the device-to-host copy of b's result overlaps the next call.
+    # The step moves the inputs in chunks of (batch element, group of heads):
+    # the host-to-device copy of chunk c+1 (copy engine) overlaps the attention
+    # call on chunk c, and the device-to-host copy of c's result overlaps the
+    # later copies in (PCIe is full duplex). A head group of the [B,S,H,D]
+    # buffers is a strided 2-D region (S rows of hg*D elements, pitch H*D), so
+    # each tensor of a chunk is one cudaMemcpy2DAsync.
+    hg = max(1, min(H, args.e2e_chunk_heads))
+    while H % hg:
+        hg -= 1
+    chunks = [(b, h0) for b in range(B) for h0 in range(0, H, hg)]
     s_h2d, s_cmp, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(B)]
-    ev_out = [torch.cuda.Event() for _ in range(B)]
+    ev_in = [torch.cuda.Event() for _ in chunks]
+    ev_out = [torch.cuda.Event() for _ in chunks]
+    pitch = H * D * 2
+    width = hg * D * 2
 
     def step_e2e():
         for st_ in (s_h2d, s_cmp, s_d2h):
             st_.wait_stream(stream)
-        for b in range(B):
-            with torch.cuda.stream(s_h2d):
-                q_d[b].copy_(qp[b], non_blocking=True)
-                k_d[b].copy_(kp[b], non_blocking=True)
-                v_d[b].copy_(vp[b], non_blocking=True)
-                ev_in[b].record(s_h2d)
-        for b in range(B):
+        for c, (b, h0) in enumerate(chunks):
+            for dst, src in ((q_d, qp), (k_d, kp), (v_d, vp)):
+                memcpy2d_async(dst[b, 0, h0].data_ptr(), pitch, src[b, 0, h0].data_ptr(), pitch,
+                               width, S, "h2d", s_h2d)
+            ev_in[c].record(s_h2d)
+        for c, (b, h0) in enumerate(chunks):
             with torch.cuda.stream(s_cmp):
-                s_cmp.wait_event(ev_in[b])
-                o, l = _block_sparse_attn(q_d[b:b + 1].permute(0, 2, 1, 3),
-                                          k_d[b:b + 1].permute(0, 2, 1, 3),
-                                          v_d[b:b + 1].permute(0, 2, 1, 3), mask20[b:b + 1],
-                                          return_lse=True)
-                ev_out[b].record(s_cmp)
+                s_cmp.wait_event(ev_in[c])
+                sl = (slice(b, b + 1), slice(None), slice(h0, h0 + hg))
+                o, l = _block_sparse_attn(q_d[sl].permute(0, 2, 1, 3), k_d[sl].permute(0, 2, 1, 3),
+                                          v_d[sl].permute(0, 2, 1, 3),
+                                          mask20[b:b + 1, h0:h0 + hg], return_lse=True)
+                ev_out[c].record(s_cmp)
             o.record_stream(s_d2h)
             l.record_stream(s_d2h)
             with torch.cuda.stream(s_d2h):
-                s_d2h.wait_event(ev_out[b])
-                out_h[b].copy_(o[0].permute(1, 0, 2), non_blocking=True)
-                lse_h[b].copy_(l[0], non_blocking=True)
+                s_d2h.wait_event(ev_out[c])
+                # o is [1,S,hg,D]-contiguous, viewed [1,hg,S,D]
+                memcpy2d_async(out_h[b, 0, h0].data_ptr(), pitch, o.data_ptr(), width, width, S,
+                               "d2h", s_d2h)
+                lse_h[b, h0:h0 + hg].copy_(l[0], non_blocking=True)
         for st_ in (s_h2d, s_cmp, s_d2h):
             stream.wait_stream(st_)
 
@@ -505,9 +528,11 @@ def run_ours(args):
                     "stacked scores and masks of chunk c"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
+                "chunk_heads": hg,
                 "api": "sinkattn_b200.reference_api._block_sparse_attn",
-                "note": "pinned host buffers; per batch element, H2D of the next element "
-                        "overlaps the call on the current one, D2H overlaps the next call"},
+                "note": "pinned host buffers [B,S,H,D]; chunks of (batch element, chunk_heads "
+                        "heads) as 2-D copies: H2D of chunk c+1 overlaps the call on chunk c, "
+                        "D2H of c overlaps the later H2D copies"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                      "frac": achieved / peak, "traffic": traffic,
                      "kernel": "sa::attn::bsattn_fwd_kernel",
@@ -683,6 +708,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    ap.add_argument("--e2e-chunk-heads", type=int, default=1,
+                    help="heads per host<->device chunk of the end-to-end leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
                                        "calib-pass", "wan-runtime", "stats-wan", "stats-small",
                                        "qkrope-wan"],

@@ -28,77 +28,93 @@ namespace qkrope {
 
 constexpr int kMaxVecPerLane = 16;  // hidden <= 32 lanes x 16 vectors x 8 = 4096
 
+// bf16 pair (low half = even channel) -> two fp32 values, exact.
+__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) {
+  return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 template <int VPL>
 __device__ __forceinline__ float row_rstd(const uint4 (&raw)[VPL], int count, int hidden,
                                           float eps) {
-  float ss = 0.f;
+  // even and odd channels accumulate in the two halves of one f32x2 sum
+  uint64_t ss2 = f2_pack(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     if (i >= count) continue;
-    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&raw[i]);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float2 f = __bfloat1622float2(p[e]);
-      ss = fmaf(f.x, f.x, ss);
-      ss = fmaf(f.y, f.y, ss);
+      const uint64_t x2 = bf16x2_to_f2(w[e]);
+      ss2 = f2_fma(x2, x2, ss2);
     }
   }
+  float s0, s1;
+  f2_unpack(ss2, s0, s1);
+  float ss = s0 + s1;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hidden), eps)));
 }
 
-__device__ __forceinline__ void load_w8(const void* w, int w_is_bf16, int c0, float* out) {
+// Weights of channels c0..c0+7 as four f32x2 pairs (all 1 without weights).
+__device__ __forceinline__ void load_w8(const void* w, int w_is_bf16, int c0, uint64_t (&out)[4]) {
   if (w == nullptr) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) out[e] = 1.f;
+    for (int e = 0; e < 4; ++e) out[e] = f2_pack(1.f, 1.f);
   } else if (w_is_bf16) {
     const uint4 v = reinterpret_cast<const uint4*>(w)[c0 >> 3];
-    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __bfloat1622float2(p[e]);
-      out[2 * e] = f.x;
-      out[2 * e + 1] = f.y;
-    }
+    for (int e = 0; e < 4; ++e) out[e] = bf16x2_to_f2(p[e]);
   } else {
     const float4 a = reinterpret_cast<const float4*>(w)[c0 >> 2];
     const float4 b = reinterpret_cast<const float4*>(w)[(c0 >> 2) + 1];
-    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
-    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+    out[0] = f2_pack(a.x, a.y); out[1] = f2_pack(a.z, a.w);
+    out[2] = f2_pack(b.x, b.y); out[3] = f2_pack(b.z, b.w);
   }
 }
 
-// Normalise, round to bf16 and rotate 8 channels (4 pairs) of one row.
-__device__ __forceinline__ uint4 norm_rope8(const uint4 raw, float rstd, const float* w,
-                                            const float* cs, const float* sn) {
-  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+// Normalise, round to bf16 and rotate 8 channels (4 pairs) of one row, on
+// f32x2 pairs. Per lane this is the scalar arithmetic
+//   y = bf16((x * rstd) * w),
+//   out_even = fma(y_even, cos, -(y_odd * sin)), out_odd = fma(y_even, sin, y_odd * cos),
+// with csn[e] = (cos, sin) and nsc[e] = (-sin, cos): -(y_odd*sin) = y_odd*(-sin)
+// exactly, so the packed products round exactly as the scalar ones.
+__device__ __forceinline__ uint4 norm_rope8(const uint4 raw, uint64_t rstd2,
+                                            const uint64_t (&w2)[4], bool rope,
+                                            const uint64_t (&csn)[4], const uint64_t (&nsc)[4]) {
+  const uint32_t* p = reinterpret_cast<const uint32_t*>(&raw);
   uint4 res;
   uint32_t* r32 = reinterpret_cast<uint32_t*>(&res);
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const float2 f = __bfloat1622float2(p[e]);
+    float a0, a1;
+    f2_unpack(f2_mul(f2_mul(bf16x2_to_f2(p[e]), rstd2), w2[e]), a0, a1);
     // the RMSNorm output as the reference stores it (bf16)
-    float y0 = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(f.x, rstd), w[2 * e])));
-    float y1 = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(f.y, rstd), w[2 * e + 1])));
-    if (cs != nullptr) {
-      const float o0 = fmaf(y0, cs[e], -__fmul_rn(y1, sn[e]));
-      const float o1 = fmaf(y0, sn[e], __fmul_rn(y1, cs[e]));
-      y0 = o0;
-      y1 = o1;
+    const uint32_t yb = pack_bf16x2(a0, a1);
+    if (rope) {
+      const float y0 = __uint_as_float(yb << 16);
+      const float y1 = __uint_as_float(yb & 0xffff0000u);
+      const uint64_t u = f2_mul(f2_pack(y1, y1), nsc[e]);
+      float o0, o1;
+      f2_unpack(f2_fma(f2_pack(y0, y0), csn[e], u), o0, o1);
+      r32[e] = pack_bf16x2(o0, o1);
+    } else {
+      r32[e] = yb;
     }
-    const __nv_bfloat162 ob = __floats2bfloat162_rn(y0, y1);
-    r32[e] = *reinterpret_cast<const uint32_t*>(&ob);
   }
   return res;
 }
 
-// grid: ceil(rows / 8) CTAs of 8 warps; warp w of CTA c handles token row
-// 8c + w of Q and of K. Both rows are loaded before either is reduced, and
-// the weights and the position's cos/sin are read as 16-byte vectors shared
-// by the two tensors.
+// grid: one single-warp CTA per token row, which handles that row of Q and
+// of K. Both rows are loaded (streaming, evict-first) before either is
+// reduced, and the weights and the position's cos/sin are read as 16-byte
+// vectors shared by the two tensors. Up to hidden = 1536 (6 vectors per lane)
+// the register budget is capped for 24 resident warps per SM: the extra rows
+// in flight are worth more than the few spilled registers, and single-warp
+// CTAs retire and refill the SM without waiting for slower sibling warps.
 template <int VPL>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32, (VPL <= 6 ? 24 : 1))
     qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ q_in, const __nv_bfloat16* __restrict__ k_in,
                         int64_t qs_in, int64_t ks_in, int rows, int S, int hidden, int D,
                         const void* __restrict__ wq, const void* __restrict__ wk, int w_is_bf16,
@@ -106,7 +122,7 @@ __global__ void __launch_bounds__(256)
                         int64_t fs, __nv_bfloat16* __restrict__ q_out,
                         __nv_bfloat16* __restrict__ k_out, int64_t qs_out, int64_t ks_out) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t row = blockIdx.x;
   if (row >= rows) return;
   const int nvec = hidden >> 3;
   const int count = (nvec - lane + 31) >> 5;  // vectors of this lane
@@ -116,12 +132,12 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     if (i < count) {
-      rq[i] = qv[lane + 32 * i];
-      rk[i] = kv[lane + 32 * i];
+      rq[i] = __ldcs(qv + lane + 32 * i);
+      rk[i] = __ldcs(kv + lane + 32 * i);
     }
   }
-  const float rstd_q = row_rstd<VPL>(rq, count, hidden, eps);
-  const float rstd_k = row_rstd<VPL>(rk, count, hidden, eps);
+  const uint64_t rstd_q = [&] { const float r = row_rstd<VPL>(rq, count, hidden, eps); return f2_pack(r, r); }();
+  const uint64_t rstd_k = [&] { const float r = row_rstd<VPL>(rk, count, hidden, eps); return f2_pack(r, r); }();
   const int s = (int)(row % S);
   const float* crow = cos_t != nullptr ? cos_t + (int64_t)s * fs : nullptr;
   const float* srow = sin_t != nullptr ? sin_t + (int64_t)s * fs : nullptr;
@@ -132,23 +148,25 @@ __global__ void __launch_bounds__(256)
     if (i >= count) continue;
     const int v = lane + 32 * i;
     const int c0 = v * 8;
-    float cs[4], sn[4];
-    const float* csp = nullptr;
-    const float* snp = nullptr;
-    if (crow != nullptr) {
+    uint64_t csn[4], nsc[4];
+    const bool rope = crow != nullptr;
+    if (rope) {
       const int p0 = (c0 % D) >> 1;  // 4 consecutive pairs, 16-byte aligned
       const float4 c4 = *reinterpret_cast<const float4*>(crow + p0);
       const float4 s4 = *reinterpret_cast<const float4*>(srow + p0);
-      cs[0] = c4.x; cs[1] = c4.y; cs[2] = c4.z; cs[3] = c4.w;
-      sn[0] = s4.x; sn[1] = s4.y; sn[2] = s4.z; sn[3] = s4.w;
-      csp = cs;
-      snp = sn;
+      csn[0] = f2_pack(c4.x, s4.x); csn[1] = f2_pack(c4.y, s4.y);
+      csn[2] = f2_pack(c4.z, s4.z); csn[3] = f2_pack(c4.w, s4.w);
+      nsc[0] = f2_pack(-s4.x, c4.x); nsc[1] = f2_pack(-s4.y, c4.y);
+      nsc[2] = f2_pack(-s4.z, c4.z); nsc[3] = f2_pack(-s4.w, c4.w);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) csn[e] = nsc[e] = 0ull;
     }
-    float w8[8];
-    load_w8(wq, w_is_bf16, c0, w8);
-    qo[v] = norm_rope8(rq[i], rstd_q, w8, csp, snp);
-    load_w8(wk, w_is_bf16, c0, w8);
-    ko[v] = norm_rope8(rk[i], rstd_k, w8, csp, snp);
+    uint64_t w2[4];
+    load_w8(wq, w_is_bf16, c0, w2);
+    __stcs(qo + v, norm_rope8(rq[i], rstd_q, w2, rope, csn, nsc));
+    load_w8(wk, w_is_bf16, c0, w2);
+    __stcs(ko + v, norm_rope8(rk[i], rstd_k, w2, rope, csn, nsc));
   }
 }
 
@@ -185,13 +203,13 @@ extern "C" int sa_qk_norm_rope(const void* q_in, const void* k_in, int64_t q_in_
   SA_CHECK_ARG((w_q == nullptr) == (w_k == nullptr), "sa_qk_norm_rope: weights go together");
   if (rows == 0) return SA_OK;
   const int vpl = (hidden / 8 + 31) / 32;
-  const dim3 grid((unsigned)((rows + 7) / 8));
+  const dim3 grid((unsigned)rows);
   const auto* qi = reinterpret_cast<const __nv_bfloat16*>(q_in);
   const auto* ki = reinterpret_cast<const __nv_bfloat16*>(k_in);
   auto* qo = reinterpret_cast<__nv_bfloat16*>(q_out);
   auto* ko = reinterpret_cast<__nv_bfloat16*>(k_out);
 #define SA_QKROPE_LAUNCH(V)                                                                    \
-  qk_norm_rope_kernel<V><<<grid, 256, 0, stream>>>(qi, ki, q_in_row_stride, k_in_row_stride,   \
+  qk_norm_rope_kernel<V><<<grid, 32, 0, stream>>>(qi, ki, q_in_row_stride, k_in_row_stride,   \
                                                    rows, S, hidden, D, w_q, w_k, w_is_bf16, eps, \
                                                    cos_table, sin_table, freq_row_stride, qo,  \
                                                    ko, q_out_row_stride, k_out_row_stride)
