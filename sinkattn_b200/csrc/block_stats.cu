@@ -20,17 +20,20 @@
 //          here rows past S take no part in the column maxima and keys past S
 //          are masked, as the Triton kernel masks its last key block.
 //
-// Persistent grid (one CTA per SM, looping over 128-row query tiles); 256
-// threads:
-//   warp 0      TMA producer: K tiles into a 6-slot ring
-//   warp 1      MMA issuer: S = Q K^T (Q from TMEM, K from shared memory)
-//               into one of 3 TMEM buffers, so it runs up to 3 blocks ahead
+// Persistent grid (one CTA per SM) looping over pairs of 128-row query tiles
+// of one head: every K tile brought into shared memory serves both query
+// tiles, which halves the L2 -> shared-memory traffic per MMA. 384 threads:
+//   warp 0      TMA producer: K tiles into a 5-slot ring
+//   warp 1      MMA issuer: S = Q_a K^T (Q_a from TMEM, K from shared memory)
+//               for a = 0, 1, into 3 TMEM buffers used round robin
 //   warp 2      TMEM allocator
-//   warps 4-7   statistics, thread t owns query row t; they also write the
-//               tile's Q into TMEM
-// TMEM: S buffers [0,384), Q [384,448) (bf16 pairs, the A-operand layout).
-// Each CTA owns one scratch slot of nk x 128 fp32 values (block masses, or
-// the bf16-rounded block maxima), written with one coalesced store per block.
+//   warps 4-7   statistics of query tile 0 (thread t owns query row t)
+//   warps 8-11  statistics of query tile 1
+//   Each statistics group writes its tile's Q into TMEM.
+// TMEM: S buffers [0,384), Q_0 [384,448), Q_1 [448,512) (bf16 pairs, the
+// A-operand layout). Each CTA owns one scratch slot of 2 x nk x 128 fp32
+// values (block masses, or the bf16-rounded block maxima), written with one
+// coalesced store per block.
 
 #include <math.h>
 
@@ -40,23 +43,24 @@ namespace sa {
 namespace stats {
 
 constexpr int kBM = 128, kBN = 128, kHD = 128;
-constexpr int kStages = 6;
+constexpr int kStages = 5;
 constexpr int kSBuf = 3;
-constexpr int kThreads = 256;
+constexpr int kGroups = 2;  // query tiles per work item
+constexpr int kThreads = 128 + kGroups * 128;
 constexpr int kTileBytes = kBN * kHD * 2;
 constexpr int kBoxBytes = kTileBytes / 2;
 constexpr int kMaxNB = 1024;
-constexpr uint32_t kColQ = 384;
+constexpr uint32_t kColQ = 384;  // Q of tile a at kColQ + 64 a
 
 enum Mode { kExact = 0, kMax = 1 };
 
 struct Params {
-  int B, H, S, nq, nk, mode, tiles;
+  int B, H, S, nq, nk, mode, pairs;
   float scale_log2;
   const __nv_bfloat16* q;
   int64_t qs0, qs1, qs2;
   float* scores;          // [B,H,nq,nk] fp32
-  float* scratch;         // [gridDim.x][nk][128] fp32
+  float* scratch;         // [gridDim.x][kGroups][nk][128] fp32
   int32_t* status;
 };
 
@@ -64,14 +68,15 @@ struct __align__(8) SmemCtl {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[kSBuf];
-  uint64_t s_empty[kSBuf];
-  uint64_t q_ready;       // one phase per tile, 128 arrivals
+  uint64_t s_empty[kSBuf];   // 128 arrivals: the statistics group of the item
+  uint64_t q_ready[kGroups]; // one phase per work item of the group, 128 arrivals
   uint64_t mma_drain;
   uint32_t tmem_base;
   int abort_flag;
-  float red[4][kMaxNB];   // per-warp column partials
-  float po[kMaxNB];       // MAX: bf16 column maxima before normalisation
-  float psum[4];
+  int s_tag[kSBuf];          // index of the S item last issued into each buffer
+  float red[kGroups][4][kMaxNB];  // per-warp column partials
+  float po[kGroups][kMaxNB];      // MAX: bf16 column maxima before normalisation
+  float psum[kGroups][4];
 };
 
 constexpr size_t kSmemBytes = 1024 + kStages * kTileBytes + sizeof(SmemCtl);
@@ -80,15 +85,47 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-__device__ __forceinline__ void stats_bar_sync() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+// Named barrier of one statistics group (ids 1 and 2, 128 threads each).
+__device__ __forceinline__ void stats_bar_sync(int group) {
+  asm volatile("bar.sync %0, 128;" ::"r"(group + 1) : "memory");
 }
 
-__device__ __forceinline__ void tile_coords(const Params& p, int t, int& qb, int& h, int& b) {
-  qb = t % p.nq;
-  const int bh = t / p.nq;
+// Work item t: query tiles 2 qp and 2 qp + 1 (if it exists) of head (b, h).
+__device__ __forceinline__ void pair_coords(const Params& p, int t, int& qp, int& h, int& b,
+                                            int& ntp) {
+  const int nqp = (p.nq + 1) >> 1;
+  qp = t % nqp;
+  const int bh = t / nqp;
   h = bh % p.H;
   b = bh / p.H;
+  ntp = min(kGroups, p.nq - 2 * qp);
+}
+
+// Bounded wait until the MMA thread has issued S item `want` into a buffer.
+// The buffers are shared by the two statistics groups, so the phase parity of
+// s_full alone cannot tell item g from item g - 3 of the other group; the tag
+// can (it is written before the item's MMAs are issued, and only after item
+// g - 3 has been consumed).
+__device__ __forceinline__ bool wait_tag(const int* tag, int want, int32_t* status,
+                                         volatile int* abort_flag) {
+  const volatile int* t = tag;
+  if (*t == want) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (*t == want) return true;
+    if ((it & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (status != nullptr && *reinterpret_cast<volatile int32_t*>(status) != 0) {
+        *abort_flag = 1;
+        return false;
+      }
+      if (global_timer_ns() - t0 > kWaitNs) {
+        *abort_flag = 1;
+        if (status != nullptr) atomicExch(status, SA_DEV_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -101,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int passes = p.mode == kExact ? 2 : 1;
-  const int items = passes * p.nk;  // per tile
+  const int items = passes * p.nk;  // K tiles per work item
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -111,8 +148,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kSBuf; ++i) {
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->s_empty[i], kBM);
+      ctl->s_tag[i] = -1;
     }
-    mbar_init(&ctl->q_ready, kBM);
+    for (int a = 0; a < kGroups; ++a) mbar_init(&ctl->q_ready[a], kBM);
     mbar_init(&ctl->mma_drain, 1);
     ctl->abort_flag = 0;
     fence_barrier_init();
@@ -132,9 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int g = 0;  // K tiles produced by this CTA
       bool ok = true;
-      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-        int qb, h, b;
-        tile_coords(p, t, qb, h, b);
+      for (int t = blockIdx.x; t < p.pairs && ok; t += gridDim.x) {
+        int qp, h, b, ntp;
+        pair_coords(p, t, qp, h, b, ntp);
         for (int it = 0; it < items; ++it, ++g) {
           const int stage = g % kStages;
           if (!mbar_wait(&ctl->kv_empty[stage], ((uint32_t)(g / kStages) & 1u) ^ 1u, p.status,
@@ -157,30 +195,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_bf16(kBM, kBN, 0, 0);
       const uint32_t ring_base = smem_u32(ring);
-      int g = 0, tc = 0;
+      int g = 0, gs = 0;          // K tiles consumed, S items issued
+      int qc[kGroups] = {0, 0};   // work items started per group (q_ready phases)
       bool ok = true;
-      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++tc) {
-        if (!mbar_wait(&ctl->q_ready, (uint32_t)tc & 1u, p.status, abort_flag)) break;
+      for (int t = blockIdx.x; t < p.pairs && ok; t += gridDim.x) {
+        int qp, h, b, ntp;
+        pair_coords(p, t, qp, h, b, ntp);
+        for (int a = 0; a < ntp && ok; ++a) {
+          ok = mbar_wait(&ctl->q_ready[a], (uint32_t)qc[a] & 1u, p.status, abort_flag);
+          ++qc[a];
+        }
+        if (!ok) break;
         tc_fence_after();
-        for (int it = 0; it < items; ++it, ++g) {
-          const int stage = g % kStages, buf = g % kSBuf;
+        for (int it = 0; it < items && ok; ++it, ++g) {
+          const int stage = g % kStages;
           if (!mbar_wait(&ctl->kv_full[stage], (uint32_t)(g / kStages) & 1u, p.status,
-                         abort_flag) ||
-              !mbar_wait(&ctl->s_empty[buf], ((uint32_t)(g / kSBuf) & 1u) ^ 1u, p.status,
                          abort_flag)) {
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t tile = ring_base + stage * kTileBytes;
+          for (int a = 0; a < ntp; ++a, ++gs) {
+            const int buf = gs % kSBuf;
+            if (!mbar_wait(&ctl->s_empty[buf], ((uint32_t)(gs / kSBuf) & 1u) ^ 1u, p.status,
+                           abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            *reinterpret_cast<volatile int*>(&ctl->s_tag[buf]) = gs;
 #pragma unroll
-          for (int kk = 0; kk < kHD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-            mma_ts(tmem + buf * 128, tmem + kColQ + kk * 8, make_sdesc_sw128(tile + off, 16, 1024),
-                   idesc, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kHD / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+              mma_ts(tmem + buf * 128, tmem + kColQ + a * 64 + kk * 8,
+                     make_sdesc_sw128(tile + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&ctl->s_full[buf]);
           }
-          mma_commit(&ctl->kv_empty[stage]);
-          mma_commit(&ctl->s_full[buf]);
+          if (ok) mma_commit(&ctl->kv_empty[stage]);
         }
       }
       mma_commit(&ctl->mma_drain);
@@ -188,20 +240,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp >= 4) {
+    const int grp = (warp - 4) >> 2;  // query tile of the work item
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    float* slot = p.scratch + (int64_t)blockIdx.x * p.nk * kBM;
+    float* slot = p.scratch + ((int64_t)blockIdx.x * kGroups + grp) * p.nk * kBM;
+    float* red = ctl->red[grp][0];    // red[wq][j] at red[wq * kMaxNB + j]
+    float* po_s = ctl->po[grp];
+    float* psum = ctl->psum[grp];
     bool ok = true;
-    int g = 0;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
-      int qb, h, b;
-      tile_coords(p, t, qb, h, b);
+    int gbase = 0;  // index of the work item's first S item in this CTA's sequence
+    for (int t = blockIdx.x; t < p.pairs; t += gridDim.x) {
+      int qp, h, b, ntp;
+      pair_coords(p, t, qp, h, b, ntp);
+      if (grp >= ntp) {
+        gbase += items * ntp;
+        continue;
+      }
+      const int qb = 2 * qp + grp;
       const int grow = qb * kBM + row;
       const bool row_valid = grow < p.S;
       const int rows_valid = min(kBM, p.S - qb * kBM);
-      // Q row -> TMEM (all S of the previous tile has been read, so its QK
-      // MMAs are complete). Rows past S are zero.
+      // Q row -> TMEM (all S of this group's previous work item has been read,
+      // so the MMAs that read Q_grp are complete). Rows past S are zero.
       {
         const uint4* src = reinterpret_cast<const uint4*>(
             p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2);
@@ -213,19 +274,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint4 w = row_valid ? src[half * 8 + v] : make_uint4(0, 0, 0, 0);
             qv[4 * v] = w.x; qv[4 * v + 1] = w.y; qv[4 * v + 2] = w.z; qv[4 * v + 3] = w.w;
           }
-          tmem_st32(tmem + lane_off + kColQ + half * 32, qv);
+          tmem_st32(tmem + lane_off + kColQ + grp * 64 + half * 32, qv);
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&ctl->q_ready);
+        mbar_arrive(&ctl->q_ready[grp]);
       }
       float m = -INFINITY, l = 0.f;
-      for (int it = 0; it < items; ++it, ++g) {
-        const int buf = g % kSBuf;
+      for (int it = 0; it < items; ++it) {
+        const int gi = gbase + it * ntp + grp;
+        const int buf = gi % kSBuf;
         const int pass = it / p.nk, j = it % p.nk;
         if (ok)
-          ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf], (uint32_t)(g / kSBuf) & 1u,
-                                                   p.status, abort_flag));
+          ok = __all_sync(0xffffffffu,
+                          wait_tag(&ctl->s_tag[buf], gi, p.status, abort_flag) &&
+                              mbar_wait(&ctl->s_full[buf], (uint32_t)(gi / kSBuf) & 1u, p.status,
+                                        abort_flag));
         if (!ok) continue;
         tc_fence_after();
         uint32_t r[4][32];
@@ -278,8 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         l += mass;
         slot[(int64_t)j * kBM + row] = mass;
       }
+      gbase += items * ntp;
       __syncwarp();
-      float* out = p.scores + ((int64_t)t) * p.nk;  // tiles are ordered (b, h, qb)
+      float* out = p.scores + ((int64_t)(b * p.H + h) * p.nq + qb) * p.nk;
       if (p.mode == kExact) {
         // sum over the tile's rows of mass / max(l, 1e-6) (sparse_attention.py:224),
         // divided by the number of valid rows (the mean of line 225)
@@ -288,12 +353,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v = row_valid ? __fdiv_rn(slot[(int64_t)j * kBM + row], lc) : 0.f;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == 0) ctl->red[wq][j] = v;
+          if (lane == 0) red[wq * kMaxNB + j] = v;
         }
-        stats_bar_sync();
+        stats_bar_sync(grp);
         const float inv_rows = 1.0f / (float)rows_valid;
         for (int j = row; j < p.nk; j += kBM)
-          out[j] = ((ctl->red[0][j] + ctl->red[1][j]) + (ctl->red[2][j] + ctl->red[3][j])) * inv_rows;
+          out[j] = ((red[j] + red[kMaxNB + j]) + (red[2 * kMaxNB + j] + red[3 * kMaxNB + j])) *
+                   inv_rows;
       } else {
         // Po[qb, kb] = bf16(max over the tile's rows of exp2(R - m_r)); l_i = 1
         // in the Triton kernel, so there is no division (pooling_kernel.py:65-75).
@@ -301,27 +367,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           float x = row_valid ? ex2_approx(slot[(int64_t)j * kBM + row] - m) : 0.f;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-          if (lane == 0) ctl->red[wq][j] = x;
+          if (lane == 0) red[wq * kMaxNB + j] = x;
         }
-        stats_bar_sync();
+        stats_bar_sync(grp);
         float part = 0.f;
         for (int j = row; j < p.nk; j += kBM) {
-          const float po = bf16_round(fmaxf(fmaxf(ctl->red[0][j], ctl->red[1][j]),
-                                            fmaxf(ctl->red[2][j], ctl->red[3][j])));
-          ctl->po[j] = po;
+          const float po = bf16_round(fmaxf(fmaxf(red[j], red[kMaxNB + j]),
+                                            fmaxf(red[2 * kMaxNB + j], red[3 * kMaxNB + j])));
+          po_s[j] = po;
           part += po;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        if (lane == 0) ctl->psum[wq] = part;
-        stats_bar_sync();
+        if (lane == 0) psum[wq] = part;
+        stats_bar_sync(grp);
         // Po / sum(Po) with bf16 tensors (pooling_kernel.py:243-244): the sum is
         // accumulated in fp32 and rounded to bf16, the quotient rounded to bf16.
-        const float sum =
-            bf16_round((ctl->psum[0] + ctl->psum[1]) + (ctl->psum[2] + ctl->psum[3]));
-        for (int j = row; j < p.nk; j += kBM) out[j] = bf16_round(__fdiv_rn(ctl->po[j], sum));
+        const float sum = bf16_round((psum[0] + psum[1]) + (psum[2] + psum[3]));
+        for (int j = row; j < p.nk; j += kBM) out[j] = bf16_round(__fdiv_rn(po_s[j], sum));
       }
-      stats_bar_sync();  // red / po are rewritten by the next tile's epilogue
+      stats_bar_sync(grp);  // red / po are rewritten by the next work item's epilogue
     }
   }
 
@@ -361,11 +426,13 @@ bool stats_strides_ok(const int64_t st[4]) {
   return true;
 }
 
-// CTAs of the persistent grid: one per SM, at most one per tile.
+// CTAs of the persistent grid: one per SM, at most one per work item (pair
+// of query tiles of one head).
 int stats_grid(int B, int H, int S) {
-  const int64_t tiles = (int64_t)B * H * ((S + 127) / 128);
+  const int64_t nq = (S + 127) / 128;
+  const int64_t pairs = (int64_t)B * H * ((nq + 1) / 2);
   const int sms = sa::sm_count_current_device();
-  return (int)(tiles < sms ? tiles : sms);
+  return (int)(pairs < sms ? pairs : sms);
 }
 
 }  // namespace
@@ -374,7 +441,7 @@ extern "C" size_t sa_block_stats_workspace_size(int B, int H, int S, int mode) {
   if (B < 1 || H < 1 || S < 1) return 0;
   if (mode != sa::stats::kExact && mode != sa::stats::kMax) return 0;
   const size_t nk = (size_t)((S + 127) / 128);
-  return (size_t)stats_grid(B, H, S) * nk * 128 * sizeof(float);
+  return (size_t)stats_grid(B, H, S) * sa::stats::kGroups * nk * 128 * sizeof(float);
 }
 
 extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_strides[4],
@@ -402,7 +469,7 @@ extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_stri
   if ((rc = make_map_bhsd(&tk, k, k_strides, B, H, S, D)) != SA_OK) return rc;
   Params p;
   p.B = B; p.H = H; p.S = S; p.nq = nq; p.nk = nk; p.mode = mode;
-  p.tiles = B * H * nq;
+  p.pairs = B * H * ((nq + 1) / 2);
   // 1/sqrt(D) in double then fp32, as a Python float passed to fp32 math
   const float scale = softmax_scale > 0.f ? softmax_scale : (float)(1.0 / sqrt((double)D));
   p.scale_log2 = scale * 1.4426950408889634f;
