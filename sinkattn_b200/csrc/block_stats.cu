@@ -67,13 +67,12 @@ struct Params {
 struct __align__(8) SmemCtl {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[kSBuf];
+  uint64_t s_full[kSBuf][kGroups];  // [buffer][query tile of the item]
   uint64_t s_empty[kSBuf];   // 128 arrivals: the statistics group of the item
   uint64_t q_ready[kGroups]; // one phase per work item of the group, 128 arrivals
   uint64_t mma_drain;
   uint32_t tmem_base;
   int abort_flag;
-  int s_tag[kSBuf];          // index of the S item last issued into each buffer
   float red[kGroups][4][kMaxNB];  // per-warp column partials
   float po[kGroups][kMaxNB];      // MAX: bf16 column maxima before normalisation
   float psum[kGroups][4];
@@ -101,33 +100,6 @@ __device__ __forceinline__ void pair_coords(const Params& p, int t, int& qp, int
   ntp = min(kGroups, p.nq - 2 * qp);
 }
 
-// Bounded wait until the MMA thread has issued S item `want` into a buffer.
-// The buffers are shared by the two statistics groups, so the phase parity of
-// s_full alone cannot tell item g from item g - 3 of the other group; the tag
-// can (it is written before the item's MMAs are issued, and only after item
-// g - 3 has been consumed).
-__device__ __forceinline__ bool wait_tag(const int* tag, int want, int32_t* status,
-                                         volatile int* abort_flag) {
-  const volatile int* t = tag;
-  if (*t == want) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (*t == want) return true;
-    if ((it & 63u) == 0u) {
-      if (*abort_flag) return false;
-      if (status != nullptr && *reinterpret_cast<volatile int32_t*>(status) != 0) {
-        *abort_flag = 1;
-        return false;
-      }
-      if (global_timer_ns() - t0 > kWaitNs) {
-        *abort_flag = 1;
-        if (status != nullptr) atomicExch(status, SA_DEV_WAIT_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     block_stats_kernel(const __grid_constant__ CUtensorMap tm_k, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -146,9 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ctl->kv_empty[i], 1);
     }
     for (int i = 0; i < kSBuf; ++i) {
-      mbar_init(&ctl->s_full[i], 1);
+      for (int a = 0; a < kGroups; ++a) mbar_init(&ctl->s_full[i][a], 1);
       mbar_init(&ctl->s_empty[i], kBM);
-      ctl->s_tag[i] = -1;
     }
     for (int a = 0; a < kGroups; ++a) mbar_init(&ctl->q_ready[a], kBM);
     mbar_init(&ctl->mma_drain, 1);
@@ -195,7 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_bf16(kBM, kBN, 0, 0);
       const uint32_t ring_base = smem_u32(ring);
-      int g = 0, gs = 0;          // K tiles consumed, S items issued
+      int stage = 0, buf = 0;     // ring slot of the next K tile, TMEM buffer of the next S
+      uint32_t kv_ph = 0, se_ph = 0;  // phase bits of the ring slot / of the buffer's reuse
       int qc[kGroups] = {0, 0};   // work items started per group (q_ready phases)
       bool ok = true;
       for (int t = blockIdx.x; t < p.pairs && ok; t += gridDim.x) {
@@ -207,32 +179,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         tc_fence_after();
-        for (int it = 0; it < items && ok; ++it, ++g) {
-          const int stage = g % kStages;
-          if (!mbar_wait(&ctl->kv_full[stage], (uint32_t)(g / kStages) & 1u, p.status,
-                         abort_flag)) {
+        for (int it = 0; it < items && ok; ++it) {
+          if (!mbar_wait(&ctl->kv_full[stage], kv_ph, p.status, abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t tile = ring_base + stage * kTileBytes;
-          for (int a = 0; a < ntp; ++a, ++gs) {
-            const int buf = gs % kSBuf;
-            if (!mbar_wait(&ctl->s_empty[buf], ((uint32_t)(gs / kSBuf) & 1u) ^ 1u, p.status,
-                           abort_flag)) {
+          const uint64_t desc0 = make_sdesc_sw128(ring_base + stage * kTileBytes, 16, 1024);
+          for (int a = 0; a < ntp; ++a) {
+            if (!mbar_wait(&ctl->s_empty[buf], se_ph ^ 1u, p.status, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            *reinterpret_cast<volatile int*>(&ctl->s_tag[buf]) = gs;
+            // the start-address field (bits 0-13, 16-byte units) of desc0 plus
+            // the K step's offset: the sum stays below 2^14 in shared memory
 #pragma unroll
-            for (int kk = 0; kk < kHD / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+            for (int kk = 0; kk < kHD / 16; ++kk)
               mma_ts(tmem + buf * 128, tmem + kColQ + a * 64 + kk * 8,
-                     make_sdesc_sw128(tile + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+                     desc0 + (uint64_t)((((kk >> 2) * kBoxBytes) + (kk & 3) * 32) >> 4), idesc,
+                     kk > 0 ? 1u : 0u);
+            mma_commit(&ctl->s_full[buf][a]);
+            if (++buf == kSBuf) {
+              buf = 0;
+              se_ph ^= 1u;
             }
-            mma_commit(&ctl->s_full[buf]);
           }
-          if (ok) mma_commit(&ctl->kv_empty[stage]);
+          if (!ok) break;
+          mma_commit(&ctl->kv_empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            kv_ph ^= 1u;
+          }
         }
       }
       mma_commit(&ctl->mma_drain);
@@ -250,6 +227,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* psum = ctl->psum[grp];
     bool ok = true;
     int gbase = 0;  // index of the work item's first S item in this CTA's sequence
+    // uses of each TMEM buffer by this group's items: the phase parity of
+    // s_full[buf][grp]. A buffer's consecutive uses by this group are separated
+    // by this group's own consumption, so the parity cannot alias.
+    uint32_t uses = 0;  // bit buf: parity of this group's uses of buffer buf
     for (int t = blockIdx.x; t < p.pairs; t += gridDim.x) {
       int qp, h, b, ntp;
       pair_coords(p, t, qp, h, b, ntp);
@@ -286,10 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = gi % kSBuf;
         const int pass = it / p.nk, j = it % p.nk;
         if (ok)
-          ok = __all_sync(0xffffffffu,
-                          wait_tag(&ctl->s_tag[buf], gi, p.status, abort_flag) &&
-                              mbar_wait(&ctl->s_full[buf], (uint32_t)(gi / kSBuf) & 1u, p.status,
-                                        abort_flag));
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf][grp], (uses >> buf) & 1u,
+                                                 p.status, abort_flag));
+        uses ^= 1u << buf;
         if (!ok) continue;
         tc_fence_after();
         uint32_t r[4][32];

@@ -10,8 +10,9 @@
 // Kernel structure (one CTA per query tile, 384 threads):
 //   warp 0       TMA producer: K/V tiles into a 6-slot ring
 //   warp 1       QK issuer (one thread): S = Q K^T
-//   warp 2       TMEM allocator + the tile's kept-block list
-//   warp 3       PV issuer (one thread): O[h] += P[h] V
+//   warp 2       TMEM allocator
+//   warp 3       the tile's kept-block list, then PV issuer (one thread):
+//                O[h] += P[h] V
 //   warps 4-7    softmax stream 0: keys 0-63 of every kept block
 //   warps 8-11   softmax stream 1: keys 64-127 of every kept block
 // Each kept 128-key block is split into two 64-key halves. Stream h owns half
@@ -127,6 +128,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h = blockIdx.y;
   const int b = blockIdx.z;
 
+  // The softmax threads fetch their half row of Q now, so that the global
+  // load overlaps the set-up (stream st: head dims 64st..64st+63, as the 32
+  // columns of bf16 pairs of the QK MMA's A operand). Rows past Sq are 0.
+  uint32_t qv[32];
+  if (warp >= 4) {
+    const int grow = qt * kBM + (warp & 3) * 32 + lane;
+    if (grow < p.Sq) {
+      const uint4* src = reinterpret_cast<const uint4*>(
+          p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2 +
+          ((warp - 4) >> 2) * 64);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const uint4 w = src[v];
+        qv[4 * v] = w.x; qv[4 * v + 1] = w.y; qv[4 * v + 2] = w.z; qv[4 * v + 3] = w.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) qv[e] = 0u;
+    }
+  }
+
   // ---- set-up: barriers, TMEM, kept-block list ----------------------------
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -158,6 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) {
     tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
+  } else if (warp == 3) {
+    // kept-block list (in parallel with the TMEM allocation of warp 2)
     int mh = h;
     bool dense = false;
     if (p.head_mask_type != nullptr) {
@@ -165,12 +189,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t > 0) mh = t - 1; else dense = true;
     }
     const uint8_t* row = p.mask + (int64_t)b * p.ms0 + (int64_t)mh * p.ms1 + (int64_t)qt * p.ms2;
-    int count = 0;
-    for (int c0 = 0; c0 < p.nk; c0 += 32) {
-      const int c = c0 + lane;
+    // All mask bytes of the row are loaded before any is used (one memory
+    // latency instead of one per 32 blocks): bit i of `bits` is block 32 i + lane.
+    const int nw = (p.nk + 31) >> 5;  // <= 32 (nk <= kMaxBlocks)
+    uint32_t bits = 0;
+#pragma unroll 8
+    for (int i = 0; i < nw; ++i) {
+      const int c = i * 32 + lane;
       const bool keep = c < p.nk && (dense || row[(int64_t)c * p.ms3] != 0);
+      bits |= (uint32_t)keep << i;
+    }
+    int count = 0;
+    for (int i = 0; i < nw; ++i) {
+      const bool keep = (bits >> i) & 1u;
       const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-      if (keep) ctl->list[count + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)c;
+      if (keep) ctl->list[count + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(i * 32 + lane);
       count += __popc(bal);
     }
     // the dynamic branch: every pooled-key block, after the kept sink blocks
@@ -288,21 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     bool ok = true;
     if (n > 0) {
-      // Q row -> TMEM: stream st writes head dims 64st..64st+63 (32 columns of
-      // bf16 pairs, the A-operand layout of the QK MMA). Rows past Sq are 0.
-      uint32_t qv[32];
-      if (grow < p.Sq) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2 + st * 64);
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const uint4 w = src[v];
-          qv[4 * v] = w.x; qv[4 * v + 1] = w.y; qv[4 * v + 2] = w.z; qv[4 * v + 3] = w.w;
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) qv[e] = 0u;
-      }
+      // Q half row (loaded before the set-up) -> TMEM
       tmem_st32(tmem + lane_off + kColQ + st * 32, qv);
       tmem_wait_st();
       tc_fence_before();
