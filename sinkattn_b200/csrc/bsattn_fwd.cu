@@ -42,6 +42,8 @@
 
 #include <math.h>
 
+#include <atomic>
+
 #include "sa_common.cuh"
 
 namespace sa {
@@ -52,12 +54,15 @@ constexpr int kBN = 128;      // keys per block
 constexpr int kHalf = 64;     // keys per stream per block
 constexpr int kHD = 128;      // head dim
 constexpr int kStages = 6;    // K/V ring slots
-constexpr int kThreads = 384;  // 4 role warps + 2 softmax warpgroups
+constexpr int kThreads = 512;  // 4 role warps + 2 softmax warpgroups + 1 epilogue warpgroup
 constexpr int kTileBytes = kBM * kHD * 2;   // 32 KB bf16 tile
 constexpr int kBoxBytes = kTileBytes / 2;   // one 64-column box
 constexpr int kHalfRowsBytes = kHalf * 128; // 64 rows of a box: 8 KB
 constexpr int kMaxBlocks = 1024;            // max key blocks per row (S <= 131072)
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+// readers of a kept-block list slot: TMA, QK and PV threads, 256 softmax and
+// 128 epilogue threads
+constexpr int kListReaders = 3 + 256 + 128;
 // TMEM columns
 constexpr uint32_t kColS = 0, kColP = 128, kColQ = 192, kColO = 256;
 
@@ -75,25 +80,40 @@ struct Params {
   int64_t os0, os1, os2;
   float* lse;
   int32_t* status;
+  int tiles;         // nq * H * B
+  int sched;         // tile-counter slot of this launch
 };
+
+// Dynamic tile scheduler: per launch slot, [0] the next tile to hand out and
+// [1] the CTAs that have finished. The last CTA of a launch resets both, so
+// the slot is zero for the next launch that uses it; launches take slots
+// round robin, so concurrent launches on different streams use different
+// slots.
+constexpr int kSchedSlots = 64;
+__device__ int g_sched[kSchedSlots][2];
 
 struct __align__(8) SmemCtl {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t q_ready;      // Q written to TMEM, 256 arrivals
-  uint64_t s_full;       // S of block j computed (commit)
-  uint64_t s_free;       // S of block j copied out by both streams, 256 arrivals
-  uint64_t p_full[2];    // [stream], 128 arrivals per phase
-  uint64_t pv_done[2];   // [stream], committed after each PV
-  uint64_t o_final[2];
-  uint64_t xbar;         // final (max, sum) exchange, 256 arrivals
-  uint64_t mma_drain[2];  // [0] QK issuer, [1] PV issuer
+  uint64_t list_full[2];   // [slot] kept-block list of a tile written, 1 arrival
+  uint64_t list_empty[2];  // [slot] released by every reader, kListReaders arrivals
+  uint64_t q_ready;        // Q of a tile written to TMEM (epilogue group), 128 arrivals
+  uint64_t q_free;         // the last QK of a tile is complete (commit)
+  uint64_t s_full;         // S of a block computed (commit)
+  uint64_t s_free;         // S of a block copied out by both streams, 256 arrivals
+  uint64_t p_full[2];      // [stream], 128 arrivals per phase
+  uint64_t pv_done[2];     // [stream], committed after each PV
+  uint64_t o_final[2];     // [stream], committed after a tile's last PV
+  uint64_t x_ready[2];     // [tile parity] both streams' (max, sum) written, 256 arrivals
+  uint64_t o_free;         // the epilogue has read O of a tile, 128 arrivals
+  uint64_t mma_drain[2];   // [0] QK issuer, [1] PV issuer
   uint32_t tmem_base;
   int abort_flag;
-  int n_blocks;
-  uint16_t list[kMaxBlocks];  // key blocks; bit 15 marks a pooled-key block
-  float xm[2][kBM];
-  float xl[2][kBM];
+  int n_blocks[2];         // [slot]
+  int tile_id[2];          // [slot] tile of the list, -1: no more tiles
+  uint16_t list[2][kMaxBlocks];  // [slot] key blocks; bit 15 marks a pooled-key block
+  float xm[2][2][kBM];     // [tile parity][stream][row]
+  float xl[2][2][kBM];
 };
 
 constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kTileBytes + sizeof(SmemCtl);
@@ -111,6 +131,20 @@ __device__ __forceinline__ void for_each_item(const int n, F&& f) {
   }
 }
 
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& qt, int& h, int& b) {
+  qt = t % p.nq;
+  const int bh = t / p.nq;
+  h = bh % p.H;
+  b = bh / p.H;
+}
+
+// Persistent grid, one CTA per SM. Warp 2 takes the CTA's next tile from the
+// launch's tile counter (tile t = query tile t % nq of head t / nq) and
+// publishes it with its kept-block list, two tiles ahead, in one of two list
+// slots; every role walks that same sequence. The barriers of the per-block
+// pipeline (ring slots, S, P, PV) count blocks over all of the CTA's tiles,
+// so the pipeline runs from one tile into the next without draining; the
+// per-tile barriers count the tiles that have kept blocks.
 __global__ void __launch_bounds__(kThreads, 1)
     bsattn_fwd_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v,
@@ -124,48 +158,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qt = blockIdx.x;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
 
-  // The softmax threads fetch their half row of Q now, so that the global
-  // load overlaps the set-up (stream st: head dims 64st..64st+63, as the 32
-  // columns of bf16 pairs of the QK MMA's A operand). Rows past Sq are 0.
-  uint32_t qv[32];
-  if (warp >= 4) {
-    const int grow = qt * kBM + (warp & 3) * 32 + lane;
-    if (grow < p.Sq) {
-      const uint4* src = reinterpret_cast<const uint4*>(
-          p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2 +
-          ((warp - 4) >> 2) * 64);
-#pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        const uint4 w = src[v];
-        qv[4 * v] = w.x; qv[4 * v + 1] = w.y; qv[4 * v + 2] = w.z; qv[4 * v + 3] = w.w;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) qv[e] = 0u;
-    }
-  }
-
-  // ---- set-up: barriers, TMEM, kept-block list ----------------------------
+  // ---- set-up: barriers, TMEM ----------------------------------------------
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&ctl->kv_full[i], 1);
       mbar_init(&ctl->kv_empty[i], 1);
     }
-    mbar_init(&ctl->q_ready, 2 * kBM);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->list_full[i], 1);
+      mbar_init(&ctl->list_empty[i], kListReaders);
+      mbar_init(&ctl->p_full[i], kBM);
+      mbar_init(&ctl->pv_done[i], 1);
+      mbar_init(&ctl->o_final[i], 1);
+      mbar_init(&ctl->x_ready[i], 2 * kBM);
+      mbar_init(&ctl->mma_drain[i], 1);
+    }
+    mbar_init(&ctl->q_ready, kBM);
+    mbar_init(&ctl->q_free, 1);
     mbar_init(&ctl->s_full, 1);
     mbar_init(&ctl->s_free, 2 * kBM);
-    for (int st = 0; st < 2; ++st) {
-      mbar_init(&ctl->p_full[st], kBM);
-      mbar_init(&ctl->pv_done[st], 1);
-      mbar_init(&ctl->o_final[st], 1);
-    }
-    mbar_init(&ctl->xbar, 2 * kBM);
-    mbar_init(&ctl->mma_drain[0], 1);
-    mbar_init(&ctl->mma_drain[1], 1);
+    mbar_init(&ctl->o_free, kBM);
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
@@ -180,67 +193,115 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) {
     tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
-  } else if (warp == 3) {
-    // kept-block list (in parallel with the TMEM allocation of warp 2)
-    int mh = h;
-    bool dense = false;
-    if (p.head_mask_type != nullptr) {
-      const int t = p.head_mask_type[h];
-      if (t > 0) mh = t - 1; else dense = true;
-    }
-    const uint8_t* row = p.mask + (int64_t)b * p.ms0 + (int64_t)mh * p.ms1 + (int64_t)qt * p.ms2;
-    // All mask bytes of the row are loaded before any is used (one memory
-    // latency instead of one per 32 blocks): bit i of `bits` is block 32 i + lane.
-    const int nw = (p.nk + 31) >> 5;  // <= 32 (nk <= kMaxBlocks)
-    uint32_t bits = 0;
-#pragma unroll 8
-    for (int i = 0; i < nw; ++i) {
-      const int c = i * 32 + lane;
-      const bool keep = c < p.nk && (dense || row[(int64_t)c * p.ms3] != 0);
-      bits |= (uint32_t)keep << i;
-    }
-    int count = 0;
-    for (int i = 0; i < nw; ++i) {
-      const bool keep = (bits >> i) & 1u;
-      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-      if (keep) ctl->list[count + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(i * 32 + lane);
-      count += __popc(bal);
-    }
-    // the dynamic branch: every pooled-key block, after the kept sink blocks
-    for (int t = lane; t < p.nk2; t += 32) ctl->list[count + t] = (uint16_t)(0x8000u | t);
-    count += p.nk2;
-    if (lane == 0) ctl->n_blocks = count;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
   const uint32_t tmem = ctl->tmem_base;
-  const int n = ctl->n_blocks;
   volatile int* abort_flag = &ctl->abort_flag;
 
-  if (warp == 0) {
+  if (warp == 2) {
+    // ---------------- kept-block lists, two tiles ahead ----------------
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int slot = k & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&ctl->list_empty[slot],
+                                             ((uint32_t)(k >> 1) & 1u) ^ 1u, p.status,
+                                             abort_flag));
+      if (!ok) break;
+      // the next tile from the launch's counter (tiles are handed out in
+      // order, so the CTAs work on neighbouring tiles of one head at a time)
+      int t = 0;
+      if (lane == 0) t = atomicAdd(&g_sched[p.sched][0], 1);
+      t = __shfl_sync(0xffffffffu, t, 0);
+      if (t >= p.tiles) {
+        if (lane == 0) {
+          ctl->tile_id[slot] = -1;
+          ctl->n_blocks[slot] = 0;
+          mbar_arrive(&ctl->list_full[slot]);
+        }
+        break;
+      }
+      int qt, h, b;
+      tile_coords(p, t, qt, h, b);
+      int mh = h;
+      bool dense = false;
+      if (p.head_mask_type != nullptr) {
+        const int ty = p.head_mask_type[h];
+        if (ty > 0) mh = ty - 1; else dense = true;
+      }
+      const uint8_t* row =
+          p.mask + (int64_t)b * p.ms0 + (int64_t)mh * p.ms1 + (int64_t)qt * p.ms2;
+      // all mask bytes of the row are loaded before any is used: bit i of
+      // `bits` is block 32 i + lane
+      const int nw = (p.nk + 31) >> 5;  // <= 32 (nk <= kMaxBlocks)
+      uint32_t bits = 0;
+#pragma unroll 8
+      for (int i = 0; i < nw; ++i) {
+        const int c = i * 32 + lane;
+        const bool keep = c < p.nk && (dense || row[(int64_t)c * p.ms3] != 0);
+        bits |= (uint32_t)keep << i;
+      }
+      uint16_t* list = ctl->list[slot];
+      int count = 0;
+      for (int i = 0; i < nw; ++i) {
+        const bool keep = (bits >> i) & 1u;
+        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) list[count + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(i * 32 + lane);
+        count += __popc(bal);
+      }
+      // the dynamic branch: every pooled-key block, after the kept sink blocks
+      for (int u = lane; u < p.nk2; u += 32) list[count + u] = (uint16_t)(0x8000u | u);
+      count += p.nk2;
+      if (lane == 0) {
+        ctl->n_blocks[slot] = count;
+        ctl->tile_id[slot] = t;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->list_full[slot]);
+    }
+  } else if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       int it = 0;
-      for_each_item(n, [&](const int j, const int is_v) -> bool {
-        const int stage = it % kStages;
-        const uint32_t phase = (uint32_t)(it / kStages) & 1u;
-        if (!mbar_wait(&ctl->kv_empty[stage], phase ^ 1u, p.status, abort_flag)) return false;
-        uint8_t* dst = ring + stage * kTileBytes;
-        const uint32_t ent = ctl->list[j];
-        const int kb = (int)(ent & 0x7fffu);
-        const bool pooled = (ent & 0x8000u) != 0;
-        const CUtensorMap* map = is_v ? (pooled ? &tm_v2 : &tm_v) : (pooled ? &tm_k2 : &tm_k);
-        mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
-        tma_load_4d(map, &ctl->kv_full[stage], dst, 0, kb * kBN, h, b);
-        tma_load_4d(map, &ctl->kv_full[stage], dst + kBoxBytes, 64, kb * kBN, h, b);
-        ++it;
-        return true;
-      });
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!mbar_wait(&ctl->list_full[slot], (uint32_t)(k >> 1) & 1u, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int t = ctl->tile_id[slot];
+        if (t < 0) break;
+        int qt, h, b;
+        tile_coords(p, t, qt, h, b);
+        (void)qt;
+        const int n = ctl->n_blocks[slot];
+        const uint16_t* list = ctl->list[slot];
+        for_each_item(n, [&](const int j, const int is_v) -> bool {
+          const int stage = it % kStages;
+          const uint32_t phase = (uint32_t)(it / kStages) & 1u;
+          if (!mbar_wait(&ctl->kv_empty[stage], phase ^ 1u, p.status, abort_flag)) {
+            ok = false;
+            return false;
+          }
+          uint8_t* dst = ring + stage * kTileBytes;
+          const uint32_t ent = list[j];
+          const int kb = (int)(ent & 0x7fffu);
+          const bool pooled = (ent & 0x8000u) != 0;
+          const CUtensorMap* map = is_v ? (pooled ? &tm_v2 : &tm_v) : (pooled ? &tm_k2 : &tm_k);
+          mbar_arrive_expect_tx(&ctl->kv_full[stage], kTileBytes);
+          tma_load_4d(map, &ctl->kv_full[stage], dst, 0, kb * kBN, h, b);
+          tma_load_4d(map, &ctl->kv_full[stage], dst + kBoxBytes, 64, kb * kBN, h, b);
+          ++it;
+          return true;
+        });
+        if (ok) mbar_arrive(&ctl->list_empty[slot]);
+      }
       // Drain: make sure no TMA write is still in flight before the CTA exits.
-      for (int k = (it > kStages ? it - kStages : 0); k < it; ++k)
-        mbar_wait_drain(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u);
+      for (int i = (it > kStages ? it - kStages : 0); i < it; ++i)
+        mbar_wait_drain(&ctl->kv_full[i % kStages], (uint32_t)(i / kStages) & 1u);
     }
     __syncwarp();
   } else if (warp == 1 || warp == 3) {
@@ -248,27 +309,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Both walk the K/V sequence to find the ring stage of each item and
     // take only their own kind (K tiles for QK, V tiles for PV).
     const int role_v = warp == 3 ? 1 : 0;
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_bf16(kBM, kHD, 0, 1);
-      const bool ok = mbar_wait(&ctl->q_ready, 0, p.status, abort_flag);
-      tc_fence_after();
       const uint32_t ring_base = smem_u32(ring);
-      int it = 0;
-      if (ok) {
+      int it = 0;   // ring items walked
+      int jg = 0;   // blocks of earlier tiles
+      int e = 0;    // earlier tiles with kept blocks
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!mbar_wait(&ctl->list_full[slot], (uint32_t)(k >> 1) & 1u, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (ctl->tile_id[slot] < 0) break;
+        const int n = ctl->n_blocks[slot];
+        if (n > 0 && !role_v) {
+          // Q of this tile in TMEM (the epilogue group writes it once the
+          // previous tile's last QK has completed)
+          if (!mbar_wait(&ctl->q_ready, (uint32_t)e & 1u, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
         for_each_item(n, [&](const int j, const int is_v) -> bool {
           if (is_v != role_v) {
             ++it;
             return true;
           }
+          const int J = jg + j;
           const int stage = it % kStages;
           const uint32_t phase = (uint32_t)(it / kStages) & 1u;
-          if (!is_v && j > 0) {
-            // S is single-buffered: both streams have copied S(j-1) out
-            if (!mbar_wait(&ctl->s_free, (uint32_t)(j - 1) & 1u, p.status, abort_flag))
+          if (!is_v && J > 0) {
+            // S is single-buffered: both streams have copied S(J-1) out
+            if (!mbar_wait(&ctl->s_free, (uint32_t)(J - 1) & 1u, p.status, abort_flag)) {
+              ok = false;
               return false;
+            }
           }
-          if (!mbar_wait(&ctl->kv_full[stage], phase, p.status, abort_flag)) return false;
+          if (is_v && j == 0 && e > 0) {
+            // the first PV of a tile overwrites O: the epilogue group has read
+            // the previous tile's O
+            if (!mbar_wait(&ctl->o_free, (uint32_t)(e - 1) & 1u, p.status, abort_flag)) {
+              ok = false;
+              return false;
+            }
+          }
+          if (!mbar_wait(&ctl->kv_full[stage], phase, p.status, abort_flag)) {
+            ok = false;
+            return false;
+          }
           const uint32_t tile = ring_base + stage * kTileBytes;
           if (!is_v) {
             tc_fence_after();
@@ -281,11 +373,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             mma_commit(&ctl->s_full);
             mma_commit(&ctl->kv_empty[stage]);
+            if (j == n - 1) mma_commit(&ctl->q_free);  // Q columns may be rewritten
           } else {
 #pragma unroll
             for (int st = 0; st < 2; ++st) {
-              if (!mbar_wait(&ctl->p_full[st], (uint32_t)j & 1u, p.status, abort_flag))
+              if (!mbar_wait(&ctl->p_full[st], (uint32_t)J & 1u, p.status, abort_flag)) {
+                ok = false;
                 return false;
+              }
               tc_fence_after();
               // O[st] += P[st] (128 x 64, bf16 in TMEM) . V[keys 64st .. 64st+63]
 #pragma unroll
@@ -303,13 +398,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++it;
           return true;
         });
+        if (!ok) break;
+        if (n > 0) {
+          jg += n;
+          ++e;
+        }
+        mbar_arrive(&ctl->list_empty[slot]);
       }
       // Drain every MMA this thread issued before TMEM can be released.
       mma_commit(&ctl->mma_drain[role_v]);
       mbar_wait_drain(&ctl->mma_drain[role_v], 0);
     }
     __syncwarp();
-  } else if (warp >= 4) {
+  } else if (warp < 12) {
     // ---------------- softmax streams ----------------
     // Stream st = 0/1 (warps 4-7 / 8-11) owns keys 64st..64st+63 of every
     // kept block. Thread (warp quarter wq, lane) owns query row wq*32+lane,
@@ -317,156 +418,180 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int st = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
-    const int grow = qt * kBM + row;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     bool ok = true;
-    if (n > 0) {
-      // Q half row (loaded before the set-up) -> TMEM
-      tmem_st32(tmem + lane_off + kColQ + st * 32, qv);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&ctl->q_ready);
-    }
-    float m_used = -INFINITY;
-    float l = 0.f;
-    for (int j = 0; j < n && ok; ++j) {
-      // warp-uniform outcome: the TMEM loads below are warp-collective
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait(&ctl->s_full, (uint32_t)j & 1u, p.status, abort_flag))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t r[2][32];
-      tmem_ld32(tmem + lane_off + kColS + st * kHalf + 0, r[0]);
-      tmem_ld32(tmem + lane_off + kColS + st * kHalf + 32, r[1]);
-      tmem_wait_ld();
-      reg_fence32(r[0]);
-      reg_fence32(r[1]);
-      tc_fence_before();
-      mbar_arrive(&ctl->s_free);  // S may be overwritten by the next QK
-      const uint32_t ent = ctl->list[j];
-      const int kb = (int)(ent & 0x7fffu);
-      const bool pooled = (ent & 0x8000u) != 0;
-      const int valid = min(kHalf, (pooled ? p.Sk2 : p.Sk) - kb * kBN - st * kHalf);
-      const float bias = pooled ? p.bias_log2 : 0.f;
-      if (valid < kHalf) {
-#pragma unroll
-        for (int c = 0; c < kHalf; ++c)
-          if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
-      }
-      // Row maximum over this stream's 64 columns: 8 chains of 3-input max.
-      float mxp[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mxp[t] = __uint_as_float(r[0][t]);
-#pragma unroll
-      for (int c = 8; c + 16 <= kHalf; c += 16) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-          mxp[t] = fmax3(mxp[t], __uint_as_float(r[(c + t) >> 5][(c + t) & 31]),
-                         __uint_as_float(r[(c + 8 + t) >> 5][(c + 8 + t) & 31]));
-      }
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mxp[t] = fmaxf(mxp[t], __uint_as_float(r[1][24 + t]));
-      const float mx_raw = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
-                                 fmaxf(mxp[6], mxp[7]));
-      const float mx = fmaf(mx_raw, p.scale_log2, bias);  // -inf stays -inf
-      float alpha = 1.0f;
-      const bool rescale = mx > m_used + kRescaleThreshold;
-      if (rescale) {
-        alpha = ex2_approx(m_used - mx);  // 0 when m_used = -inf
-        l *= alpha;
-        m_used = mx;
-      }
-      // P = exp2(S*scale*log2e + bias - m); a row that has seen no valid key
-      // yet (m = -inf) gets P = 0 from its -inf inputs.
-      const float negm = m_used == -INFINITY ? 0.f : -m_used;
-      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
-      const uint64_t negm2 = f2_pack(bias + negm, bias + negm);
-      uint64_t lp2[4] = {0ull, 0ull, 0ull, 0ull};
-      uint32_t pk[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int c = 2 * e;
-        const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(r[c >> 5][c & 31]),
-                                           __uint_as_float(r[(c + 1) >> 5][(c + 1) & 31])),
-                                   scale2, negm2);
-        float x0, x1;
-        f2_unpack(x2, x0, x1);
-        const float p0 = ex2_approx(x0);
-        const float p1 = ex2_approx(x1);
-        lp2[e & 3] = f2_add(lp2[e & 3], f2_pack(p0, p1));
-        pk[e] = pack_bf16x2(p0, p1);
-      }
-      {
-        const uint64_t t2 = f2_add(f2_add(lp2[0], lp2[1]), f2_add(lp2[2], lp2[3]));
-        float a0, a1;
-        f2_unpack(t2, a0, a1);
-        l += a0 + a1;
-      }
-      // P[st] and O[st] are free once PV of block j-1 has completed.
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&ctl->pv_done[st], (uint32_t)(j - 1) & 1u,
-                                               p.status, abort_flag))) {
+    int jg = 0, e = 0;
+    for (int k = 0; ok; ++k) {
+      const int slot = k & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&ctl->list_full[slot], (uint32_t)(k >> 1) & 1u,
+                                             p.status, abort_flag));
+      if (!ok) break;
+      if (ctl->tile_id[slot] < 0) break;
+      const int n = ctl->n_blocks[slot];
+      const uint16_t* list = ctl->list[slot];
+      float m_used = -INFINITY;
+      float l = 0.f;
+      for (int j = 0; j < n && ok; ++j) {
+        const int J = jg + j;
+        // warp-uniform outcome: the TMEM loads below are warp-collective
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(&ctl->s_full, (uint32_t)J & 1u, p.status, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-      }
-      tmem_st32(tmem + lane_off + kColP + st * 32, pk);
-      // Rescale O when the maximum moved after the first block. tcgen05.ld/st
-      // are warp-collective (.sync.aligned): the whole warp takes this branch
-      // when any of its rows rescales; other rows use alpha = 1.
-      if (__any_sync(0xffffffffu, rescale && j > 0)) {
-        if (!(rescale && j > 0)) alpha = 1.0f;
-        const uint32_t o_self = tmem + lane_off + kColO + st * 128;
+        uint32_t r[2][32];
+        tmem_ld32(tmem + lane_off + kColS + st * kHalf + 0, r[0]);
+        tmem_ld32(tmem + lane_off + kColS + st * kHalf + 32, r[1]);
+        tmem_wait_ld();
+        reg_fence32(r[0]);
+        reg_fence32(r[1]);
+        tc_fence_before();
+        mbar_arrive(&ctl->s_free);  // S may be overwritten by the next QK
+        const uint32_t ent = list[j];
+        const int kb = (int)(ent & 0x7fffu);
+        const bool pooled = (ent & 0x8000u) != 0;
+        const int valid = min(kHalf, (pooled ? p.Sk2 : p.Sk) - kb * kBN - st * kHalf);
+        const float bias = pooled ? p.bias_log2 : 0.f;
+        if (valid < kHalf) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_self + c * 32, o);
-          tmem_wait_ld();
-          reg_fence32(o);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(o_self + c * 32, o);
+          for (int c = 0; c < kHalf; ++c)
+            if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
         }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&ctl->p_full[st]);
-    }
-    // Epilogue: merge the two streams' (max, sum, O) for each row; stream st
-    // writes output columns 64st..64st+63, stream 0 the LSE.
-    if (ok && n > 0) ok = mbar_wait(&ctl->o_final[st], 0, p.status, abort_flag);
-    float m_oth = -INFINITY, l_oth = 0.f;
-    if (ok && n > 0) {
-      ctl->xm[st][row] = m_used;
-      ctl->xl[st][row] = l;
-      mbar_arrive(&ctl->xbar);
-      ok = mbar_wait(&ctl->xbar, 0, p.status, abort_flag);
-      if (ok) {
-        m_oth = ctl->xm[st ^ 1][row];
-        l_oth = ctl->xl[st ^ 1][row];
-      }
-    }
-    ok = __all_sync(0xffffffffu, ok);  // the O loads below are warp-collective
-    tc_fence_after();
-    const bool write = grow < p.Sq;
-    __nv_bfloat16* orow = p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 +
-                          (int64_t)grow * p.os2 + st * kHalf;
-    if (n > 0 && ok) {
-      const float m = fmaxf(m_used, m_oth);
-      const float a_self = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m);
-      const float a_oth = m_oth == -INFINITY ? 0.f : ex2_approx(m_oth - m);
-      const float L = l * a_self + l_oth * a_oth;
-      const float inv_l = 1.0f / L;
-      const float w0 = (st == 0 ? a_self : a_oth) * inv_l;  // weight of O[0]
-      const float w1 = (st == 0 ? a_oth : a_self) * inv_l;  // weight of O[1]
+        // Row maximum over this stream's 64 columns: 8 chains of 3-input max.
+        float mxp[8];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+        for (int u = 0; u < 8; ++u) mxp[u] = __uint_as_float(r[0][u]);
+#pragma unroll
+        for (int c = 8; c + 16 <= kHalf; c += 16) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            mxp[u] = fmax3(mxp[u], __uint_as_float(r[(c + u) >> 5][(c + u) & 31]),
+                           __uint_as_float(r[(c + 8 + u) >> 5][(c + 8 + u) & 31]));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mxp[u] = fmaxf(mxp[u], __uint_as_float(r[1][24 + u]));
+        const float mx_raw = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                                   fmaxf(mxp[6], mxp[7]));
+        const float mx = fmaf(mx_raw, p.scale_log2, bias);  // -inf stays -inf
+        float alpha = 1.0f;
+        const bool rescale = mx > m_used + kRescaleThreshold;
+        if (rescale) {
+          alpha = ex2_approx(m_used - mx);  // 0 when m_used = -inf
+          l *= alpha;
+          m_used = mx;
+        }
+        // P = exp2(S*scale*log2e + bias - m); a row that has seen no valid key
+        // yet (m = -inf) gets P = 0 from its -inf inputs.
+        const float negm = m_used == -INFINITY ? 0.f : -m_used;
+        const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t negm2 = f2_pack(bias + negm, bias + negm);
+        uint64_t lp2[4] = {0ull, 0ull, 0ull, 0ull};
+        uint32_t pk[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          const int c = 2 * u;
+          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(r[c >> 5][c & 31]),
+                                             __uint_as_float(r[(c + 1) >> 5][(c + 1) & 31])),
+                                     scale2, negm2);
+          float x0, x1;
+          f2_unpack(x2, x0, x1);
+          const float p0 = ex2_approx(x0);
+          const float p1 = ex2_approx(x1);
+          lp2[u & 3] = f2_add(lp2[u & 3], f2_pack(p0, p1));
+          pk[u] = pack_bf16x2(p0, p1);
+        }
+        {
+          const uint64_t t2 = f2_add(f2_add(lp2[0], lp2[1]), f2_add(lp2[2], lp2[3]));
+          float a0, a1;
+          f2_unpack(t2, a0, a1);
+          l += a0 + a1;
+        }
+        // P[st] (and O[st]) are free once the previous PV has completed, which
+        // may belong to the previous tile.
+        if (J > 0) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&ctl->pv_done[st], (uint32_t)(J - 1) & 1u,
+                                                 p.status, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        tmem_st32(tmem + lane_off + kColP + st * 32, pk);
+        // Rescale O when the maximum moved after the tile's first block.
+        // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
+        // takes this branch when any of its rows rescales; other rows use 1.
+        if (__any_sync(0xffffffffu, rescale && j > 0)) {
+          if (!(rescale && j > 0)) alpha = 1.0f;
+          const uint32_t o_self = tmem + lane_off + kColO + st * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_self + c * 32, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int u = 0; u < 32; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * alpha);
+            tmem_st32(o_self + c * 32, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&ctl->p_full[st]);
+      }
+      if (!ok) break;
+      if (n > 0) {
+        // this stream's (max, sum) of the row, for the epilogue group
+        ctl->xm[e & 1][st][row] = m_used;
+        ctl->xl[e & 1][st][row] = l;
+        mbar_arrive(&ctl->x_ready[e & 1]);
+        jg += n;
+        ++e;
+      }
+      mbar_arrive(&ctl->list_empty[slot]);
+    }
+  } else {
+    // ---------------- epilogue group (warps 12-15) ----------------
+    // For each tile with kept blocks: write its Q into TMEM as soon as the
+    // previous tile's last QK has completed, then finish the previous tile
+    // (merge the two streams' max, sum and O; write the output rows and LSE)
+    // while the softmax streams already work on this one.
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    bool ok = true;
+    int e = 0;
+    int prev_t = -1;  // the last tile with kept blocks whose output is pending
+
+    auto finish = [&](const int tp, const int ep) {
+      int qt, h, b;
+      tile_coords(p, tp, qt, h, b);
+      const int grow = qt * kBM + row;
+      if (ok)
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&ctl->o_final[0], (uint32_t)ep & 1u, p.status, abort_flag) &&
+                            mbar_wait(&ctl->o_final[1], (uint32_t)ep & 1u, p.status,
+                                      abort_flag) &&
+                            mbar_wait(&ctl->x_ready[ep & 1], (uint32_t)(ep >> 1) & 1u,
+                                      p.status, abort_flag));
+      if (!ok) return;
+      tc_fence_after();
+      const float m0 = ctl->xm[ep & 1][0][row], m1 = ctl->xm[ep & 1][1][row];
+      const float l0 = ctl->xl[ep & 1][0][row], l1 = ctl->xl[ep & 1][1][row];
+      const float m = fmaxf(m0, m1);
+      const float a0 = m0 == -INFINITY ? 0.f : ex2_approx(m0 - m);
+      const float a1 = m1 == -INFINITY ? 0.f : ex2_approx(m1 - m);
+      const float L = l0 * a0 + l1 * a1;
+      const float inv_l = 1.0f / L;
+      const float w0 = a0 * inv_l, w1 = a1 * inv_l;
+      const bool write = grow < p.Sq;
+      __nv_bfloat16* orow =
+          p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)grow * p.os2;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
         uint32_t o0[32], o1[32];
-        tmem_ld32(tmem + lane_off + kColO + st * kHalf + c * 32, o0);
-        tmem_ld32(tmem + lane_off + kColO + 128 + st * kHalf + c * 32, o1);
+        tmem_ld32(tmem + lane_off + kColO + c * 32, o0);
+        tmem_ld32(tmem + lane_off + kColO + 128 + c * 32, o1);
         tmem_wait_ld();
         reg_fence32(o0);
         reg_fence32(o1);
@@ -476,9 +601,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int v = 0; v < 4; ++v) {
             uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i0 = 8 * v + 2 * e;
-              w[e] = pack_bf16x2(
+            for (int u = 0; u < 4; ++u) {
+              const int i0 = 8 * v + 2 * u;
+              w[u] = pack_bf16x2(
                   fmaf(__uint_as_float(o0[i0]), w0, __uint_as_float(o1[i0]) * w1),
                   fmaf(__uint_as_float(o0[i0 + 1]), w0, __uint_as_float(o1[i0 + 1]) * w1));
             }
@@ -486,19 +611,80 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (write && st == 0 && p.lse != nullptr)
+      tc_fence_before();
+      mbar_arrive(&ctl->o_free);  // O may be overwritten by the next tile's first PV
+      if (write && p.lse != nullptr)
         p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = (m + __log2f(L)) * 0.69314718055994531f;
-    } else if (write) {
-      uint4* dst = reinterpret_cast<uint4*>(orow);
-      for (int v = 0; v < 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
-      if (st == 0 && p.lse != nullptr) p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = -INFINITY;
+    };
+
+    for (int k = 0; ok; ++k) {
+      const int slot = k & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&ctl->list_full[slot], (uint32_t)(k >> 1) & 1u,
+                                             p.status, abort_flag));
+      if (!ok) break;
+      const int t = ctl->tile_id[slot];
+      if (t < 0) break;
+      const int n = ctl->n_blocks[slot];
+      mbar_arrive(&ctl->list_empty[slot]);  // only t and n are needed from the slot
+      int qt, h, b;
+      tile_coords(p, t, qt, h, b);
+      const int grow = qt * kBM + row;
+      if (n == 0) {
+        // no kept block: zero output, LSE -inf
+        if (grow < p.Sq) {
+          uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)b * p.os0 + (int64_t)h * p.os1 +
+                                                (int64_t)grow * p.os2);
+          for (int v = 0; v < 16; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+          if (p.lse != nullptr) p.lse[((int64_t)b * p.H + h) * p.Sq + grow] = -INFINITY;
+        }
+        continue;
+      }
+      // Q row of this tile -> TMEM columns [kColQ, kColQ+64) as bf16 pairs
+      // (the A-operand layout of the QK MMA). Rows past Sq are 0.
+      uint32_t qv[2][32];
+      if (grow < p.Sq) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2);
+#pragma unroll
+        for (int v = 0; v < 16; ++v) {
+          const uint4 w = src[v];
+          qv[v >> 3][4 * (v & 7)] = w.x; qv[v >> 3][4 * (v & 7) + 1] = w.y;
+          qv[v >> 3][4 * (v & 7) + 2] = w.z; qv[v >> 3][4 * (v & 7) + 3] = w.w;
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < 32; ++u) qv[0][u] = qv[1][u] = 0u;
+      }
+      if (e > 0)
+        ok = __all_sync(0xffffffffu, mbar_wait(&ctl->q_free, (uint32_t)(e - 1) & 1u, p.status,
+                                               abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      tmem_st32(tmem + lane_off + kColQ, qv[0]);
+      tmem_st32(tmem + lane_off + kColQ + 32, qv[1]);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&ctl->q_ready);
+      if (prev_t >= 0) finish(prev_t, e - 1);
+      prev_t = t;
+      ++e;
     }
+    if (ok && prev_t >= 0) finish(prev_t, e - 1);
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem, 512);
+  if (threadIdx.x == 0) {
+    // every tile fetch of this CTA is done: the last CTA resets the slot
+    __threadfence();
+    if (atomicAdd(&g_sched[p.sched][1], 1) == (int)gridDim.x - 1) {
+      g_sched[p.sched][0] = 0;
+      g_sched[p.sched][1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 }  // namespace attn
@@ -563,7 +749,7 @@ int launch_attention(const char* fn, const void* q, const void* k, const void* v
                "%s: pooled keys need k2, v2, their strides and Sk2 >= 1", fn);
   SA_CHECK_ARG(nk + nk2 <= kMaxBlocks && nk2 < 0x8000,
                "%s: %d + %d key blocks exceed %d", fn, nk, nk2, kMaxBlocks);
-  SA_CHECK_ARG(B <= 65535 && H <= 65535, "%s: B/H too large", fn);
+  SA_CHECK_ARG((int64_t)nq * H * B <= 0x7fffffff, "%s: too many query tiles", fn);
   SA_CHECK_ARG(strides_ok(q_strides) && strides_ok(k_strides) && strides_ok(v_strides) &&
                    strides_ok(o_strides) && (!dual || (strides_ok(k2_strides) && strides_ok(v2_strides))),
                "%s: q/k/v/out need stride(dim)=1 and other strides multiple of 8 "
@@ -603,6 +789,9 @@ int launch_attention(const char* fn, const void* q, const void* k, const void* v
   p.os0 = o_strides[0]; p.os1 = o_strides[1]; p.os2 = o_strides[2];
   p.lse = lse;
   p.status = status;
+  p.tiles = nq * H * B;
+  static std::atomic<unsigned> launch_seq{0};
+  p.sched = (int)(launch_seq.fetch_add(1, std::memory_order_relaxed) % kSchedSlots);
 
   int dev = 0;
   SA_CUDA_TRY(cudaGetDevice(&dev));
@@ -613,7 +802,9 @@ int launch_attention(const char* fn, const void* q, const void* k, const void* v
                                      (int)kSmemBytes));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  dim3 grid(nq, H, B);
+  // persistent grid: one CTA per SM (at most one per tile)
+  const int sms = sa::sm_count_current_device();
+  const int grid = p.tiles < sms ? p.tiles : sms;
   bsattn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tk, tv, tk2, tv2, p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
