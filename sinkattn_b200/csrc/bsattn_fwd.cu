@@ -7,26 +7,30 @@
 // (sinkattention/sparse_attention.py:735-771): 128x128 blocks, no dropout,
 // not causal, scale 1/sqrt(D) by default.
 //
-// Kernel structure (one CTA per query tile, 384 threads):
+// Kernel structure (persistent: one CTA per SM looping over query tiles
+// taken from a per-launch tile counter, 512 threads):
 //   warp 0       TMA producer: K/V tiles into a 6-slot ring
 //   warp 1       QK issuer (one thread): S = Q K^T
-//   warp 2       TMEM allocator
-//   warp 3       the tile's kept-block list, then PV issuer (one thread):
-//                O[h] += P[h] V
+//   warp 2       TMEM allocator; then fetches the next tiles and builds their
+//                kept-block lists, two tiles ahead
+//   warp 3       PV issuer (one thread): O[h] += P[h] V
 //   warps 4-7    softmax stream 0: keys 0-63 of every kept block
 //   warps 8-11   softmax stream 1: keys 64-127 of every kept block
+//   warps 12-15  epilogue: writes the next tile's Q into TMEM and merges the
+//                finished tile's two (max, sum, O), writing its output rows
 // Each kept 128-key block is split into two 64-key halves. Stream h owns half
 // h of every block with its own running maximum, row sum and O accumulator,
 // so a stream's thread holds one query row and needs no exchange with the
-// other stream until the end, where the two (max, sum, O) are merged.
+// other stream until the end of the tile.
 //
-// Q lives in TMEM (the softmax threads write it there once), so S = Q K^T is
-// a TS MMA that reads only K from shared memory, and shared memory holds
-// nothing but the K/V ring: per block the tensor core reads 64 KB of it and
-// TMA writes 64 KB. P has its own TMEM columns, and QK and PV come from two
-// issuing threads, so QK of block j+1 is issued as soon as both streams have
-// copied S of block j to registers (whatever PV is waiting for), and the next
-// S is computed while the softmax still works on the current one.
+// Q lives in TMEM, so S = Q K^T is a TS MMA that reads only K from shared
+// memory, and shared memory holds nothing but the K/V ring: per block the
+// tensor core reads 64 KB of it and TMA writes 64 KB. P has its own TMEM
+// columns, and QK and PV come from two issuing threads, so QK of block j+1 is
+// issued as soon as both streams have copied S of block j to registers
+// (whatever PV is waiting for), and the next S is computed while the softmax
+// still works on the current one. The same holds across tiles: the next
+// tile's Q is written as soon as the last QK of the current tile completes.
 //
 // TMEM (512 columns x 128 lanes, 32-bit):
 //   S [0,128) (stream h: columns 64h..64h+63)   P[h] [128+32h, 160+32h)
