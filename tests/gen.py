@@ -70,8 +70,8 @@ def cfg1_mask(H: int = 4, nq: int = 32, nk: int = 32, seed: int = 1, p: float = 
     return m
 
 
-def cfg1_inputs(device="cpu", dtype=torch.bfloat16, B=1, H=4, S=4096, D=128):
-    g = torch.Generator(device="cpu").manual_seed(0)
+def cfg1_inputs(device="cpu", dtype=torch.bfloat16, B=1, H=4, S=4096, D=128, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(int(seed))
     q = torch.randn(B, H, S, D, generator=g)
     k = torch.randn(B, H, S, D, generator=g)
     v = torch.randn(B, H, S, D, generator=g)

@@ -120,6 +120,69 @@ def test_deterministic():
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
 
 
+def test_tile_counter_slots_reused_across_launches():
+    """The persistent kernel hands out query tiles from a per-launch counter
+    slot that its last CTA resets; launches take the 64 slots round robin.
+    150 launches of alternating shapes (fewer and more tiles than SMs) reuse
+    every slot and must each reproduce their first result bit for bit."""
+    from sinkattn_b200 import ops
+
+    cases = [cfg1_inputs(device="cuda", H=2, S=640), cfg1_inputs(device="cuda", H=12, S=4096)]
+    first = [ops.bsattn_fwd(*c) for c in cases]
+    for i in range(150):
+        o, l = ops.bsattn_fwd(*cases[i % 2])
+        o0, l0 = first[i % 2]
+        assert torch.equal(o, o0) and torch.equal(l, l0), i
+    torch.cuda.synchronize()
+
+
+def test_concurrent_launches_on_two_streams():
+    """Launches in flight on two streams use different counter slots and do
+    not take each other's tiles."""
+    from sinkattn_b200 import ops
+
+    a = cfg1_inputs(device="cuda", H=6, S=4096, seed=3)
+    b = cfg1_inputs(device="cuda", H=6, S=4096, seed=4)
+    ref_a, ref_b = ops.bsattn_fwd(*a), ops.bsattn_fwd(*b)
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = []
+    for _ in range(8):
+        with torch.cuda.stream(s1):
+            oa = ops.bsattn_fwd(*a)
+        with torch.cuda.stream(s2):
+            ob = ops.bsattn_fwd(*b)
+        outs.append((oa, ob))
+    torch.cuda.synchronize()
+    for oa, ob in outs:
+        assert torch.equal(oa[0], ref_a[0]) and torch.equal(oa[1], ref_a[1])
+        assert torch.equal(ob[0], ref_b[0]) and torch.equal(ob[1], ref_b[1])
+
+
+def test_many_tiles_with_empty_tiles_interleaved(oracle):
+    """More query tiles than SMs, with whole tiles (no kept block) scattered
+    between kept ones: the epilogue warpgroup writes zeros and -inf for the
+    empty tiles and still finishes every kept tile."""
+    from sinkattn_b200 import ops
+
+    q, k, v, mask = cfg1_inputs(device="cuda", H=4, S=8192, seed=7)
+    mask = mask.clone()
+    g = torch.Generator().manual_seed(11)
+    empty = torch.rand(mask.shape[:3], generator=g) < 0.3
+    mask[empty.to(mask.device)] = False
+    out, lse = ops.bsattn_fwd(q, k, v, mask)
+    torch.cuda.synchronize()
+    for h in (0, 3):
+        ref, ref_lse = oracle.dense_masked_attention(_np(q[:, h:h + 1]), _np(k[:, h:h + 1]),
+                                                     _np(v[:, h:h + 1]),
+                                                     mask[:, h:h + 1].cpu().numpy())
+        kept = ~empty[0, h].repeat_interleave(128)[:8192].numpy()
+        kept_t = torch.from_numpy(kept).cuda()
+        _check(out[:, h:h + 1][:, :, kept_t], ref[:, :, kept], f"head {h} kept rows")
+        assert torch.all(out[0, h][~kept_t] == 0)
+        assert torch.all(torch.isneginf(lse[0, h][~kept_t]))
+
+
 def test_empty_rows_give_zero_and_neg_inf():
     from sinkattn_b200 import ops
 
