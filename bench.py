@@ -701,6 +701,69 @@ def run_case(args):
     return 0
 
 
+def run_ulysses(args):
+    """The attention layer of the full-DiT config under sequence parallelism:
+    each rank holds a [B, S/P, H, D] shard of the Wan-shape Q/K/V, an
+    all-to-all turns them into whole-sequence (b, h) units, the kernel runs
+    on them and a second all-to-all returns the output (and LSE). Timed with
+    the exchange in one group (chunks=1) and overlapped with the kernel in
+    groups of units (chunks=C), next to the kernel alone on the rank's units.
+    Launch under torchrun with >= 2 processes."""
+    world, rank, local = dist_env()
+    if world < 2:
+        print(json.dumps({"case": "ulysses", "unavailable": "needs torchrun with >= 2 ranks"}))
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_dist(world, "nccl", dev)
+    from sinkattn_b200.sharding import (_local_units_attention, sequence_to_units,
+                                        ulysses_sink_attention, units_per_rank)
+    from tests.gen import cfg1_mask, wan_qk
+
+    q, k, v = wan_qk(seed=0, dtype=torch.bfloat16, device=dev)  # [B, H, S, D]
+    Sr = S // world
+    sl = slice(rank * Sr, (rank + 1) * Sr)
+    qs, ks, vs = (x.permute(0, 2, 1, 3)[:, sl].contiguous() for x in (q, k, v))
+    del q, k, v
+    mask = cfg1_mask(H, NB, NB, seed=1).unsqueeze(0).expand(B, -1, -1, -1).contiguous().to(dev)
+    n_per = units_per_rank(B * H, world)
+    stream = torch.cuda.current_stream(dev)
+    res = {"case": "ulysses", "n_gpus": world, "units_per_rank": n_per,
+           "exchange_mb_per_rank": 4 * B * Sr * H * D * 2 * (world - 1) / world / 1e6}
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        total, _ = time_steps(fn, args.steps, stream)
+        barrier(world)
+        return max_over_ranks(total / args.steps, world, dev)
+
+    res["ms_layer"] = {}
+    for chunks in sorted({1, min(3, n_per), n_per}):
+        res["ms_layer"][chunks] = timed(
+            lambda: ulysses_sink_attention(qs, ks, vs, mask, chunks=chunks))
+    # the kernel alone on this rank's units (inputs already exchanged)
+    units = [sequence_to_units(x) for x in (qs, ks, vs)]
+    m = mask.reshape(B * H, NB, NB)
+    ids = [rank * n_per + i for i in range(n_per)]
+    mu = torch.stack([m[i] if i < B * H else torch.ones_like(m[0]) for i in ids]).contiguous()
+    res["ms_attention_only"] = timed(lambda: _local_units_attention(*units, mu, ops_attn))
+    if rank == 0:
+        print(json.dumps(res))
+    import torch.distributed as dist
+
+    dist.destroy_process_group()
+    return 0
+
+
+def ops_attn(q, k, v, m):
+    from sinkattn_b200 import ops
+
+    return ops.bsattn_fwd(q, k, v, m)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -712,10 +775,12 @@ def main(argv=None):
                     help="heads per host<->device chunk of the end-to-end leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
                                        "calib-pass", "wan-runtime", "stats-wan", "stats-small",
-                                       "qkrope-wan"],
+                                       "qkrope-wan", "ulysses"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)
+    if args.case == "ulysses":
+        return run_ulysses(args)
     if args.case:
         return run_case(args)
     if args.impl == "reference":

@@ -48,9 +48,12 @@ def _worker(rank, world, port, result_dir):
         Sr = S // world
         sl = slice(rank * Sr, (rank + 1) * Sr)
         dev = torch.device("cuda", rank)
-        out, lse = ulysses_sink_attention(q[:, sl].to(dev).contiguous(), k[:, sl].to(dev).contiguous(),
-                                          v[:, sl].to(dev).contiguous(), mask.to(dev))
+        qs, ks, vs = (x[:, sl].to(dev).contiguous() for x in (q, k, v))
+        out, lse = ulysses_sink_attention(qs, ks, vs, mask.to(dev))
+        # grouped exchange overlapped with the kernel on a second stream
+        out3, lse3 = ulysses_sink_attention(qs, ks, vs, mask.to(dev), chunks=3)
         torch.cuda.synchronize()
+        assert torch.equal(out3, out) and torch.equal(lse3, lse)
         torch.save({"out": out.cpu(), "lse": lse.cpu()}, os.path.join(result_dir, f"r{rank}.pt"))
         dist.barrier()
     finally:

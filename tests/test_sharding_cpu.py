@@ -79,8 +79,21 @@ def _worker(rank, world, port, result_dir):
         u = sequence_to_units(q[:, sl].contiguous())
         back = units_to_sequence(u, B, H)
         assert torch.equal(back, q[:, sl])
+        # sub-ranges of each rank's units round-trip into a shared output
+        n_per = -(-(B * H) // world)
+        part = torch.zeros_like(q[:, sl])
+        for c0, c1 in ((0, 1), (1, n_per)) if n_per > 1 else ((0, 1),):
+            units_to_sequence(sequence_to_units(q[:, sl].contiguous(), units=(c0, c1)), B, H,
+                              units=(c0, c1), out=part)
+        assert torch.equal(part, q[:, sl])
         out, lse = ulysses_sink_attention(q[:, sl].contiguous(), k[:, sl].contiguous(),
                                           v[:, sl].contiguous(), mask, attn_fn=_oracle_attn)
+        # grouped exchange (the overlapped form on GPUs) gives the same result
+        for chunks in (2, 3):
+            o2, l2 = ulysses_sink_attention(q[:, sl].contiguous(), k[:, sl].contiguous(),
+                                            v[:, sl].contiguous(), mask, attn_fn=_oracle_attn,
+                                            chunks=chunks)
+            assert torch.equal(o2, out) and torch.equal(l2, lse), chunks
         np.save(os.path.join(result_dir, f"out{rank}.npy"), out.numpy())
         np.save(os.path.join(result_dir, f"lse{rank}.npy"), lse.numpy())
     finally:
