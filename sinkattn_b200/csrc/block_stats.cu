@@ -24,14 +24,19 @@
 // of one head: every K tile brought into shared memory serves both query
 // tiles, which halves the L2 -> shared-memory traffic per MMA. 384 threads:
 //   warp 0      TMA producer: K tiles into a 5-slot ring
-//   warp 1      MMA issuer: S = Q_a K^T (Q_a from TMEM, K from shared memory)
-//               for a = 0, 1, into 3 TMEM buffers used round robin
+//   warp 1      MMA issuer of query tile 0: S = Q_0 K^T (Q_0 from TMEM, K
+//               from shared memory) into its two TMEM buffers in turn
+//   warp 3      MMA issuer of query tile 1, into its one TMEM buffer
+//               (two issuing threads halve the per-MMA-group waits and
+//               commits that a single thread serialises)
 //   warp 2      TMEM allocator
 //   warps 4-7   statistics of query tile 0 (thread t owns query row t)
 //   warps 8-11  statistics of query tile 1
-//   Each statistics group writes its tile's Q into TMEM.
-// TMEM: S buffers [0,384), Q_0 [384,448), Q_1 [448,512) (bf16 pairs, the
-// A-operand layout). Each CTA owns one scratch slot of 2 x nk x 128 fp32
+//   Each statistics group writes its tile's Q into TMEM. Every K tile is
+//   released by both issuers (by a commit after its MMAs, or an arrival when
+//   the work item has no second tile).
+// TMEM: S buffers [0,128) and [256,384) of tile 0, [128,256) of tile 1;
+// Q_0 [384,448), Q_1 [448,512) (bf16 pairs, the A-operand layout). Each CTA owns one scratch slot of 2 x nk x 128 fp32
 // values (block masses, or the bf16-rounded block maxima), written with one
 // coalesced store per block.
 
@@ -44,7 +49,7 @@ namespace stats {
 
 constexpr int kBM = 128, kBN = 128, kHD = 128;
 constexpr int kStages = 5;
-constexpr int kSBuf = 3;
+constexpr int kSBuf = 3;  // TMEM S buffers of 128 columns
 constexpr int kGroups = 2;  // query tiles per work item
 constexpr int kThreads = 128 + kGroups * 128;
 constexpr int kTileBytes = kBN * kHD * 2;
@@ -67,8 +72,8 @@ struct Params {
 struct __align__(8) SmemCtl {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[kSBuf][kGroups];  // [buffer][query tile of the item]
-  uint64_t s_empty[kSBuf];   // 128 arrivals: the statistics group of the item
+  uint64_t s_full[kSBuf];   // per TMEM buffer; each buffer belongs to one query tile
+  uint64_t s_empty[kSBuf];  // 128 arrivals: the statistics group that owns the buffer
   uint64_t q_ready[kGroups]; // one phase per work item of the group, 128 arrivals
   uint64_t mma_drain;
   uint32_t tmem_base;
@@ -100,6 +105,12 @@ __device__ __forceinline__ void pair_coords(const Params& p, int t, int& qp, int
   ntp = min(kGroups, p.nq - 2 * qp);
 }
 
+
+// TMEM S buffers of query tile a: tile 0 owns two of them, tile 1 one.
+constexpr int kNB0 = 2;
+__device__ __forceinline__ int nbuf_of(int a) { return a == 0 ? kNB0 : 1; }
+// physical buffer (columns [128 id, 128 id + 128)) of tile a's i-th buffer
+__device__ __forceinline__ int buf_id(int a, int i) { return a == 0 ? (i == 0 ? 0 : 2) : 1; }
 __global__ void __launch_bounds__(kThreads, 1)
     block_stats_kernel(const __grid_constant__ CUtensorMap tm_k, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -115,14 +126,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&ctl->kv_full[i], 1);
-      mbar_init(&ctl->kv_empty[i], 1);
+      mbar_init(&ctl->kv_empty[i], kGroups);  // one release per issuer
     }
     for (int i = 0; i < kSBuf; ++i) {
-      for (int a = 0; a < kGroups; ++a) mbar_init(&ctl->s_full[i][a], 1);
+      mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->s_empty[i], kBM);
     }
     for (int a = 0; a < kGroups; ++a) mbar_init(&ctl->q_ready[a], kBM);
-    mbar_init(&ctl->mma_drain, 1);
+    mbar_init(&ctl->mma_drain, kGroups);  // both issuers' MMAs
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
@@ -162,50 +173,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_drain(&ctl->kv_full[k % kStages], (uint32_t)(k / kStages) & 1u);
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 3) {
+    // one MMA issuer per query tile: warp 1 tile 0, warp 3 tile 1
+    const int ta = warp == 3 ? 1 : 0;
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_bf16(kBM, kBN, 0, 0);
       const uint32_t ring_base = smem_u32(ring);
-      int stage = 0, buf = 0;     // ring slot of the next K tile, TMEM buffer of the next S
-      uint32_t kv_ph = 0, se_ph = 0;  // phase bits of the ring slot / of the buffer's reuse
-      int qc[kGroups] = {0, 0};   // work items started per group (q_ready phases)
+      const int nb = nbuf_of(ta);
+      int stage = 0, bi = 0;
+      uint32_t kv_ph = 0, se_ph = 0;
+      int qc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.pairs && ok; t += gridDim.x) {
         int qp, h, b, ntp;
         pair_coords(p, t, qp, h, b, ntp);
-        for (int a = 0; a < ntp && ok; ++a) {
-          ok = mbar_wait(&ctl->q_ready[a], (uint32_t)qc[a] & 1u, p.status, abort_flag);
-          ++qc[a];
+        const bool mine = ta < ntp;
+        if (mine) {
+          ok = mbar_wait(&ctl->q_ready[ta], (uint32_t)qc & 1u, p.status, abort_flag);
+          ++qc;
+          if (!ok) break;
+          tc_fence_after();
         }
-        if (!ok) break;
-        tc_fence_after();
         for (int it = 0; it < items && ok; ++it) {
           if (!mbar_wait(&ctl->kv_full[stage], kv_ph, p.status, abort_flag)) {
             ok = false;
             break;
           }
-          const uint64_t desc0 = make_sdesc_sw128(ring_base + stage * kTileBytes, 16, 1024);
-          for (int a = 0; a < ntp; ++a) {
+          if (mine) {
+            const int buf = buf_id(ta, bi);
             if (!mbar_wait(&ctl->s_empty[buf], se_ph ^ 1u, p.status, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            // the start-address field (bits 0-13, 16-byte units) of desc0 plus
-            // the K step's offset: the sum stays below 2^14 in shared memory
+            const uint64_t desc0 = make_sdesc_sw128(ring_base + stage * kTileBytes, 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < kHD / 16; ++kk)
-              mma_ts(tmem + buf * 128, tmem + kColQ + a * 64 + kk * 8,
+              mma_ts(tmem + buf * 128, tmem + kColQ + ta * 64 + kk * 8,
                      desc0 + (uint64_t)((((kk >> 2) * kBoxBytes) + (kk & 3) * 32) >> 4), idesc,
                      kk > 0 ? 1u : 0u);
-            mma_commit(&ctl->s_full[buf][a]);
-            if (++buf == kSBuf) {
-              buf = 0;
+            mma_commit(&ctl->s_full[buf]);
+            mma_commit(&ctl->kv_empty[stage]);
+            if (++bi == nb) {
+              bi = 0;
               se_ph ^= 1u;
             }
+          } else {
+            mbar_arrive(&ctl->kv_empty[stage]);  // this issuer does not read the tile
           }
-          if (!ok) break;
-          mma_commit(&ctl->kv_empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             kv_ph ^= 1u;
@@ -226,18 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* po_s = ctl->po[grp];
     float* psum = ctl->psum[grp];
     bool ok = true;
-    int gbase = 0;  // index of the work item's first S item in this CTA's sequence
-    // uses of each TMEM buffer by this group's items: the phase parity of
-    // s_full[buf][grp]. A buffer's consecutive uses by this group are separated
-    // by this group's own consumption, so the parity cannot alias.
-    uint32_t uses = 0;  // bit buf: parity of this group's uses of buffer buf
+    // S items this group has consumed: its buffers are used round robin, and
+    // a buffer is refilled only after this group has released it, so the
+    // phase parity of s_full[buf] cannot alias.
+    int cnt = 0;
     for (int t = blockIdx.x; t < p.pairs; t += gridDim.x) {
       int qp, h, b, ntp;
       pair_coords(p, t, qp, h, b, ntp);
-      if (grp >= ntp) {
-        gbase += items * ntp;
-        continue;
-      }
+      if (grp >= ntp) continue;
       const int qb = 2 * qp + grp;
       const int grow = qb * kBM + row;
       const bool row_valid = grow < p.S;
@@ -263,13 +274,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float m = -INFINITY, l = 0.f;
       for (int it = 0; it < items; ++it) {
-        const int gi = gbase + it * ntp + grp;
-        const int buf = gi % kSBuf;
+        const int nbg = nbuf_of(grp);
+        const int buf = buf_id(grp, cnt % nbg);
+        const uint32_t sph = (uint32_t)(cnt / nbg) & 1u;
+        ++cnt;
         const int pass = it / p.nk, j = it % p.nk;
         if (ok)
-          ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf][grp], (uses >> buf) & 1u,
-                                                 p.status, abort_flag));
-        uses ^= 1u << buf;
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf], sph, p.status, abort_flag));
         if (!ok) continue;
         tc_fence_after();
         uint32_t r[4][32];
@@ -322,7 +333,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         l += mass;
         slot[(int64_t)j * kBM + row] = mass;
       }
-      gbase += items * ntp;
       __syncwarp();
       float* out = p.scores + ((int64_t)(b * p.H + h) * p.nq + qb) * p.nk;
       if (p.mode == kExact) {
