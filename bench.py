@@ -636,6 +636,37 @@ def run_case(args):
         print(json.dumps({"case": args.case, "ms": ms, "bytes": nbytes,
                           "gbs": nbytes / (ms / 1e3) / 1e9}))
         return 0
+    if args.case == "zimage":
+        # cfg4 (Z-Image 2048x2048): B=1, H=30, 16384 image + 512 text tokens = 132 blocks;
+        # text rows and columns forced dense as the Z-Image processor does
+        from tests.gen import zimg_qkv
+
+        q, k, v = zimg_qkv(seed=0, device=dev)
+        _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True)
+        cov, _ = ops.coverage_mask(bm, force_sink_col=True)
+        nbz = cov.shape[-1]
+        t0 = nbz - 4
+
+        def with_text(m):
+            m = m.clone()
+            m[:, :, t0:] = True
+            m[:, t0:, :] = True
+            return m.unsqueeze(0).contiguous()
+
+        masks = {"coverage_rule": with_text(cov),
+                 "bernoulli_0.2": with_text(cfg1_mask(30, nbz, nbz, seed=1).to(dev))}
+        res = {"case": args.case, "B": 1, "H": 30, "S": int(q.shape[2])}
+        for name, m in masks.items():
+            fn = lambda: ops.bsattn_fwd(q, k, v, m)  # noqa: E731
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            total, _ = time_steps(fn, args.steps, torch.cuda.current_stream(dev))
+            ms = total / args.steps
+            res[name] = {"density": float(m.float().mean().item()), "ms": ms,
+                         "tflops": kept_flops(m) / (ms / 1e3) / 1e12}
+        print(json.dumps(res))
+        return 0
     if args.case in ("stats-wan", "stats-small"):
         # the exact and max block-statistics modes (dense Q K^T on the tensor cores)
         Bc, Hc = (B, H) if args.case == "stats-wan" else (1, 2)
@@ -775,7 +806,7 @@ def main(argv=None):
                     help="heads per host<->device chunk of the end-to-end leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
                                        "calib-pass", "wan-runtime", "stats-wan", "stats-small",
-                                       "qkrope-wan", "ulysses"],
+                                       "qkrope-wan", "ulysses", "zimage"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)
