@@ -514,7 +514,9 @@ def run_ours(args):
                               "gbs": calib_bytes * world / (tcal / args.steps / 1e3) / 1e9,
                               "frac_of_hbm": calib_bytes / (tcal / args.steps / 1e3) / 1e9
                               / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
-                              "note": "one layer per rank; bytes and gbs whole-job, frac per GPU"},
+                              "note": "one layer per rank (pool -> pooled softmax -> batch mean "
+                                      "-> coverage mask); pool_scores_ms: the first three "
+                                      "alone; bytes and gbs whole-job, frac per GPU"},
         "calibration_pass_30_layers": {
             "ms_per_pass": pass_ms, "ms_per_layer": pass_ms / 30,
             "bytes_per_pass": pass_bytes * world,

@@ -378,16 +378,19 @@ def calibration_pass(
     want_batch_mean: bool = False,
     masks_out: Optional[torch.Tensor] = None,
     chunk: int = 3,
+    head_groups: int = 1,
 ):
     """Pooling + pooled softmax + batch mean + coverage mask for a sequence of
     layers, each given as a (q, k) pair of bf16 [B,H,S,D] CUDA tensors.
 
-    The layers go in chunks: every layer of a chunk is pooled back to back on
-    one side stream (HBM-bound, one persistent TMA kernel per layer), then the
-    chunk's pooled softmax and per-layer batch means (two launches for the
-    whole chunk) and its coverage masks (one launch) run on a second side
-    stream while the next chunk pools. The result is ordered on the caller's
-    current stream. Returns (masks bool [L,H,nb,nb], batch means fp32
+    The work goes in units of (layer, group of H/head_groups heads) and the
+    units in chunks of `chunk`: every unit of a chunk is pooled back to back
+    on one side stream (HBM-bound, one persistent TMA kernel per unit), then
+    the chunk's pooled softmax and batch means (two launches for the whole
+    chunk) and its coverage masks (one launch) run on a second side stream
+    while the next chunk pools. head_groups > 1 lets a single layer overlap
+    its own pooling with its scores and masks. The result is ordered on the
+    caller's current stream. Returns (masks bool [L,H,nb,nb], batch means fp32
     [L,H,nb,nb] or None)."""
     layers = list(layers)
     if not layers:
@@ -397,7 +400,12 @@ def calibration_pass(
     B, H, S, D = q0.shape
     nb = math.ceil(S / block)
     L = len(layers)
-    C = max(1, min(int(chunk), L))
+    G = max(1, int(head_groups))
+    if H % G:
+        raise ValueError(f"head_groups ({G}) must divide the {H} heads")
+    hg = H // G
+    U = L * G  # units (layer, head group), in layer-major order
+    C = max(1, min(int(chunk), U))
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     if idx not in _PASS_STREAMS:
         _PASS_STREAMS[idx] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
@@ -406,35 +414,40 @@ def calibration_pass(
     masks = masks_out if masks_out is not None else torch.empty(
         (L, H, nb, nb), dtype=torch.bool, device=dev)
     bmeans = torch.empty((L, H, nb, nb), dtype=torch.float32, device=dev) if want_batch_mean \
-        else torch.empty((2, C, H, nb, nb), dtype=torch.float32, device=dev)
-    qp = torch.empty((2, C, B, H, nb, D), dtype=torch.float32, device=dev)
-    kp = torch.empty((2, C, B, H, nb, D), dtype=torch.float32, device=dev)
-    logits = torch.empty(C * B * H * nb * nb, dtype=torch.float32, device=dev)
+        else torch.empty((2, C, hg, nb, nb), dtype=torch.float32, device=dev)
+    qp = torch.empty((2, C, B, hg, nb, D), dtype=torch.float32, device=dev)
+    kp = torch.empty((2, C, B, hg, nb, D), dtype=torch.float32, device=dev)
+    logits = torch.empty(C * B * hg * nb * nb, dtype=torch.float32, device=dev)
     pooled = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
+    # unit u covers rows [u*hg, (u+1)*hg) of the flattened [L*H] head rows
+    mask_rows = masks.view(L * H, nb, nb)
     sp.wait_stream(cur)
     sc.wait_stream(cur)
-    for ci, l0 in enumerate(range(0, L, C)):
-        l1 = min(L, l0 + C)
-        n = l1 - l0
+    for ci, u0 in enumerate(range(0, U, C)):
+        u1 = min(U, u0 + C)
+        n = u1 - u0
         buf = ci % 2
         with torch.cuda.stream(sp):
             if ci >= 2:
                 sp.wait_event(consumed[buf])
-            for l in range(l0, l1):
+            for u in range(u0, u1):
+                l, g = divmod(u, G)
                 q, k = layers[l]
                 if q.shape != (B, H, S, D) or k.shape != (B, H, S, D):
                     raise ValueError("all layers must share one [B,H,S,D] shape")
-                pool_means(q, k, block, qp=qp[buf, l - l0], kp=kp[buf, l - l0])
+                hs = slice(g * hg, (g + 1) * hg)
+                pool_means(q[:, hs], k[:, hs], block, qp=qp[buf, u - u0], kp=kp[buf, u - u0])
             pooled[buf].record(sp)
         with torch.cuda.stream(sc):
             sc.wait_event(pooled[buf])
-            bm = bmeans[l0:l1] if want_batch_mean else bmeans[buf, :n]
+            bm = (bmeans.view(L * H, nb, nb)[u0 * hg:u1 * hg].view(n, hg, nb, nb)
+                  if want_batch_mean else bmeans[buf, :n])
             pooled_softmax_layers(qp[buf, :n], kp[buf, :n], batch_means_out=bm, logits_ws=logits)
             consumed[buf].record(sc)
-            coverage_mask(bm.reshape(n * H, nb, nb), coverage=coverage, keep_diagonal=keep_diagonal,
+            coverage_mask(bm.reshape(n * hg, nb, nb), coverage=coverage, keep_diagonal=keep_diagonal,
                           text_blocks=text_blocks, mode=mode, force_sink_col=force_sink_col,
-                          out=masks[l0:l1].view(n * H, nb, nb))
+                          out=mask_rows[u0 * hg:u1 * hg])
     cur.wait_stream(sp)
     cur.wait_stream(sc)
     for t in (qp, kp, logits, bmeans, masks):

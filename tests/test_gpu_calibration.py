@@ -197,10 +197,11 @@ def test_mix_outputs(oracle):
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
 
 
-@pytest.mark.parametrize("chunk", [1, 2, 10])
-def test_calibration_pass_matches_serial_chain(chunk):
+@pytest.mark.parametrize("chunk,head_groups", [(1, 1), (2, 1), (10, 1), (2, 3), (4, 3)])
+def test_calibration_pass_matches_serial_chain(chunk, head_groups):
     """The chunked, two-stream pass over layers (stacked pooled softmax and one
-    mask launch per chunk) gives exactly the per-layer serial results."""
+    mask launch per chunk), also with layers split into head groups, gives
+    exactly the per-layer serial results."""
     from sinkattn_b200 import ops
 
     g = torch.Generator().manual_seed(8)
@@ -210,7 +211,7 @@ def test_calibration_pass_matches_serial_chain(chunk):
         k = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
         layers.append((q, k))
     masks, bms = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True,
-                                      chunk=chunk)
+                                      chunk=chunk, head_groups=head_groups)
     torch.cuda.synchronize()
     for l, (q, k) in enumerate(layers):
         _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True)
