@@ -87,6 +87,12 @@ SA_API int sa_device_sm_count(void);
  * softmax_scale: <= 0 selects 1/sqrt(D).
  * lse: nullable fp32 [B,H,Sq] contiguous, natural-log logsumexp per row. Rows
  *   whose mask row keeps no block produce out = 0 and lse = -inf.
+ * status: nullable device int32, set to SA_DEV_WAIT_TIMEOUT if a bounded wait
+ *   in the kernel gave up.
+ * The launch is a persistent grid (one CTA per SM) that takes query tiles from
+ *   a tile counter inside the library: 64 counter slots per device, handed to
+ *   launches round robin and reset by each launch's last CTA, so up to 64
+ *   launches may be in flight on one device.
  */
 SA_API int sa_bsattn_fwd(const void* q, const void* k, const void* v,
                   const int64_t q_strides[4], const int64_t k_strides[4],
@@ -203,11 +209,13 @@ SA_API int sa_pool_scores_noalloc(const void* q, const void* k,
  *   (sinkattention/pooling_kernel.py:194-248, selected by pooling_mode "triton"
  *   at sparse_attention.py:124-134): per row the bf16 maxima of the scaled
  *   logits of every key block, Po = bf16(max over the block's rows of
- *   exp2(R - row max)), then Po / sum(Po) rounded like bf16 tensors. S must be
- *   a multiple of 128 in this mode.
+ *   exp2(R - row max)), then Po / sum(Po) rounded like bf16 tensors. For S not
+ *   a multiple of 128, keys past S are masked and rows past S take no part in
+ *   the column maxima (the Triton kernel reads past the head there).
  * q, k: bf16 [B,H,S,D] strided, D = 128. scores: fp32 [B,H,nb,nb] contiguous.
- * workspace: sa_block_stats_workspace_size() bytes (MAX mode only; NULL/0
- * otherwise). softmax_scale <= 0 selects 1/sqrt(D). status: as sa_bsattn_fwd.
+ * workspace: sa_block_stats_workspace_size() bytes, both modes (per-CTA
+ * scratch of the persistent kernel). softmax_scale <= 0 selects 1/sqrt(D).
+ * status: as sa_bsattn_fwd.
  */
 #define SA_STATS_EXACT 0
 #define SA_STATS_MAX 1
