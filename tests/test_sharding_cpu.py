@@ -122,3 +122,15 @@ def test_ulysses_exchange_matches_full_attention(tmp_path, world, oracle):
         np.testing.assert_allclose(out, ref.transpose(0, 2, 1, 3)[:, r * Sr:(r + 1) * Sr],
                                    atol=1e-5, rtol=1e-5)
         np.testing.assert_allclose(lse, ref_lse[:, :, r * Sr:(r + 1) * Sr], atol=1e-5)
+
+
+def test_unit_range_checks():
+    """Unit sub-ranges of the Ulysses exchange must lie inside 0..n_per and the
+    output exchange must be given as many units as the range holds."""
+    from sinkattn_b200.sharding import _unit_range
+
+    assert _unit_range(None, 3) == (0, 3)
+    assert _unit_range((1, 3), 3) == (1, 3)
+    for bad in ((0, 0), (2, 1), (-1, 2), (0, 4)):
+        with pytest.raises(ValueError):
+            _unit_range(bad, 3)
