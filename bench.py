@@ -18,12 +18,12 @@ Extra figures in the same JSON line: the density of the coverage-rule mask on
 the stated generator (~0.83) and its TFLOP/s, the calibration pass (pooling
 + pooled softmax + batch mean + coverage mask of one cfg3 layer), the
 end-to-end number through the reference-facing API with host buffers, the
-roofline of the attention kernel, sampled clocks, and the CPU oracle timed on
-the host cores.
+roofline of the attention kernel, sampled clocks, and the CPU reference
+(dense masked torch attention) timed on the host cores.
 
 --impl reference times the reference's CPU path for this operation (dense
-masked fp32 attention, the oracle port in oracle/sinkattn_oracle.py) on the
-host cores, on a bounded sample of the same workload per step.
+masked fp32 attention in torch, as the benchmark defines its reference, on all
+host threads), on a bounded sample of the same workload per step.
 """
 from __future__ import annotations
 
@@ -199,22 +199,38 @@ def barrier(world: int):
 # ---------------------------------------------------------------------------
 # CPU (reference path) timing
 # ---------------------------------------------------------------------------
-def cpu_attention_sample(q, k, v, mask, units, q_blocks):
-    """Time the oracle's dense masked attention (the reference's CPU path) on
-    `units` (b, h) pairs x `q_blocks` query blocks each. Returns
-    (seconds, kept FLOPs of the sample)."""
-    from oracle import sinkattn_oracle as orc
+def torch_masked_attention(q, k, v, block_mask, row_chunk=512):
+    """Dense masked attention as the benchmark defines its reference (cfg1:
+    dense torch attention with the block mask expanded to tokens and masked
+    scores set to -inf), in fp32 torch on the CPU so that every host thread
+    works: q [Sq,D], k/v [Sk,D], block_mask bool [nq,nk]. Returns out, lse."""
+    Sq, D = q.shape
+    Sk = k.shape[0]
+    scale = 1.0 / math.sqrt(D)
+    tok = block_mask.repeat_interleave(128, 0).repeat_interleave(128, 1)[:Sq, :Sk]
+    out = torch.empty(Sq, D)
+    lse = torch.empty(Sq)
+    kt = k.t().contiguous()
+    for r0 in range(0, Sq, row_chunk):
+        r1 = min(Sq, r0 + row_chunk)
+        sc = (q[r0:r1] @ kt) * scale
+        sc.masked_fill_(~tok[r0:r1], float("-inf"))
+        lse[r0:r1] = torch.logsumexp(sc, dim=-1)
+        out[r0:r1] = torch.softmax(sc, dim=-1) @ v
+    return out, lse
 
+
+def cpu_attention_sample(q, k, v, mask, units, q_blocks):
+    """Time dense masked fp32 attention on the host (torch, all threads) on
+    `units` (b, h) pairs x `q_blocks` query blocks each. Returns (seconds,
+    kept FLOPs of the sample)."""
     flops = 0.0
     t0 = time.perf_counter()
     for (b, h) in units:
         rows = slice(0, q_blocks * 128)
-        qq = q[b:b + 1, h:h + 1, rows]
-        kk = k[b:b + 1, h:h + 1]
-        vv = v[b:b + 1, h:h + 1]
-        m = mask[0:1, h:h + 1, :q_blocks]
-        orc.dense_masked_attention(qq, kk, vv, m, row_chunk=256)
-        flops += orc.kept_block_flops(m, 1, 1, q_blocks * 128, S)
+        m = mask[0, h, :q_blocks]
+        torch_masked_attention(q[b, h, rows], k[b, h], v[b, h], m)
+        flops += 4.0 * D * 128 * 128 * float(m.sum().item())
     return time.perf_counter() - t0, flops
 
 
@@ -222,9 +238,9 @@ def make_cpu_sample(seed=0):
     from tests.gen import cfg1_mask, wan_qk
 
     q, k, v = wan_qk(seed=seed, B=1, H=2, dtype=torch.float32)
-    mask = cfg1_mask(12, NB, NB, seed=1).unsqueeze(0).numpy()[:, :2]
+    mask = cfg1_mask(12, NB, NB, seed=1).unsqueeze(0)[:, :2]
     # bf16-valued fp32, like the GPU inputs
-    q, k, v = (t.bfloat16().float().numpy() for t in (q, k, v))
+    q, k, v = (t.bfloat16().float().contiguous() for t in (q, k, v))
     return q, k, v, mask
 
 
@@ -246,7 +262,8 @@ def run_reference(args):
     total = sum(times)
     value = flops * args.steps / total / 1e12
     sample = (f"{len(units)} (b,h) units x {q_blocks} query blocks x all 256 key blocks of the "
-              f"Wan layer (cfg1-style mask, rho~0.21), dense masked fp32 numpy per step")
+              f"Wan layer (cfg1-style mask, rho~0.21), dense masked fp32 torch attention per "
+              f"step")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
@@ -489,7 +506,7 @@ def run_ours(args):
         dt, fl = cpu_attention_sample(cq, ck, cv, cm, [(0, 0), (0, 1)], 32)
         cpu = {"value": fl / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": "2 (b,h) units x 32 query blocks x 256 key blocks, rho~0.21, "
-                         "dense masked fp32 numpy oracle (the reference's CPU path)"}
+                         "dense masked fp32 torch attention (the benchmark's reference)"}
 
     traffic = load_traffic().get("bsattn_fwd_wan_rho21")
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
