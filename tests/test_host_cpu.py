@@ -1,12 +1,13 @@
 """Host-side logic that needs no GPU: argument checks of the new entry points,
 the rotary-table normalisation and RMSNorm detection of the Q/K producer
 drop-in, the Z-Image calibrator's fixed block layout, and the score-mode
-dispatch."""
+dispatch, and the CPU reference the benchmark times."""
 from __future__ import annotations
 
 import ctypes
 import math
 
+import numpy as np
 import pytest
 import torch
 
@@ -139,3 +140,21 @@ def test_score_mode_dispatch():
         ra._compute_exact_block_mass_scores(torch.zeros(1, 1, 64, 128), torch.zeros(1, 1, 64, 128),
                                             Cfg())
     assert math.isclose(1.0, 1.0)
+
+
+def test_bench_cpu_reference_matches_oracle(oracle):
+    """The CPU reference the benchmark times (dense masked torch attention on
+    all host threads) computes the oracle's dense masked attention."""
+    import bench
+
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(700, 128, generator=g)
+    k = torch.randn(900, 128, generator=g)
+    v = torch.randn(900, 128, generator=g)
+    m = torch.rand(6, 8, generator=g) < 0.5
+    m[:, 0] = True
+    out, lse = bench.torch_masked_attention(q, k, v, m, row_chunk=256)
+    ref, ref_lse = oracle.dense_masked_attention(q[None, None].numpy(), k[None, None].numpy(),
+                                                 v[None, None].numpy(), m[None, None].numpy())
+    np.testing.assert_allclose(out.numpy(), ref[0, 0], atol=1e-5)
+    np.testing.assert_allclose(lse.numpy(), ref_lse[0, 0], atol=1e-5)
