@@ -655,6 +655,49 @@ def run_case(args):
         print(json.dumps({"case": args.case, "ms": ms, "bytes": nbytes,
                           "gbs": nbytes / (ms / 1e3) / 1e9}))
         return 0
+    if args.case == "misc-wan":
+        # the two bandwidth kernels of the unfused Wan runtime at its real shape
+        # (B=2, H=12, 32760 tokens): sequence mean pooling with gap 30 (the pooled
+        # K/V of the dynamic branch) and the adaptive LSE mix of the two branches.
+        # Inputs are strided [B,S,H,D] storage as the processors produce them.
+        tokens, gap = 32760, 30
+        g = torch.Generator(device=dev).manual_seed(0)
+
+        def bshd():
+            x = torch.randn(B, tokens, H, D, generator=g, device=dev, dtype=torch.bfloat16)
+            return x.permute(0, 2, 1, 3)
+
+        xs = [bshd() for _ in range(2)]  # pooled alternately: 403 MB, more than L2
+        o_s, o_d = bshd(), bshd()
+        l_s = torch.randn(B, H, tokens, generator=g, device=dev) + 8.0
+        l_d = torch.randn(B, H, tokens, generator=g, device=dev) + 5.0
+        peak = float(load_peaks()[0].get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        elems = B * H * tokens * D
+        rows_out = math.ceil(tokens / gap)
+        cases = {
+            "mean_pool_seq": (lambda i: ops.mean_pool_seq(xs[i % 2], gap),
+                              2 * elems + 2 * B * H * rows_out * D),
+            "mix_outputs": (lambda i: ops.mix_outputs(o_s, l_s, o_d, l_d, gap),
+                            3 * 2 * elems + 2 * 4 * B * H * tokens),
+        }
+        res = {"case": args.case, "B": B, "H": H, "S": tokens, "peak_gbs": peak}
+        stream = torch.cuda.current_stream(dev)
+        for name, (fn, nbytes) in cases.items():
+            it = iter(range(1 << 30))
+            call = lambda: fn(next(it))  # noqa: E731
+            for _ in range(3):
+                call()
+            torch.cuda.synchronize()
+            # a ~25 ms device spin first, so that every timed launch is queued
+            # before the device reaches it and the per-launch events measure the
+            # kernel rather than the host's launch rate
+            torch.cuda._sleep(50_000_000)
+            _, per = time_steps(call, args.steps, stream)
+            ms = sorted(per)[len(per) // 2]
+            res[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms / 1e3) / 1e9,
+                         "frac": nbytes / (ms / 1e3) / 1e9 / peak}
+        print(json.dumps(res))
+        return 0
     if args.case == "zimage":
         # cfg4 (Z-Image 2048x2048): B=1, H=30, 16384 image + 512 text tokens = 132 blocks;
         # text rows and columns forced dense as the Z-Image processor does
@@ -825,7 +868,7 @@ def main(argv=None):
                     help="heads per host<->device chunk of the end-to-end leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
                                        "calib-pass", "wan-runtime", "stats-wan", "stats-small",
-                                       "qkrope-wan", "ulysses", "zimage"],
+                                       "qkrope-wan", "misc-wan", "ulysses", "zimage"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)
