@@ -168,7 +168,7 @@ def test_accumulate_finalize(oracle):
 
 
 @pytest.mark.parametrize("S,pool,prefix", [(32760, 30, 0), (1000, 30, 0), (1000, 30, 77),
-                                           (500, 7, 600)])
+                                           (500, 7, 600), (1000, 40, 3), (4100, 128, 0)])
 def test_mean_pool_seq(oracle, S, pool, prefix):
     from sinkattn_b200 import ops
 
