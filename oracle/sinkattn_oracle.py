@@ -9,6 +9,9 @@ Pinning:
   * Pooling, pooled-score softmax and the coverage mask builder are pinned
     against golden vectors produced by importing the reference itself
     (tests/golden/make_golden.py -> tests/golden/*.npz).
+  * Sequence mean pooling with a prefix, the adaptive mix, and both
+    calibrators' statistics (including the Z-Image alignment) are pinned the
+    same way (tests/golden/make_golden_calib.py -> tests/golden/calib.npz).
   * Attention: the reference obtains block-sparse attention from the external
     package mit-han-lab/Block-Sparse-Attention (unpinned, cloned at HEAD per
     README.md:26-33, absent here), so there is no reference output for masked
@@ -260,6 +263,40 @@ def finalize(sum_: np.ndarray, sumsq: np.ndarray, count) -> tuple[np.ndarray, np
     second = (sumsq / np.float32(count) if np.isscalar(count) else sumsq / count).astype(np.float32)
     var = np.maximum(second - mean * mean, 0).astype(np.float32)
     return mean, np.sqrt(var).astype(np.float32)
+
+
+def zimage_align(scores: np.ndarray, image_blocks: int, text_blocks: int,
+                 total_blocks: int) -> tuple[np.ndarray, np.ndarray]:
+    """_align_scores_image_text_suffix and _alignment_presence_mask
+    (zimg/runtime/sink_sparse_zimage.py:140-186): one sample's scores
+    [H, n, n], n = image_blocks + text_blocks, placed in the fixed
+    [H, total, total] layout with the image blocks first and this sample's
+    text blocks last; presence is 1 where a score landed, else 0."""
+    H, n, _ = scores.shape
+    if n != image_blocks + text_blocks or scores.shape[2] != n:
+        raise ValueError("Unexpected Z-Image block score shape. "
+                         f"Expected {image_blocks + text_blocks}x{image_blocks + text_blocks}, "
+                         f"got {n}x{scores.shape[2]}.")
+    src = np.concatenate([np.arange(image_blocks),
+                          np.arange(image_blocks, image_blocks + text_blocks)])
+    dst = np.concatenate([np.arange(image_blocks),
+                          np.arange(total_blocks - text_blocks, total_blocks)])
+    aligned = np.zeros((H, total_blocks, total_blocks), np.float32)
+    presence = np.zeros_like(aligned)
+    aligned[:, dst[:, None], dst[None, :]] = scores[:, src[:, None], src[None, :]]
+    presence[:, dst[:, None], dst[None, :]] = 1.0
+    return aligned, presence
+
+
+def finalize_presence(sum_: np.ndarray, sumsq: np.ndarray,
+                      presence: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """ZImageSinkMaskCalibrator.build_package's statistics
+    (zimg/runtime/sink_sparse_zimage.py:330-334): presence counts raised to
+    at least 1, then the presence-weighted mean and std. Returns (mean, std,
+    clamped presence)."""
+    pres = np.maximum(presence, np.float32(1.0)).astype(np.float32)
+    mean, std = finalize(sum_, sumsq, pres)
+    return mean, std, pres
 
 
 # ---------------------------------------------------------------------------

@@ -59,12 +59,18 @@ class DeviceSinkMaskCalibrator:
         kb = k if k.dtype == torch.bfloat16 else k.to(torch.bfloat16)
         _, bmean = ops.pool_scores(qb, kb, block=int(self.config.block_size), want_scores=False,
                                    want_batch_mean=True, workspace=self._workspace)
+        self._accumulate_score(layer_idx, bmean)
+
+    def _accumulate_score(self, layer_idx: int, scores: torch.Tensor) -> None:
+        """_accumulate_score (sparse_attention.py:537-549): adds one record's
+        batch-mean scores [H, nq, nk] (fp32, on the GPU) to the layer's running
+        sum and sum of squares, which stay on the GPU."""
         first = layer_idx not in self.score_sums
         if first:
-            self.score_sums[layer_idx] = torch.empty_like(bmean)
-            self.score_sq_sums[layer_idx] = torch.empty_like(bmean)
+            self.score_sums[layer_idx] = torch.empty_like(scores)
+            self.score_sq_sums[layer_idx] = torch.empty_like(scores)
             self.score_counts[layer_idx] = 0
-        ops.score_accumulate(bmean, self.score_sums[layer_idx], self.score_sq_sums[layer_idx],
+        ops.score_accumulate(scores, self.score_sums[layer_idx], self.score_sq_sums[layer_idx],
                              first=first)
         self.score_counts[layer_idx] += 1
 

@@ -16,6 +16,7 @@ if str(ROOT) not in sys.path:
 from tests.gen import digest  # noqa: E402
 
 GOLDEN = ROOT / "tests" / "golden" / "golden.npz"
+CALIB_GOLDEN = ROOT / "tests" / "golden" / "calib.npz"
 # Location of a reference checkout for the CPU-only drop-in tests (optional).
 REFERENCE_DIR = Path(os.environ.get("SINKATTN_REFERENCE", "/root/reference"))
 
@@ -36,6 +37,11 @@ def pytest_collection_modifyitems(config, items):
 @pytest.fixture(scope="session")
 def golden():
     return dict(np.load(GOLDEN, allow_pickle=False))
+
+
+@pytest.fixture(scope="session")
+def calib_golden():
+    return dict(np.load(CALIB_GOLDEN, allow_pickle=False))
 
 
 def regen_input(g: dict, case: str, key: str) -> torch.Tensor:

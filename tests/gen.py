@@ -141,3 +141,15 @@ def digest(*arrays) -> str:
             a = a.numpy()
         h.update(np.ascontiguousarray(a).tobytes())
     return h.hexdigest()
+
+
+def config_from_json(text: str):
+    """A dataclass instance carrying the fields and values of a stored
+    SinkSparseConfig (JSON of its asdict()), for code that reads config
+    attributes and calls asdict() on the config it was given."""
+    import dataclasses
+    import json
+
+    data = json.loads(str(text))
+    cls = dataclasses.make_dataclass("StoredSinkSparseConfig", list(data.keys()))
+    return cls(**data)
