@@ -72,6 +72,7 @@ def _check_package(pkg_path, g, prefix):
     loaded = torch.load(pkg_path, map_location="cpu", weights_only=True)
     assert loaded["version"] == 3
     assert loaded["meta"] == json.loads(str(g[f"{prefix}/meta"]))
+    assert loaded["config"] == json.loads(str(g[f"{prefix}/config"]))
     for layer in ("0", "1"):
         assert loaded["counts"][layer] == int(g[f"{prefix}/count/{layer}"])
         # the mean and std carry the reference's bits; the mask is the reference's
