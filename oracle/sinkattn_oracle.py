@@ -137,6 +137,40 @@ def required_mask(nq: int, nk: int, text_blocks: int, force_sink_col: bool = Fal
     return req
 
 
+def adapt_block_mask(mask: np.ndarray, source_block: int, seq_q: int, seq_k: int,
+                     kernel_block: int = 128) -> np.ndarray:
+    """_adapt_block_mask_for_kernel (sparse_attention.py:797-852): a bool
+    mask [..., nq, nk] over `source_block`-token blocks, mapped onto the
+    kernel's `kernel_block` tiles. A kernel tile is kept when any source block
+    that overlaps it is kept: coarse blocks are repeated, fine blocks are
+    any-pooled (absent blocks past the end count as not kept). The result has
+    ceil(seq / kernel_block) tiles per side."""
+    if source_block <= 0 or kernel_block <= 0:
+        raise ValueError(f"Invalid block sizes: source={source_block}, kernel={kernel_block}")
+    tq = -(-int(seq_q) // kernel_block)
+    tk = -(-int(seq_k) // kernel_block)
+    if source_block == kernel_block:
+        if mask.shape[-2:] != (tq, tk):
+            raise ValueError("Runtime block mask is already at kernel tile size but has the "
+                             f"wrong shape: expected [..., {tq}, {tk}], got {list(mask.shape)}")
+        return mask.copy()
+    if source_block > kernel_block and source_block % kernel_block:
+        raise ValueError("Cannot adapt a coarse Sink mask: source block size is not a "
+                         "multiple of the kernel block size.")
+    if source_block < kernel_block and kernel_block % source_block:
+        raise ValueError("Cannot adapt a fine Sink mask: kernel block size is not a "
+                         "multiple of the source block size.")
+    nq, nk = mask.shape[-2:]
+    out = np.zeros(mask.shape[:-2] + (tq, tk), dtype=bool)
+    for i in range(tq):
+        # source blocks overlapping kernel tile i: tokens [i*kb, (i+1)*kb)
+        q0, q1 = i * kernel_block // source_block, -(-(i + 1) * kernel_block // source_block)
+        for j in range(tk):
+            k0, k1 = j * kernel_block // source_block, -(-(j + 1) * kernel_block // source_block)
+            out[..., i, j] = mask[..., q0:min(q1, nq), k0:min(k1, nk)].any(axis=(-2, -1))
+    return out
+
+
 def _first_reach(cum32: np.ndarray, target: np.float32) -> int:
     hit = np.nonzero(cum32 >= target)[0]
     return int(hit[0]) if hit.size else -1

@@ -8,6 +8,9 @@ fixed inputs: the steps on either side of the kernels.
   sequence, and a pool of 128.
 - `_mix_attention_outputs` (sparse_attention.py:898-919) on bf16 outputs and
   bf16 LSE, as the reference's adapter returns them.
+- `_adapt_block_mask_for_kernel` (sparse_attention.py:797-852): a coarse mask
+  (256-token blocks, repeated onto 128 tiles), a fine one (32-token blocks,
+  any-pooled), both with ragged lengths, and the identity at 128.
 - `SinkMaskCalibrator` (sparse_attention.py:526-608): three generations of two
   layers, then `build_package`. The calibrator is fed fixed block scores by
   replacing `_compute_block_scores` in its module, so the statistics and masks
@@ -45,6 +48,11 @@ MEAN_POOL_CASES = {
     "mpool_d": dict(shape=(2, 1, 4100, 128), seed=53, pool=128, prefix=5),
 }
 MIX_CASE = dict(shape=(1, 2, 129, 64), seeds=(61, 62, 63, 64), sample_gap=30)
+ADAPT_CASES = {
+    "adapt_coarse": dict(source=256, Sq=1000, Sk=1300, heads=2, seed=91, p=0.3),
+    "adapt_fine": dict(source=32, Sq=1000, Sk=700, heads=2, seed=92, p=0.05),
+    "adapt_same": dict(source=128, Sq=1000, Sk=700, heads=2, seed=93, p=0.3),
+}
 
 
 def block_score_samples(gen: torch.Generator, B: int, H: int, n: int) -> torch.Tensor:
@@ -92,6 +100,19 @@ def main() -> int:
     g["mix/lse_d"] = bits(l_d.contiguous())
     g["mix/sample_gap"] = np.array(MIX_CASE["sample_gap"])
     g["mix/out"] = bits(mixed.contiguous())
+
+    # ---- mask adaptation to the kernel's 128-token tiles ----------------------
+    for name, c in ADAPT_CASES.items():
+        gen = torch.Generator().manual_seed(c["seed"])
+        nq = -(-c["Sq"] // c["source"])
+        nk = -(-c["Sk"] // c["source"])
+        src = torch.rand(1, c["heads"], nq, nk, generator=gen) < c["p"]
+        out = sa._adapt_block_mask_for_kernel(src, source_block_size=c["source"],
+                                              seq_len_q=c["Sq"], seq_len_k=c["Sk"])
+        g[f"{name}/mask"] = src.numpy()
+        g[f"{name}/source"] = np.array(c["source"])
+        g[f"{name}/seq"] = np.array([c["Sq"], c["Sk"]])
+        g[f"{name}/out"] = out.numpy()
 
     # ---- Wan calibrator: statistics, masks and package -----------------------
     gen = torch.Generator().manual_seed(71)

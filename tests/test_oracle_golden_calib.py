@@ -1,7 +1,7 @@
 """The oracle's restatements of the steps either side of the kernels against
 golden vectors made by running the reference (tests/golden/make_golden_calib.py):
-sequence mean pooling with a kept prefix, the adaptive LSE mix, and both
-calibrators' statistics and masks.
+sequence mean pooling with a kept prefix, the adaptive LSE mix, the mask
+adaptation to 128-token tiles, and both calibrators' statistics and masks.
 
 These pin the oracle functions that the GPU tests of sa_mean_pool_seq,
 sa_mix_outputs and the calibrator kernels check against.
@@ -127,3 +127,23 @@ def test_zimage_calibrator_statistics_match_reference(calib_golden, oracle):
 def test_zimage_align_rejects_a_mismatched_shape(oracle):
     with pytest.raises(ValueError, match="Unexpected Z-Image block score shape"):
         oracle.zimage_align(np.zeros((2, 9, 9), np.float32), 8, 2, 11)
+
+
+@pytest.mark.parametrize("case", ["adapt_coarse", "adapt_fine", "adapt_same"])
+def test_adapt_block_mask_matches_reference(calib_golden, oracle, case):
+    g = calib_golden
+    seq_q, seq_k = (int(v) for v in g[f"{case}/seq"])
+    got = oracle.adapt_block_mask(g[f"{case}/mask"], int(g[f"{case}/source"]), seq_q, seq_k)
+    want = g[f"{case}/out"]
+    assert got.shape == want.shape and got.dtype == want.dtype
+    assert np.array_equal(got, want)
+
+
+def test_adapt_block_mask_rejects_what_the_reference_rejects(oracle):
+    m = np.ones((1, 2, 8, 6), dtype=bool)
+    with pytest.raises(ValueError, match="wrong shape"):
+        oracle.adapt_block_mask(m, 128, 1000, 1000)
+    with pytest.raises(ValueError, match="coarse"):
+        oracle.adapt_block_mask(m, 192, 1000, 700)
+    with pytest.raises(ValueError, match="fine"):
+        oracle.adapt_block_mask(m, 48, 1000, 700)
