@@ -1,6 +1,7 @@
 """CPU-only checks of the C-ABI boundary: the library loads, exports every
-symbol include/sinkattn.h declares, and rejects bad arguments on the host
-(before any CUDA call) with SA_EINVAL and a message."""
+symbol include/sinkattn.h declares with the ctypes signature the header
+gives, and rejects bad arguments on the host (before any CUDA call) with
+SA_EINVAL and a message."""
 from __future__ import annotations
 
 import ctypes
@@ -213,3 +214,49 @@ def test_install_binds_dropins_into_reference(monkeypatch):
         sa._HAS_BLOCK_SPARSE = orig["block_sparse_attn_func"] is not None
         for m in [m for m in list(sys.modules) if m.startswith(("wanx", "zimg", "sinkattention"))]:
             sys.modules.pop(m, None)
+
+
+def header_signatures() -> dict[str, tuple[str, list[str]]]:
+    """name -> (return type, parameter declarations) of every SA_API function."""
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    sigs = {}
+    for m in re.finditer(r"^SA_API\s+([\w\s\*]+?)\b(sa_\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M):
+        params = " ".join(m.group(3).split())
+        sigs[m.group(2)] = (m.group(1).strip(),
+                            [] if params in ("", "void") else [p.strip() for p in params.split(",")])
+    return sigs
+
+
+_C_KINDS = {"int": "i32", "int32_t": "i32", "int64_t": "i64", "size_t": "size", "float": "f32"}
+
+
+def _c_kind(decl: str, is_return: bool = False) -> str:
+    decl = re.sub(r"\bconst\b", " ", decl)
+    if "*" in decl or "[" in decl or "cudaStream_t" in decl:
+        return "ptr"
+    toks = decl.split()
+    return _C_KINDS[toks[0] if is_return or len(toks) == 1 else " ".join(toks[:-1])]
+
+
+def _ctypes_kind(t) -> str:
+    return {ctypes.c_void_p: "ptr", ctypes.c_char_p: "ptr", ctypes.c_int: "i32",
+            ctypes.c_int64: "i64", ctypes.c_size_t: "size", ctypes.c_float: "f32"}[t]
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every entry point's ctypes declaration has the header's parameter count
+    and kinds (pointer, int, int64, size_t, float) in order, so a call can
+    never pass a misread argument to the library."""
+    from sinkattn_b200 import _lib
+
+    sigs = header_signatures()
+    assert set(sigs) == set(header_symbols())
+    assert set(sigs) == set(_lib._SIGNATURES), set(sigs) ^ set(_lib._SIGNATURES)
+    for name, (ret, params) in sigs.items():
+        res, args = _lib._SIGNATURES[name]
+        assert _ctypes_kind(res) == _c_kind(ret, is_return=True), name
+        want = [_c_kind(p) for p in params]
+        got = [_ctypes_kind(a) for a in args]
+        assert got == want, f"{name}: ctypes {got} != header {want}"
