@@ -416,8 +416,10 @@ _PATCHES = {
 
 def install(modules: Optional[list[str]] = None, fused_dynamic: bool = True) -> list[str]:
     """Bind the replacements into the reference's modules (importing them if
-    needed). Returns the list of patched module names; modules that cannot be
-    imported are skipped. With fused_dynamic, WanSinkSparseInnerAttention.forward
+    needed). Returns the list of patched module names. A module whose import
+    fails with ImportError (a route whose dependencies are absent) is skipped,
+    unless the caller named it in `modules`, in which case the error is
+    raised. With fused_dynamic, WanSinkSparseInnerAttention.forward
     is replaced by fused_wan_inner_forward (one kernel for the sink branch, the
     pooled dynamic branch and their mix). In the Wan runtime the Q/K RMSNorm and
     rotary embedding become one kernel (fused_prepare_attention_tensors)."""
@@ -429,7 +431,9 @@ def install(modules: Optional[list[str]] = None, fused_dynamic: bool = True) -> 
             continue
         try:
             mod = sys.modules.get(name) or importlib.import_module(name)
-        except Exception:  # the caller's environment may lack that route
+        except ImportError:
+            if modules is not None:
+                raise
             continue
         for attr, val in attrs.items():
             setattr(mod, attr, val)

@@ -260,3 +260,14 @@ def test_ctypes_signatures_match_the_header():
         want = [_c_kind(p) for p in params]
         got = [_ctypes_kind(a) for a in args]
         assert got == want, f"{name}: ctypes {got} != header {want}"
+
+
+def test_install_skips_absent_routes_unless_named(monkeypatch):
+    """A route whose module cannot be imported is skipped by install(), and
+    raises when the caller asked for it by name."""
+    from sinkattn_b200 import reference_api as ra
+
+    monkeypatch.setattr(ra, "_PATCHES", {"sinkattn_absent_route.runtime": {"x": 1}})
+    assert ra.install() == []
+    with pytest.raises(ImportError):
+        ra.install(modules=["sinkattn_absent_route.runtime"])
