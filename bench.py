@@ -18,8 +18,10 @@ Extra figures in the same JSON line: the density of the coverage-rule mask on
 the stated generator (~0.83) and its TFLOP/s, the calibration pass (pooling
 + pooled softmax + batch mean + coverage mask of one cfg3 layer), the
 end-to-end number through the reference-facing API with host buffers, the
-roofline of the attention kernel, sampled clocks, and the CPU reference
-(dense masked torch attention) timed on the host cores.
+roofline of the attention kernel, sampled clocks, and the CPU references
+timed on the host cores: dense masked torch attention, and the calibration
+path of two cfg3 layers (torch pooling and softmax, the oracle's coverage
+mask).
 
 --impl reference times the reference's CPU path for this operation (dense
 masked fp32 attention in torch, as the benchmark defines its reference, on all
@@ -232,6 +234,40 @@ def cpu_attention_sample(q, k, v, mask, units, q_blocks):
         torch_masked_attention(q[b, h, rows], k[b, h], v[b, h], m)
         flops += 4.0 * D * 128 * 128 * float(m.sum().item())
     return time.perf_counter() - t0, flops
+
+
+def cpu_calibration_layer(q, k, oracle):
+    """One cfg3 layer of the calibration path on the host, as the reference
+    computes it with pooling_mode "mean" (sparse_attention.py:118-142, 575-582,
+    268-376): fp32 means of Q and K over 128-token blocks, pooled logits scaled
+    by 1/sqrt(D), a row softmax and the batch mean in torch on all threads,
+    then the coverage mask (0.85, key block 0 kept) by the oracle's
+    restatement. q, k: bf16 [B,H,S,D] with S a multiple of 128. Returns the
+    mask [H,nb,nb]."""
+    Bq, Hq, Sq, Dq = q.shape
+    nb = Sq // 128
+    qp = q.float().view(Bq, Hq, nb, 128, Dq).mean(3)
+    kp = k.float().view(Bq, Hq, nb, 128, Dq).mean(3)
+    scores = torch.softmax(torch.matmul(qp, kp.transpose(-1, -2)) / math.sqrt(Dq), dim=-1)
+    bm = scores.mean(0)
+    return oracle.coverage_mask(bm.numpy(), force_sink_col=True,
+                                row_total=bm.sum(-1).numpy()).mask
+
+
+def cpu_calibration_sample(layers=2):
+    """Time `layers` cfg3 layers (seed = layer index) of cpu_calibration_layer
+    after one untimed layer. Returns (seconds, algorithmic bytes: Q and K read
+    in bf16 plus the 1-byte mask write, per layer)."""
+    from oracle import sinkattn_oracle as oracle
+    from tests.gen import wan_qk
+
+    inputs = [wan_qk(seed=s, dtype=torch.bfloat16)[:2] for s in range(layers)]
+    cpu_calibration_layer(*inputs[0], oracle)
+    t0 = time.perf_counter()
+    for q, k in inputs:
+        cpu_calibration_layer(q, k, oracle)
+    dt = time.perf_counter() - t0
+    return dt, layers * (2 * B * H * S * D * 2 + H * NB * NB)
 
 
 def make_cpu_sample(seed=0):
@@ -497,7 +533,7 @@ def run_ours(args):
 
     trace("e2e timed")
     # ---- CPU baseline (rank 0, N=1 only) ------------------------------------
-    cpu = None
+    cpu = cpu_cal = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
@@ -507,6 +543,12 @@ def run_ours(args):
         cpu = {"value": fl / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": "2 (b,h) units x 32 query blocks x 256 key blocks, rho~0.21, "
                          "dense masked fp32 torch attention (the benchmark's reference)"}
+        ct, cb = cpu_calibration_sample(2)
+        cpu_cal = {"value": cb / ct / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                   "ms_per_layer": 1e3 * ct / 2,
+                   "sample": "2 cfg3 layers (seeds 0, 1) after 1 untimed: torch fp32 128-token "
+                             "block means of Q and K, pooled softmax, batch mean, then the "
+                             "oracle's coverage mask (0.85, key block 0 kept)"}
 
     traffic = load_traffic().get("bsattn_fwd_wan_rho21")
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
@@ -560,6 +602,7 @@ def run_ours(args):
         "gpu_launches": args.steps * world,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
+        "cpu_baseline_calibration": cpu_cal,
     }
     from sinkattn_b200.ops import DeviceStatus
 

@@ -158,3 +158,21 @@ def test_bench_cpu_reference_matches_oracle(oracle):
                                                  v[None, None].numpy(), m[None, None].numpy())
     np.testing.assert_allclose(out.numpy(), ref[0, 0], atol=1e-5)
     np.testing.assert_allclose(lse.numpy(), ref_lse[0, 0], atol=1e-5)
+
+
+def test_bench_cpu_calibration_reference_matches_oracle(oracle):
+    """The CPU calibration reference the benchmark times (torch block means,
+    pooled softmax and batch mean, then the coverage rule with the sink
+    column) builds the oracle's mask from the oracle's pooled scores."""
+    import bench
+
+    g = torch.Generator().manual_seed(6)
+    q = torch.randn(2, 3, 1024, 128, generator=g).bfloat16()
+    k = torch.randn(2, 3, 1024, 128, generator=g).bfloat16()
+    got = bench.cpu_calibration_layer(q, k, oracle)
+    scores = oracle.pooled_block_scores(q.float().numpy(), k.float().numpy(), 128).mean(0)
+    ref = oracle.coverage_mask(scores, force_sink_col=True)
+    assert got.shape == (3, 8, 8) and got[:, :, 0].all()
+    # the two score computations differ in fp32 rounding only, which moves no
+    # coverage cut on these inputs
+    assert np.array_equal(got, ref.mask)
