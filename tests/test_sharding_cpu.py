@@ -1,6 +1,7 @@
 """Multi-rank logic on CPU: unit partitioning and the Ulysses exchange, run
-as gloo ranks (world sizes 2 and 4). The local attention of each rank is the
-CPU oracle here (the product path runs the CUDA kernel)."""
+as gloo ranks (world sizes 2, 4 and 8; at 8 the 6 units are padded to 8, so
+two ranks hold only padding). The local attention of each rank is the CPU
+oracle here (the product path runs the CUDA kernel)."""
 from __future__ import annotations
 
 import datetime
@@ -100,7 +101,7 @@ def _worker(rank, world, port, result_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_ulysses_exchange_matches_full_attention(tmp_path, world, oracle):
     port = _free_port()
     mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
