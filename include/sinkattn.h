@@ -48,7 +48,6 @@ extern "C" {
 /* Device status codes written into `status` by kernels. */
 #define SA_DEV_OK 0
 #define SA_DEV_WAIT_TIMEOUT 1 /* an mbarrier wait exceeded its iteration limit */
-#define SA_DEV_BAD_INDEX 2    /* an index check failed (bounds-check builds) */
 
 /* Mask-builder modes (offline_text_video_coverage_mode). */
 #define SA_COVERAGE_JOINT 0

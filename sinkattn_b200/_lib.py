@@ -21,7 +21,6 @@ SA_ECUDA = -4
 
 SA_DEV_OK = 0
 SA_DEV_WAIT_TIMEOUT = 1
-SA_DEV_BAD_INDEX = 2
 
 SA_COVERAGE_JOINT = 0
 SA_COVERAGE_VIDEO_RESIDUAL = 1

@@ -1,6 +1,6 @@
 """Build libsinkattn.so in-tree with nvcc for sm_100a (B200).
 
-Usage: python -m sinkattn_b200.build [--debug-bounds] [--verbose]
+Usage: python -m sinkattn_b200.build [--verbose] [--force]
 
 Each csrc/*.cu file is compiled to an object under sinkattn_b200/_build/ and
 linked into sinkattn_b200/libsinkattn.so. The build is incremental on file
@@ -60,13 +60,11 @@ def _compile(nvcc: str, src: Path, obj: Path, extra: list[str], verbose: bool) -
         print(res.stdout + res.stderr, flush=True)
 
 
-def build(debug_bounds: bool = False, verbose: bool = False, force: bool = False) -> Path:
+def build(verbose: bool = False, force: bool = False) -> Path:
     """Compile every CUDA source and link the shared library; returns its path."""
     nvcc = find_nvcc()
     BUILD.mkdir(exist_ok=True)
     extra: list[str] = []
-    if debug_bounds:
-        extra.append("-DSA_DEBUG_BOUNDS=1")
     if verbose:
         extra += ["-Xptxas", "-v"]
     stamp = BUILD / "flags.txt"
@@ -99,11 +97,10 @@ def build(debug_bounds: bool = False, verbose: bool = False, force: bool = False
 
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--debug-bounds", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--force", action="store_true")
     args = ap.parse_args(argv)
-    path = build(debug_bounds=args.debug_bounds, verbose=args.verbose, force=args.force)
+    path = build(verbose=args.verbose, force=args.force)
     print(path)
     return 0
 
