@@ -219,3 +219,20 @@ def test_calibration_pass_matches_serial_chain(chunk, head_groups):
         torch.cuda.synchronize()
         assert torch.equal(bm, bms[l])
         assert torch.equal(m, masks[l])
+
+
+def test_pool_means_then_pooled_softmax_equals_pool_scores():
+    """sa_pool_means followed by sa_pooled_softmax (the two halves, for hosts
+    that pipeline them) gives sa_pool_scores' scores and batch mean bit for
+    bit."""
+    from sinkattn_b200 import ops
+
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
+    k = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
+    sc, bm = ops.pool_scores(q, k, want_scores=True, want_batch_mean=True)
+    qp, kp = ops.pool_means(q, k)
+    sc2, bm2 = ops.pooled_softmax(qp, kp, want_scores=True, want_batch_mean=True)
+    torch.cuda.synchronize()
+    assert sc.shape == sc2.shape == (2, 3, 8, 8) and bm2.shape == (3, 8, 8)
+    assert torch.equal(sc, sc2) and torch.equal(bm, bm2)
