@@ -1,13 +1,15 @@
 """Multi-rank logic on CPU: unit partitioning and the Ulysses exchange, run
 as gloo ranks (world sizes 2, 4 and 8; at 8 the 6 units are padded to 8, so
 two ranks hold only padding). The local attention of each rank is the CPU
-oracle here (the product path runs the CUDA kernel)."""
+oracle here (the product path runs the CUDA kernel). A rank that leaves
+between steps makes the other rank's next exchange raise."""
 from __future__ import annotations
 
 import datetime
 import os
 import socket
 import sys
+import time
 from pathlib import Path
 
 import numpy as np
@@ -135,3 +137,41 @@ def test_unit_range_checks():
     for bad in ((0, 0), (2, 1), (-1, 2), (0, 4)):
         with pytest.raises(ValueError):
             _unit_range(bad, 3)
+
+
+def _leaving_worker(rank, world, port, result_dir):
+    """Rank 1 leaves between steps (after the first exchange, before the
+    second); rank 0 must see its next exchange end with an error, not hang."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    sys.path.insert(0, str(ROOT))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    from sinkattn_b200.sharding import sequence_to_units
+
+    x = torch.randn(2, 64, 3, 16)
+    sequence_to_units(x)  # one full step together
+    if rank == 1:
+        os._exit(0)  # leaves without joining the next exchange
+    t0 = time.monotonic()
+    try:
+        sequence_to_units(x)
+        outcome = "no error"
+    except Exception as exc:  # the backend's own error type
+        outcome = f"error: {type(exc).__name__}"
+    with open(os.path.join(result_dir, "rank0.txt"), "w") as f:
+        f.write(f"{outcome}\n{time.monotonic() - t0:.1f}\n")
+    os._exit(0)  # the group is broken; skip its teardown
+
+
+@pytest.mark.timeout(120)
+def test_exchange_errors_when_a_rank_leaves(tmp_path):
+    """Failure detection on the host: a rank that leaves between steps makes
+    the other rank's next all-to-all raise (peer closed or the group's 10 s
+    timeout) instead of waiting forever."""
+    port = _free_port()
+    mp.start_processes(_leaving_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    outcome, seconds = (tmp_path / "rank0.txt").read_text().split("\n")[:2]
+    assert outcome.startswith("error"), outcome
+    assert float(seconds) < 60
