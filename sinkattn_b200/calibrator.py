@@ -43,21 +43,53 @@ class DeviceSinkMaskCalibrator:
 
     @torch.no_grad()
     def record(self, layer_idx: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
-        """SinkMaskCalibrator.record (sparse_attention.py:575-582) on the device."""
+        """SinkMaskCalibrator.record (sparse_attention.py:575-582) on the device.
+
+        The score mode is dispatched as _compute_block_scores does
+        (sparse_attention.py:230-238): "exact" -> block masses of the full
+        softmax, "triton" (the SinkSparseConfig default, compared
+        case-sensitively as line 124 does) -> the Triton kernel's block maxima,
+        "mean" (and a "triton" in another case, which line 124 sends to the
+        torch path) -> the mean-pooled rule. The batch mean (line 580) stays on
+        the device: torch's mean for the tensor-core statistics, as the
+        reference takes it; the mean-pooled kernel forms it in its own epilogue.
+        """
         if layer_idx == 0:
             self.current_step += 1
         mode = str(self.config.pooling_mode).strip().lower()
-        if mode not in {"mean", "triton"}:
-            raise NotImplementedError(
-                f"DeviceSinkMaskCalibrator supports pooling_mode mean/triton, got {mode}")
+        if mode not in {"exact", "triton", "mean"}:
+            raise ValueError(
+                f"Unsupported pooling_mode: {self.config.pooling_mode}. Expected one of: "
+                "exact, triton, mean.")
+        ops._require_cuda(q, k)
+        if mode == "exact" or self.config.pooling_mode == "triton":
+            scores = _compute_block_scores(q, k, v, self.config)
+            self._accumulate_score(layer_idx, scores.float().mean(dim=0))
+            return
         B, H, S, D = q.shape
-        need = ops.pool_scores_workspace_size(B, H, S, D, int(self.config.block_size))
+        block = int(self.config.block_size)
+        need = ops.pool_scores_workspace_size(B, H, S, D, block)
         if self._workspace is None or self._workspace.numel() < need or \
                 self._workspace.device != q.device:
-            self._workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            self._workspace = ops.pool_scores_workspace(B, H, S, D, block, device=q.device)
         qb = q if q.dtype == torch.bfloat16 else q.to(torch.bfloat16)
         kb = k if k.dtype == torch.bfloat16 else k.to(torch.bfloat16)
-        _, bmean = ops.pool_scores(qb, kb, block=int(self.config.block_size), want_scores=False,
+        if ops._fused_calibration_ok(qb, block):
+            # one launch: scores, batch mean and the running sums
+            first = layer_idx not in self.score_sums
+            if first:
+                nb = -(-S // block)
+                self.score_sums[layer_idx] = torch.empty((H, nb, nb), dtype=torch.float32,
+                                                         device=q.device)
+                self.score_sq_sums[layer_idx] = torch.empty_like(self.score_sums[layer_idx])
+                self.score_counts[layer_idx] = 0
+            ops.calibration_layer(qb, kb, want_batch_mean=False,
+                                  accumulate=(self.score_sums[layer_idx],
+                                              self.score_sq_sums[layer_idx], first),
+                                  workspace=self._workspace)
+            self.score_counts[layer_idx] += 1
+            return
+        _, bmean = ops.pool_scores(qb, kb, block=block, want_scores=False,
                                    want_batch_mean=True, workspace=self._workspace)
         self._accumulate_score(layer_idx, bmean)
 

@@ -17,8 +17,28 @@ from tests.gen import digest  # noqa: E402
 
 GOLDEN = ROOT / "tests" / "golden" / "golden.npz"
 CALIB_GOLDEN = ROOT / "tests" / "golden" / "calib.npz"
-# Location of a reference checkout for the CPU-only drop-in tests (optional).
-REFERENCE_DIR = Path(os.environ.get("SINKATTN_REFERENCE", "/root/reference"))
+
+
+def _reference_dir() -> Path:
+    """Where the reference's Python packages (sinkattention, wanx, zimg) are
+    imported from by the tests that drive its own code: the directory named
+    by the SINKATTN_REFERENCE environment variable, else the offline install
+    under baseline/_ref. Tests that need it skip when it holds no package."""
+    env = os.environ.get("SINKATTN_REFERENCE")
+    return Path(env) if env else ROOT / "baseline" / "_ref"
+
+
+REFERENCE_DIR = _reference_dir()
+
+
+@pytest.fixture
+def reference(monkeypatch):
+    """Puts the reference's packages on sys.path for one test (skips when
+    they are not available)."""
+    if not (REFERENCE_DIR / "sinkattention").exists():
+        pytest.skip(f"reference packages not found under {REFERENCE_DIR}")
+    monkeypatch.syspath_prepend(str(REFERENCE_DIR))
+    return REFERENCE_DIR
 
 
 def pytest_configure(config):

@@ -153,3 +153,26 @@ def config_from_json(text: str):
     data = json.loads(str(text))
     cls = dataclasses.make_dataclass("StoredSinkSparseConfig", list(data.keys()))
     return cls(**data)
+
+
+# SinkSparseConfig() field defaults (sinkattention/sparse_attention.py:35-53),
+# as asdict() gives them; tests/test_host_cpu.py checks this copy against the
+# reference's dataclass when a reference checkout is importable.
+REFERENCE_DEFAULT_CONFIG = {
+    "block_size": 128, "sample_gap": 30, "token_width": 52, "token_height": 30,
+    "token_depth": 21, "text_length": 0, "force_text_global_attention": False,
+    "offline_text_video_coverage_mode": "joint", "keep_diagonal": True,
+    "runtime_diagonal_band_width": 0, "pooling_mode": "triton", "dynamic_mode": "pooled_kv",
+    "dynamic_kernel": "auto", "mixing_mode": "adaptive", "force_dense_steps": None,
+    "force_dense_layers": None, "offline_direct_coverage": 0.85,
+}
+
+
+def default_config(**overrides):
+    """A SinkSparseConfig stand-in with the reference's defaults (see
+    REFERENCE_DEFAULT_CONFIG), fields overridden by keyword."""
+    import json
+
+    data = dict(REFERENCE_DEFAULT_CONFIG)
+    data.update(overrides)
+    return config_from_json(json.dumps(data))

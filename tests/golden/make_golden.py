@@ -75,7 +75,8 @@ def fake_block_sparse_attn_func(q_unpad, k_unpad, v_unpad, cu_seqlens_q, cu_seql
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="directory holding the reference's sinkattention/ (a checkout or an install)")
     ap.add_argument("--out", default=str(HERE / "golden.npz"))
     args = ap.parse_args()
     sys.path.insert(0, args.reference)

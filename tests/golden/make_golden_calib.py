@@ -64,7 +64,8 @@ def block_score_samples(gen: torch.Generator, B: int, H: int, n: int) -> torch.T
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="directory holding the reference's sinkattention/ (a checkout or an install)")
     ap.add_argument("--out", default=str(HERE / "calib.npz"))
     args = ap.parse_args()
     sys.path.insert(0, args.reference)

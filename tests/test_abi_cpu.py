@@ -93,7 +93,11 @@ def test_pool_scores_workspace_and_validation(lib):
 
     B, H, S, D = 2, 12, 32768, 128
     nb = 256
-    assert lib.sa_pool_scores_workspace_size(B, H, S, D, 128) == 4 * B * H * nb * (2 * D + nb)
+    # 256-byte-rounded work counters, then pooled Q, K and logits in fp32
+    assert lib.sa_pool_scores_workspace_size(B, H, S, D, 128) == \
+        256 + 4 * B * H * nb * (2 * D + nb)
+    assert lib.sa_calibration_layer_workspace_size(B, H, S) == 256 + 4 * B * H * nb * 2 * D
+    assert lib.sa_calibration_layer_workspace_size(1, 100, 128) == 512 + 4 * 100 * 2 * 128
     assert lib.sa_pool_scores_workspace_size(0, H, S, D, 128) == 0
     st = _i64(H * S * D, S * D, D, 1)
     rc = lib.sa_pool_scores(16, 16, st, st, B, H, S, D, 128, -1.0, 16, None, 16, 8, None)
@@ -102,6 +106,33 @@ def test_pool_scores_workspace_and_validation(lib):
     assert rc == _lib.SA_EINVAL and "both NULL" in _lib.last_error()
     rc = lib.sa_pool_scores(16, 16, st, st, B, H, S, 100, 128, -1.0, 16, None, 16, 1 << 40, None)
     assert rc == _lib.SA_EINVAL
+
+
+def test_calibration_layer_validation(lib):
+    """sa_calibration_layer rejects what it cannot run before any launch."""
+    from sinkattn_b200 import _lib
+
+    B, H, S = 2, 12, 32768
+    st = _i64(H * S * 128, S * 128, 128, 1)
+    ws = 1 << 40
+
+    def call(*, D=128, S=S, scores=16, acc=(None, None), mask=None, flags=None, mode=0,
+             cov=0.85, text=0, ws_bytes=ws, strides=st, q=256):
+        return lib.sa_calibration_layer(q, 256, strides, strides, B, H, S, D, -1.0, scores, None,
+                                        acc[0], acc[1], 0, mask, flags, mode, cov, 1, text, 0,
+                                        256, ws_bytes, None, None)
+
+    assert call(D=64) == _lib.SA_EINVAL and "D must be 128" in _lib.last_error()
+    assert call(S=32769) == _lib.SA_EINVAL and "256 blocks" in _lib.last_error()
+    assert call(scores=None) == _lib.SA_EINVAL and "no output" in _lib.last_error()
+    assert call(acc=(16, None)) == _lib.SA_EINVAL and "go together" in _lib.last_error()
+    assert call(flags=16) == _lib.SA_EINVAL and "needs mask_out" in _lib.last_error()
+    assert call(mode=5) == _lib.SA_EINVAL and "mode" in _lib.last_error()
+    assert call(cov=float("nan")) == _lib.SA_EINVAL and "NaN" in _lib.last_error()
+    assert call(text=-1) == _lib.SA_EINVAL
+    assert call(strides=_i64(H * S * 128, S * 128, 100, 1)) == _lib.SA_EINVAL
+    assert call(q=264) == _lib.SA_EINVAL and "aligned" in _lib.last_error()
+    assert call(ws_bytes=1024) == _lib.SA_EINVAL and "workspace" in _lib.last_error()
 
 
 def test_coverage_mask_validation(lib):
@@ -145,19 +176,14 @@ def test_ops_reject_cpu_tensors():
         ops.coverage_mask(torch.rand(1, 4, 4))
 
 
-def test_install_binds_dropins_into_reference(monkeypatch):
-    """With the reference checkout importable, install() rebinds its hot-path
+def test_install_binds_dropins_into_reference(reference):
+    """With the reference's packages importable, install() rebinds its hot-path
     names (including the fused Wan inner forward); the rebound functions
     refuse CPU tensors (no CPU fallback)."""
     import sys
 
     import torch
 
-    from tests.conftest import REFERENCE_DIR
-
-    if not (REFERENCE_DIR / "sinkattention").exists():
-        pytest.skip("reference checkout not available")
-    monkeypatch.syspath_prepend(str(REFERENCE_DIR))
     import sinkattention.sparse_attention as sa
     import wanx.runtime.sink_sparse_wan as wan
 

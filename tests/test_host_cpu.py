@@ -176,3 +176,32 @@ def test_bench_cpu_calibration_reference_matches_oracle(oracle):
     # the two score computations differ in fp32 rounding only, which moves no
     # coverage cut on these inputs
     assert np.array_equal(got, ref.mask)
+
+
+def test_default_config_copy_matches_reference(reference):
+    """The tests' stand-in for SinkSparseConfig() carries the reference's
+    defaults, pooling_mode "triton" among them."""
+    from dataclasses import asdict
+
+    from sinkattention.sparse_attention import SinkSparseConfig
+    from tests.gen import REFERENCE_DEFAULT_CONFIG, default_config
+
+    assert asdict(SinkSparseConfig()) == REFERENCE_DEFAULT_CONFIG
+    assert asdict(default_config()) == REFERENCE_DEFAULT_CONFIG
+    assert default_config().pooling_mode == "triton"
+
+
+@pytest.mark.parametrize("mode", ["triton", "exact", "mean", "Triton", " EXACT "])
+def test_device_calibrator_refuses_cpu_tensors(mode):
+    """Every score mode of the device calibrator runs on CUDA tensors only
+    (no CPU fallback); an unknown mode raises the reference's ValueError."""
+    from sinkattn_b200.calibrator import DeviceSinkMaskCalibrator
+    from tests.gen import default_config
+
+    x = torch.zeros(1, 1, 256, 128, dtype=torch.bfloat16)
+    cal = DeviceSinkMaskCalibrator(default_config(pooling_mode=mode))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cal.record(0, x, x, x)
+    bad = DeviceSinkMaskCalibrator(default_config(pooling_mode="max"))
+    with pytest.raises(ValueError, match="Unsupported pooling_mode"):
+        bad.record(0, x, x, x)
