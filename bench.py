@@ -387,13 +387,14 @@ def run_ours(args):
     def step20():
         ops.bsattn_fwd(q, k, v, mask20, out=out, lse=lse)
 
-    # calibration pass on this layer's Q/K: pool + softmax + batch mean + mask
-    ws = torch.empty(ops.pool_scores_workspace_size(B, H, S, D), dtype=torch.uint8, device=dev)
-    calib = {}
+    # calibration layer on this layer's Q/K, one fused launch: pool -> pooled
+    # logits -> softmax -> batch mean -> coverage mask (key block 0 forced)
+    ws = ops.pool_scores_workspace(B, H, S, D, device=dev)
+    calib = {"mask": torch.empty(H, NB, NB, dtype=torch.bool, device=dev)}
 
     def step_calib():
-        _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
-        calib["mask"], _ = ops.coverage_mask(bm, force_sink_col=True)
+        ops.calibration_layer(q, k, want_batch_mean=False, mask_out=calib["mask"],
+                              force_sink_col=True, workspace=ws)
 
     step_calib()
     torch.cuda.synchronize()
@@ -445,6 +446,20 @@ def run_ours(args):
     tpool, _ = time_steps(step_pool_only, args.steps, stream)
     tpool = max_over_ranks(tpool, world, dev)
 
+    # the device calibrator's record (reference default config with the mean
+    # rule): one fused launch that also adds to the layer's running sums
+    from sinkattn_b200.calibrator import DeviceSinkMaskCalibrator
+    from tests.gen import default_config
+
+    cal = DeviceSinkMaskCalibrator(default_config(pooling_mode="mean"))
+
+    def step_record():
+        cal.record(0, q, k, v)
+
+    step_record()
+    trec, _ = time_steps(step_record, args.steps, stream)
+    trec = max_over_ranks(trec, world, dev)
+
     trace("calibration layer timed")
     # ---- cfg3: the 30-layer calibration pass, layers pipelined on two streams
     from tests.gen import wan_qk_layers_on_device
@@ -453,7 +468,7 @@ def run_ours(args):
     masks30 = torch.empty(30, H, NB, NB, dtype=torch.bool, device=dev)
 
     def step_pass():
-        ops.calibration_pass(layers, force_sink_col=True, masks_out=masks30)
+        ops.calibration_pass(layers, force_sink_col=True, masks_out=masks30, workspace=ws)
 
     for _ in range(2):
         step_pass()
@@ -464,7 +479,20 @@ def run_ours(args):
     pass_ms = tpass / pass_steps
     pass_bytes = 30 * calib_bytes
     density30 = float(masks30.float().mean().item())
-    del layers
+    # the pass's masks against the reference rule on the same batch means with
+    # the reference's fp32 row totals (CPU torch.sum), outside the timed region
+    _, bms30, flags30 = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True,
+                                             want_flags=True, workspace=ws)
+    bms30_c = bms30.cpu()
+    ref30 = torch.stack([ops.coverage_mask(bms30[l], force_sink_col=True,
+                                           row_total=bms30_c[l].sum(-1).to(dev))[0]
+                         for l in range(30)])
+    diff30 = (ref30 != masks30).any(-1)
+    near = (flags30 & (_lib.SA_ROW_NEAR_TARGET | _lib.SA_ROW_TIE_AT_CUT)) != 0
+    pass_check = {"rows": int(diff30.numel()), "flagged_rows": int(near.sum()),
+                  "differing_rows": int(diff30.sum()),
+                  "differing_unflagged_rows": int((diff30 & ~near).sum())}
+    del layers, bms30, ref30
 
     trace("calibration pass timed")
     # ---- end to end through the reference-facing API (host buffers) ---------
@@ -569,13 +597,20 @@ def run_ours(args):
                                "unit": UNIT},
         "calibration_layer": {"ms_per_layer": tcal / args.steps,
                               "pool_scores_ms": tpool / args.steps,
+                              "calibrator_record_ms": trec / args.steps,
                               "bytes": calib_bytes * world,
                               "gbs": calib_bytes * world / (tcal / args.steps / 1e3) / 1e9,
                               "frac_of_hbm": calib_bytes / (tcal / args.steps / 1e3) / 1e9
                               / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
-                              "note": "one layer per rank (pool -> pooled softmax -> batch mean "
-                                      "-> coverage mask); pool_scores_ms: the first three "
-                                      "alone; bytes and gbs whole-job, frac per GPU"},
+                              "pool_scores_frac_of_hbm": 2 * B * H * S * D * 2
+                              / (tpool / args.steps / 1e3) / 1e9
+                              / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
+                              "note": "one layer per rank, one fused launch (pool -> pooled "
+                                      "logits -> softmax -> batch mean -> coverage mask); "
+                                      "pool_scores_ms: the same without the mask (scores' "
+                                      "batch mean only); calibrator_record_ms: "
+                                      "DeviceSinkMaskCalibrator.record, mean rule, with the "
+                                      "running sums; bytes and gbs whole-job, frac per GPU"},
         "calibration_pass_30_layers": {
             "ms_per_pass": pass_ms, "ms_per_layer": pass_ms / 30,
             "bytes_per_pass": pass_bytes * world,
@@ -583,10 +618,12 @@ def run_ours(args):
             "frac_of_hbm": pass_bytes / (pass_ms / 1e3) / 1e9
             / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
             "mask_density": density30,
+            "vs_reference_totals": pass_check,
             "note": "cfg3: 30 layers x Q,K [2,12,32768,128] bf16 (GPU-generated, seed=layer); "
-                    "pool -> pooled softmax -> batch mean -> coverage mask (sink column "
-                    "forced); layers in chunks of 3, the pooling of chunk c+1 overlaps the "
-                    "stacked scores and masks of chunk c"},
+                    "one fused launch per layer (pool -> pooled logits -> softmax -> batch "
+                    "mean -> coverage mask, sink column forced, device row totals); "
+                    "vs_reference_totals: rows whose mask differs from the rule with the "
+                    "reference's CPU fp32 row totals, all of which must be flagged"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
                 "chunk_heads": hg,

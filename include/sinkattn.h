@@ -125,8 +125,10 @@ SA_API int sa_sink_dynamic_attn_fwd(
     cudaStream_t stream);
 
 /*
- * Scratch bytes sa_pool_scores needs: pooled Q and K in fp32 plus the fp32
- * pooled logits, 4 * B * H * nb * (2 * D + nb) bytes with nb = ceil(S/block).
+ * Scratch bytes sa_pool_scores needs: the work counters of the fused kernel
+ * (the first sa_calibration_layer_workspace_size-style header, 256-byte
+ * rounded 4 * (H + 4) bytes), then pooled Q and K in fp32 and the fp32 pooled
+ * logits, 4 * B * H * nb * (2 * D + nb) bytes with nb = ceil(S/block).
  */
 SA_API size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int block);
 
@@ -142,8 +144,17 @@ SA_API size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int bloc
  * batch_mean: nullable fp32 [H,nb,nb] contiguous = scores.mean(dim=0)
  *   (SinkMaskCalibrator.record, sparse_attention.py:580-581).
  * At least one of scores / batch_mean must be non-NULL.
- * workspace: device scratch of sa_pool_scores_workspace_size() bytes.
+ * workspace: device scratch of sa_pool_scores_workspace_size() bytes,
+ *   256-byte aligned. Its first bytes are the work counters of the fused
+ *   kernel: zero them once when the workspace is allocated; every call
+ *   returns them to zero. Calls sharing one workspace must not overlap on
+ *   the GPU.
  * scale <= 0 selects 1/sqrt(D).
+ * At D = 128, block = 128, nb <= 256 this runs the fused calibration-layer
+ * kernel (as sa_calibration_layer) with the same results bit for bit as the
+ * pool / logits / softmax chain that other shapes run. No status word: a
+ * bounded wait that gives up (it does not in a working launch) leaves NaN
+ * in the affected rows.
  */
 SA_API int sa_pool_scores(const void* q, const void* k, const int64_t q_strides[4],
                    const int64_t k_strides[4], int B, int H, int S, int D,
@@ -180,6 +191,44 @@ SA_API int sa_pooled_softmax_layers(const float* qp, const float* kp, int L, int
                                     cudaStream_t stream);
 
 /*
+ * One calibration layer of the `mean` score mode in a single launch:
+ * pooling of Q and K, pooled logits, per-batch softmax, batch mean, and
+ * optionally the calibrator's running sums and the coverage mask.
+ * Replaces: _compute_pooled_qk_block_scores with pooling_mode="mean"
+ *   (sinkattention/sparse_attention.py:118-142), the batch mean of
+ *   SinkMaskCalibrator.record (line 580), _accumulate_score (lines 537-549)
+ *   and _build_direct_mean_coverage_mask (lines 241-376) on the batch mean.
+ * The HBM-bound pooling overlaps the score work inside the launch: heads are
+ * pooled in order and each head's rows are scored as soon as it is complete.
+ * q, k: bf16 [B,H,S,128] strided (stride(dim) == 1, other strides multiples
+ *   of 8 elements, 16-byte aligned); S <= 32768 (at most 256 blocks of 128).
+ * scores: nullable fp32 [B,H,nb,nb]; batch_mean: nullable fp32 [H,nb,nb].
+ * acc_sum / acc_sumsq: nullable pair fp32 [H,nb,nb]: sum += mean and
+ *   sumsq += mean * mean with separate roundings, or set when acc_first != 0.
+ * mask_out: nullable bool [H,nb,nb]: the coverage rule of sa_coverage_mask
+ *   (mode, coverage, keep_diagonal, text_blocks, force_sink_col as there)
+ *   on the batch mean, with row totals summed in fp64 and rounded;
+ *   row_flags: nullable int32 [H,nb] SA_ROW_* bits (needs mask_out).
+ * At least one output must be requested. The results equal sa_pool_scores
+ * followed by sa_score_accumulate and sa_coverage_mask (row_total NULL) bit
+ * for bit.
+ * workspace: sa_calibration_layer_workspace_size() bytes, 256-byte aligned;
+ *   its first 256-byte-rounded 4 * (H + 4) bytes are work counters that must
+ *   be zero when the workspace is first used (every call returns them to
+ *   zero). Calls sharing one workspace must not overlap on the GPU.
+ * scale <= 0 selects 1/sqrt(128). status: as sa_bsattn_fwd; the rows whose
+ *   wait gave up get NaN scores and all-kept mask rows.
+ */
+SA_API size_t sa_calibration_layer_workspace_size(int B, int H, int S);
+SA_API int sa_calibration_layer(const void* q, const void* k, const int64_t q_strides[4],
+                                const int64_t k_strides[4], int B, int H, int S, int D,
+                                float scale, float* scores, float* batch_mean, float* acc_sum,
+                                float* acc_sumsq, int acc_first, uint8_t* mask_out,
+                                int32_t* row_flags, int mode, float coverage, int keep_diagonal,
+                                int text_blocks, int force_sink_col, void* workspace,
+                                size_t ws_bytes, int32_t* status, cudaStream_t stream);
+
+/*
  * sa_pool_scores without a workspace argument. It has no counterpart in the
  * reference: it exists for callers that cannot allocate device memory when
  * they call in (a C/FFI host with no device allocator, or a server that
@@ -188,9 +237,12 @@ SA_API int sa_pooled_softmax_layers(const float* qp, const float* kp, int L, int
  * that loads it until the process exits; shapes needing more than 16 MiB
  * (see sa_pool_scores_workspace_size) return SA_EINVAL. The first call on a
  * device resolves the array's address with cudaGetSymbolAddress, so make it
- * before any stream capture. All calls share the array: calls that overlap on
- * the GPU race and must be serialised by the caller. Arguments and results
- * are those of sa_pool_scores.
+ * before any stream capture; the address is kept until the process exits, so
+ * no call may follow a cudaDeviceReset of that device. Each call clears the
+ * work counters at the start of the array (cudaMemsetAsync). All calls share
+ * the array: calls that overlap on the GPU race and must be serialised by the
+ * caller. Arguments and results are those of sa_pool_scores, which runs the
+ * same kernels.
  */
 SA_API int sa_pool_scores_noalloc(const void* q, const void* k,
                                   const int64_t q_strides[4],

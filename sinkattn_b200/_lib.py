@@ -58,6 +58,12 @@ _SIGNATURES = {
         _i,
         [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, ctypes.c_size_t, _vp],
     ),
+    "sa_calibration_layer_workspace_size": (ctypes.c_size_t, [_i, _i, _i]),
+    "sa_calibration_layer": (
+        _i,
+        [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _f, _i,
+         _i, _i, _vp, ctypes.c_size_t, _vp, _vp],
+    ),
     "sa_pool_means": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "sa_pooled_softmax_layers": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sa_pooled_softmax": (_i, [_vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),

@@ -6,6 +6,8 @@
 #include <stdio.h>
 
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "sa_common.cuh"
 
@@ -16,6 +18,8 @@ thread_local char g_err[512] = "";
 std::mutex g_mu;
 EncodeTiledFn g_encode = nullptr;
 int g_sm_count[64] = {};
+// (device, kernel, attribute, value) already applied by func_attr_once
+std::set<std::tuple<int, const void*, int, int>> g_attrs;
 }  // namespace
 
 void set_error(const char* fmt, ...) {
@@ -60,6 +64,17 @@ int sm_count_current_device() {
     g_sm_count[dev] = n;
   }
   return n;
+}
+
+int func_attr_once(const void* func, cudaFuncAttribute attr, int value) {
+  int dev = 0;
+  SA_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_mu);
+  const auto key = std::make_tuple(dev, func, (int)attr, value);
+  if (g_attrs.count(key) != 0) return SA_OK;
+  SA_CUDA_TRY(cudaFuncSetAttribute(func, attr, value));
+  g_attrs.insert(key);
+  return SA_OK;
 }
 
 }  // namespace sa

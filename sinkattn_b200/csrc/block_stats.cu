@@ -468,14 +468,10 @@ extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_stri
   p.scores = scores;
   p.scratch = reinterpret_cast<float*>(workspace);
   p.status = status;
-  int dev = 0;
-  SA_CUDA_TRY(cudaGetDevice(&dev));
-  static bool attr_set[64] = {};
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    SA_CUDA_TRY(cudaFuncSetAttribute(block_stats_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  if (int rc = sa::func_attr_once((const void*)block_stats_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      rc != SA_OK)
+    return rc;
   block_stats_kernel<<<stats_grid(B, H, S), kThreads, kSmemBytes, stream>>>(tk, p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;

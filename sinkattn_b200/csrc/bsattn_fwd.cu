@@ -797,15 +797,10 @@ int launch_attention(const char* fn, const void* q, const void* k, const void* v
   static std::atomic<unsigned> launch_seq{0};
   p.sched = (int)(launch_seq.fetch_add(1, std::memory_order_relaxed) % kSchedSlots);
 
-  int dev = 0;
-  SA_CUDA_TRY(cudaGetDevice(&dev));
-  static bool attr_set[64] = {};  // the attribute is per device
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    SA_CUDA_TRY(cudaFuncSetAttribute(bsattn_fwd_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kSmemBytes));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  if (int rc = sa::func_attr_once((const void*)bsattn_fwd_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      rc != SA_OK)
+    return rc;
   // persistent grid: one CTA per SM (at most one per tile)
   const int sms = sa::sm_count_current_device();
   const int grid = p.tiles < sms ? p.tiles : sms;

@@ -8,18 +8,26 @@
 //   scores = softmax(q_pool @ k_pool^T * (1/sqrt(D)), dim=-1)
 // and the batch mean SinkMaskCalibrator.record takes next (line 580-581).
 //
-// Three kernels, stream-ordered:
-//   pool_rows     HBM-bound: reads Q and K once with 16-byte loads, writes
-//                 fp32 block means [B,H,nb,D] to the workspace
+// At the calibration shapes (D = 128, 128-token blocks, at most 256 blocks,
+// TMA-compatible strides) sa_pool_scores runs the fused calibration-layer
+// kernel of calib_layer.cu: one launch whose score work overlaps its HBM-bound
+// pooling. Other shapes, and the two halves sa_pool_means / sa_pooled_softmax,
+// run three kernels, stream-ordered:
+//   pool_rows     HBM-bound: reads Q and K once with 16-byte loads (or TMA
+//                 tiles at D = 128, block = 128), writes fp32 block means
+//                 [B,H,nb,D] to the workspace
 //   pooled_logits fp32 SIMT GEMM, 64x64 tiles: logits = q_pool k_pool^T, then
 //                 the scale multiply (a separate rounding, as torch does)
 //   row_softmax   one warp per (head, query block): softmax of every batch's
 //                 row, optional per-batch output and the batch mean
-// fp32 throughout so the scores track the reference's fp32 matmul closely
-// (the coverage mask downstream is decided on these values).
+// Both forms take the same floating-point steps in the same order, so they
+// agree bit for bit. fp32 throughout so the scores track the reference's
+// fp32 matmul closely (the coverage mask downstream is decided on these
+// values).
 
 #include <math.h>
 
+#include "calib_layer.cuh"
 #include "sa_common.cuh"
 
 namespace sa {
@@ -301,21 +309,24 @@ namespace pool {
 // the next layer (launched on another stream) instead of waiting for a
 // carveout change.
 int prefer_max_shared_carveout() {
-  int dev = 0;
-  SA_CUDA_TRY(cudaGetDevice(&dev));
-  static bool done[64] = {};
-  if (dev >= 0 && dev < 64 && done[dev]) return SA_OK;
-  SA_CUDA_TRY(cudaFuncSetAttribute(pool_rows_tma_kernel,
-                                   cudaFuncAttributePreferredSharedMemoryCarveout,
-                                   cudaSharedmemCarveoutMaxShared));
-  SA_CUDA_TRY(cudaFuncSetAttribute(pooled_logits_kernel,
-                                   cudaFuncAttributePreferredSharedMemoryCarveout,
-                                   cudaSharedmemCarveoutMaxShared));
-  SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
-                                   cudaFuncAttributePreferredSharedMemoryCarveout,
-                                   cudaSharedmemCarveoutMaxShared));
-  if (dev >= 0 && dev < 64) done[dev] = true;
+  const void* fns[3] = {(const void*)pool_rows_tma_kernel, (const void*)pooled_logits_kernel,
+                        (const void*)row_softmax_kernel};
+  for (const void* f : fns)
+    if (int rc = func_attr_once(f, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+        rc != SA_OK)
+      return rc;
   return SA_OK;
+}
+
+// The row-softmax kernel's dynamic shared memory (8 warps x nb fp32) may
+// exceed the 48 KB default; the limit is raised once to the largest size
+// the entry points accept (200 KB).
+constexpr int kSoftmaxSmemMax = 200 * 1024;
+int allow_softmax_smem(size_t smem) {
+  if (smem <= 48 * 1024) return SA_OK;
+  return func_attr_once((const void*)row_softmax_kernel,
+                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSoftmaxSmemMax);
 }
 
 // Pools Q and K into qp / kp, through TMA staging when the shape allows.
@@ -346,15 +357,10 @@ int launch_pool_rows(const void* q, const void* k, const int64_t q_strides[4],
         return SA_ECUDA;
       }
     }
-    int dev = 0;
-    SA_CUDA_TRY(cudaGetDevice(&dev));
-    static bool attr_set[64] = {};
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      SA_CUDA_TRY(cudaFuncSetAttribute(pool_rows_tma_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kTmaSmem));
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
+    if (int rc = func_attr_once((const void*)pool_rows_tma_kernel,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaSmem);
+        rc != SA_OK)
+      return rc;
     const int64_t items = 2LL * B * H * nb;
     const int sms = sm_count_current_device();
     const int64_t warps_needed = (items + 0) / 1;
@@ -380,8 +386,62 @@ int launch_pool_rows(const void* q, const void* k, const int64_t q_strides[4],
 extern "C" size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int block) {
   if (B < 1 || H < 1 || S < 1 || D < 1 || block < 1) return 0;
   const size_t nb = (size_t)((S + block - 1) / block);
-  return 2 * (size_t)B * H * nb * D * sizeof(float) + (size_t)B * H * nb * nb * sizeof(float);
+  return sa::calib::counter_bytes(H) + 2 * (size_t)B * H * nb * D * sizeof(float) +
+         (size_t)B * H * nb * nb * sizeof(float);
 }
+
+namespace sa {
+namespace pool {
+
+// sa_pool_scores after its argument checks: the fused kernel where it
+// applies, else the three-kernel chain. The workspace starts with the fused
+// kernel's counters in both cases.
+int pool_scores_impl(const void* q, const void* k, const int64_t q_strides[4],
+                     const int64_t k_strides[4], int B, int H, int S, int D, int block,
+                     float scale, float* scores, float* batch_mean, void* workspace,
+                     size_t ws_bytes, cudaStream_t stream) {
+  const int nb = (S + block - 1) / block;
+  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
+  if (calib::eligible(q, k, q_strides, k_strides, B, H, S, D, block)) {
+    calib::LayerArgs a = {};
+    a.q = q;
+    a.k = k;
+    a.q_strides = q_strides;
+    a.k_strides = k_strides;
+    a.B = B;
+    a.H = H;
+    a.S = S;
+    a.scale = scale;
+    a.scores = scores;
+    a.batch_mean = batch_mean;
+    a.mode = SA_COVERAGE_JOINT;
+    a.workspace = workspace;
+    a.ws_bytes = ws_bytes;
+    return calib::launch(a, stream);
+  }
+  float* qp = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
+                                       calib::counter_bytes(H));
+  float* kp = qp + (size_t)B * H * nb * D;
+  float* logits = kp + (size_t)B * H * nb * D;
+
+  int rc = launch_pool_rows(q, k, q_strides, k_strides, B, H, S, D, block, nb, qp, kp, stream);
+  if (rc != SA_OK) return rc;
+  const int tiles = (nb + kT - 1) / kT;
+  pooled_logits_kernel<<<dim3(tiles, tiles, B * H), 256, 0, stream>>>(qp, kp, nb, D, scale, logits);
+  SA_CUDA_TRY(cudaGetLastError());
+  const int warps = 8;
+  const size_t smem = (size_t)warps * nb * sizeof(float);
+  SA_CHECK_ARG(smem <= kSoftmaxSmemMax, "sa_pool_scores: nb=%d too large", nb);
+  if (int rc2 = allow_softmax_smem(smem); rc2 != SA_OK) return rc2;
+  const int64_t rows = (int64_t)H * nb;
+  row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
+      logits, 1, B, H, nb, scores, batch_mean);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+}  // namespace pool
+}  // namespace sa
 
 extern "C" int sa_pool_scores(const void* q, const void* k, const int64_t q_strides[4],
                               const int64_t k_strides[4], int B, int H, int S, int D, int block,
@@ -401,32 +461,11 @@ extern "C" int sa_pool_scores(const void* q, const void* k, const int64_t q_stri
   const size_t need = sa_pool_scores_workspace_size(B, H, S, D, block);
   SA_CHECK_ARG(workspace != nullptr && ws_bytes >= need,
                "sa_pool_scores: workspace of %zu bytes required, got %zu", need, ws_bytes);
-  SA_CHECK_ARG(((uintptr_t)workspace) % 16 == 0, "sa_pool_scores: workspace must be 16-byte aligned");
-  const int nb = (S + block - 1) / block;
+  SA_CHECK_ARG(((uintptr_t)workspace) % 256 == 0,
+               "sa_pool_scores: workspace must be 256-byte aligned");
   SA_CHECK_ARG((int64_t)B * H <= 65535, "sa_pool_scores: B*H too large");
-  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
-
-  float* qp = reinterpret_cast<float*>(workspace);
-  float* kp = qp + (size_t)B * H * nb * D;
-  float* logits = kp + (size_t)B * H * nb * D;
-
-  int rc = launch_pool_rows(q, k, q_strides, k_strides, B, H, S, D, block, nb, qp, kp, stream);
-  if (rc != SA_OK) return rc;
-  const int tiles = (nb + kT - 1) / kT;
-  pooled_logits_kernel<<<dim3(tiles, tiles, B * H), 256, 0, stream>>>(qp, kp, nb, D, scale, logits);
-  SA_CUDA_TRY(cudaGetLastError());
-  const int warps = 8;
-  const size_t smem = (size_t)warps * nb * sizeof(float);
-  if (smem > 48 * 1024) {
-    SA_CHECK_ARG(smem <= 200 * 1024, "sa_pool_scores: nb=%d too large", nb);
-    SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  }
-  const int64_t rows = (int64_t)H * nb;
-  row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
-      logits, 1, B, H, nb, scores, batch_mean);
-  SA_CUDA_TRY(cudaGetLastError());
-  return SA_OK;
+  return pool_scores_impl(q, k, q_strides, k_strides, B, H, S, D, block, scale, scores,
+                          batch_mean, workspace, ws_bytes, stream);
 }
 
 extern "C" int sa_pool_means(const void* q, const void* k, const int64_t q_strides[4],
@@ -464,10 +503,8 @@ extern "C" int sa_pooled_softmax(const float* qp, const float* kp, int B, int H,
   SA_CUDA_TRY(cudaGetLastError());
   const int warps = 8;
   const size_t smem = (size_t)warps * nb * sizeof(float);
-  SA_CHECK_ARG(smem <= 200 * 1024, "sa_pooled_softmax: nb=%d too large", nb);
-  if (smem > 48 * 1024)
-    SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  SA_CHECK_ARG(smem <= kSoftmaxSmemMax, "sa_pooled_softmax: nb=%d too large", nb);
+  if (int rc = allow_softmax_smem(smem); rc != SA_OK) return rc;
   const int64_t rows = (int64_t)H * nb;
   row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
       logits_ws, 1, B, H, nb, scores, batch_mean);
@@ -498,10 +535,8 @@ extern "C" int sa_pooled_softmax_layers(const float* qp, const float* kp, int L,
   SA_CUDA_TRY(cudaGetLastError());
   const int warps = 8;
   const size_t smem = (size_t)warps * nb * sizeof(float);
-  SA_CHECK_ARG(smem <= 200 * 1024, "sa_pooled_softmax_layers: nb=%d too large", nb);
-  if (smem > 48 * 1024)
-    SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  SA_CHECK_ARG(smem <= kSoftmaxSmemMax, "sa_pooled_softmax_layers: nb=%d too large", nb);
+  if (int rc = allow_softmax_smem(smem); rc != SA_OK) return rc;
   const int64_t rows = (int64_t)L * H * nb;
   row_softmax_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, smem, stream>>>(
       logits_ws, L, B, H, nb, nullptr, batch_means);
@@ -516,20 +551,22 @@ extern "C" int sa_pooled_softmax_layers(const float* qp, const float* kp, int L,
 // that binds the .so without any device allocator of its own, or a serving
 // loop that reserved all device memory when it started and may not call
 // cudaMalloc on its hot path (cudaMalloc can synchronise the device and can
-// fail once memory is committed). For them the pooled Q/K and logits live in
-// one file-scope device array of kNoAllocScratchBytes (16 MiB), which every
-// GPU that loads this module keeps until the process exits. That covers the
-// Wan calibration shape (B=2, H=12, S=32768, D=128 needs 12.6 MB); larger
-// requests are rejected with SA_EINVAL.
+// fail once memory is committed). For them the scratch of sa_pool_scores
+// (work counters, pooled Q/K, logits) lives in one file-scope device array of
+// kNoAllocScratchBytes (16 MiB), which every GPU that loads this module keeps
+// until the process exits. That covers the Wan calibration shape (B=2, H=12,
+// S=32768, D=128 needs 12.6 MB); larger requests are rejected with SA_EINVAL.
+// The call runs exactly what sa_pool_scores runs for the same arguments.
 //
 // The first call on a device looks up the array's device address with
 // cudaGetSymbolAddress (host code only sees a host-side stand-in for the
-// symbol); make that first call before any stream capture begins. All calls
-// share the one array and it keeps the last call's contents: every byte a
-// call reads is written earlier in the same call, so nothing needs clearing,
-// but calls whose kernels overlap on the GPU (different streams, or several
-// host threads, on one device) race on it and must be serialised by the
-// caller.
+// symbol); make that first call before any stream capture begins. The
+// address is kept for the life of the process, so no call may follow a
+// cudaDeviceReset of that device. All calls share the one array and it keeps
+// the last call's contents: each call clears the work counters at its start
+// (cudaMemsetAsync, no allocation) and writes every other byte it reads, but
+// calls whose kernels overlap on the GPU (different streams, or several host
+// threads, on one device) race on it and must be serialised by the caller.
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -589,31 +626,13 @@ extern "C" int sa_pool_scores_noalloc(const void* q, const void* k, const int64_
                "caller-provided workspace",
                need, kNoAllocScratchBytes);
   const int nb = (S + block - 1) / block;
-  const size_t smem = (size_t)8 * nb * sizeof(float);
-  SA_CHECK_ARG(smem <= 200 * 1024, "sa_pool_scores_noalloc: nb=%d too large", nb);
-  if (scale <= 0.f) scale = 1.0f / sqrtf((float)D);
+  SA_CHECK_ARG((size_t)8 * nb * sizeof(float) <= kSoftmaxSmemMax,
+               "sa_pool_scores_noalloc: nb=%d too large", nb);
 
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc != SA_OK) return rc;
-  float* qp = reinterpret_cast<float*>(scratch);
-  float* kp = qp + (size_t)B * H * nb * D;
-  float* logits = kp + (size_t)B * H * nb * D;
-
-  pool_rows_kernel<<<dim3(nb, B * H, 2), kPoolThreads, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
-      q_strides[0], q_strides[1], q_strides[2], k_strides[0], k_strides[1], k_strides[2], H, S,
-      D, block, nb, qp, kp);
-  SA_CUDA_TRY(cudaGetLastError());
-  const int tiles = (nb + kT - 1) / kT;
-  pooled_logits_kernel<<<dim3(tiles, tiles, B * H), 256, 0, stream>>>(qp, kp, nb, D, scale, logits);
-  SA_CUDA_TRY(cudaGetLastError());
-  if (smem > 48 * 1024)
-    SA_CUDA_TRY(cudaFuncSetAttribute(row_softmax_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const int64_t rows = (int64_t)H * nb;
-  row_softmax_kernel<<<(unsigned)((rows + 7) / 8), 256, smem, stream>>>(logits, 1, B, H, nb,
-                                                                         scores, batch_mean);
-  SA_CUDA_TRY(cudaGetLastError());
-  return SA_OK;
+  SA_CUDA_TRY(cudaMemsetAsync(scratch, 0, sa::calib::counter_bytes(H), stream));
+  return pool_scores_impl(q, k, q_strides, k_strides, B, H, S, D, block, scale, scores,
+                          batch_mean, scratch, kNoAllocScratchBytes, stream);
 }

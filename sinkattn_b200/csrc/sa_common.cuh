@@ -32,6 +32,13 @@ EncodeTiledFn encode_tiled_fn();
 
 int sm_count_current_device();
 
+// Sets a kernel attribute on the current device once per (device, kernel,
+// attribute, value), under the library's mutex, so that first calls from
+// several host threads neither race on the bookkeeping nor repeat the call.
+// Kernels whose dynamic shared memory size varies by call set the largest
+// size they can need, so that no call lowers it under another's launch.
+int func_attr_once(const void* func, cudaFuncAttribute attr, int value);
+
 }  // namespace sa
 
 #define SA_CHECK_ARG(cond, ...)      \

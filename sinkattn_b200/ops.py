@@ -213,6 +213,28 @@ def pool_scores_workspace_size(B: int, H: int, S: int, D: int, block: int = BLOC
     return int(_lib.load().sa_pool_scores_workspace_size(B, H, S, D, block))
 
 
+def counter_bytes(H: int) -> int:
+    """Bytes of work counters at the start of a pool_scores / calibration_layer
+    workspace (zero when the workspace is first used; every call returns
+    them to zero)."""
+    return ((4 * (H + 4)) + 255) // 256 * 256
+
+
+def pool_scores_workspace(B: int, H: int, S: int, D: int, block: int = BLOCK,
+                          device=None) -> torch.Tensor:
+    """A workspace for pool_scores (and calibration_layer) with its work
+    counters zeroed, ready for any number of calls on one stream."""
+    need = pool_scores_workspace_size(B, H, S, D, block)
+    ws = torch.empty(need, dtype=torch.uint8, device=device)
+    ws[:counter_bytes(H)].zero_()
+    return ws
+
+
+def _fused_calibration_ok(q: torch.Tensor, block: int) -> bool:
+    B, H, S, D = q.shape
+    return D == BLOCK and block == BLOCK and math.ceil(S / BLOCK) <= 256
+
+
 def pool_scores(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -226,6 +248,8 @@ def pool_scores(
 
     q, k: bf16 [B,H,S,D] (any strides with stride(-1)=1). Returns
     (scores fp32 [B,H,nb,nb] or None, batch_mean fp32 [H,nb,nb] or None).
+    A given `workspace` must come from pool_scores_workspace (its counters
+    zero) or have been used only by earlier calls on the same stream.
     """
     dev = _require_cuda(q, k)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
@@ -237,7 +261,7 @@ def pool_scores(
     q, k = _as_kernel_layout(q), _as_kernel_layout(k)
     need = pool_scores_workspace_size(B, H, S, D, block)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        workspace = pool_scores_workspace(B, H, S, D, block, device=dev)
     scores = torch.empty((B, H, nb, nb), dtype=torch.float32, device=dev) if want_scores else None
     bmean = torch.empty((H, nb, nb), dtype=torch.float32, device=dev) if want_batch_mean else None
     sc = -1.0 if scale is None else float(scale)
@@ -340,6 +364,90 @@ def block_stats(q: torch.Tensor, k: torch.Tensor, mode: str = "exact",
     return out
 
 
+def calibration_layer(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    scale: Optional[float] = None,
+    want_scores: bool = False,
+    want_batch_mean: bool = True,
+    accumulate: Optional[tuple] = None,
+    want_mask: bool = False,
+    want_flags: bool = False,
+    coverage: float = 0.85,
+    keep_diagonal: bool = True,
+    text_blocks: int = 0,
+    mode: str = "joint",
+    force_sink_col: bool = False,
+    workspace: Optional[torch.Tensor] = None,
+    scores_out: Optional[torch.Tensor] = None,
+    batch_mean_out: Optional[torch.Tensor] = None,
+    mask_out: Optional[torch.Tensor] = None,
+    flags_out: Optional[torch.Tensor] = None,
+) -> dict:
+    """One calibration layer of the `mean` score mode in one launch
+    (sa_calibration_layer): block means of q, k -> pooled logits -> softmax
+    per batch element -> batch mean [-> running sums] [-> coverage mask].
+
+    q, k: bf16 [B,H,S,128] (S <= 32768). accumulate: (sum, sumsq, first)
+    with contiguous fp32 [H,nb,nb] accumulators. Returns a dict with the
+    requested "scores" [B,H,nb,nb], "batch_mean" [H,nb,nb], "mask" bool
+    [H,nb,nb] and "flags" int32 [H,nb]. The coverage mask uses row totals
+    summed on the device (fp64, rounded); rows whose decision lies within
+    2 ulp of the target carry SA_ROW_NEAR_TARGET in the flags."""
+    dev = _require_cuda(q, k)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or q.shape != k.shape or q.dim() != 4:
+        raise RuntimeError("calibration_layer expects bf16 q, k of one shape [B,H,S,128]")
+    B, H, S, D = q.shape
+    nb = math.ceil(S / BLOCK)
+    q, k = _as_kernel_layout(q), _as_kernel_layout(k)
+    need = int(_lib.load().sa_calibration_layer_workspace_size(B, H, S))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = pool_scores_workspace(B, H, S, D, BLOCK, device=dev)
+    out: dict = {}
+    if want_scores or scores_out is not None:
+        out["scores"] = scores_out if scores_out is not None else torch.empty(
+            (B, H, nb, nb), dtype=torch.float32, device=dev)
+    if want_batch_mean or batch_mean_out is not None:
+        out["batch_mean"] = batch_mean_out if batch_mean_out is not None else torch.empty(
+            (H, nb, nb), dtype=torch.float32, device=dev)
+    if want_mask or mask_out is not None:
+        out["mask"] = mask_out if mask_out is not None else torch.empty(
+            (H, nb, nb), dtype=torch.bool, device=dev)
+        if want_flags or flags_out is not None:
+            out["flags"] = flags_out if flags_out is not None else torch.empty(
+                (H, nb), dtype=torch.int32, device=dev)
+    for name, t, dt in (("scores", out.get("scores"), torch.float32),
+                        ("batch_mean", out.get("batch_mean"), torch.float32),
+                        ("mask", out.get("mask"), torch.bool),
+                        ("flags", out.get("flags"), torch.int32)):
+        if t is not None and (t.dtype != dt or not t.is_contiguous() or t.device != dev):
+            raise RuntimeError(f"calibration_layer: {name} must be contiguous {dt} on {dev}")
+    acc_sum = acc_sumsq = None
+    first = 0
+    if accumulate is not None:
+        acc_sum, acc_sumsq, first = accumulate
+        for t in (acc_sum, acc_sumsq):
+            if t.shape != (H, nb, nb) or t.dtype != torch.float32 or not t.is_contiguous():
+                raise RuntimeError("calibration_layer: accumulators must be contiguous fp32 "
+                                   f"[{H}, {nb}, {nb}]")
+    mode_id = (_lib.SA_COVERAGE_VIDEO_RESIDUAL
+               if str(mode).strip().lower() in {"video_residual", "video_residual_only",
+                                                "residual_video"}
+               else _lib.SA_COVERAGE_JOINT)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.sa_calibration_layer(
+            q.data_ptr(), k.data_ptr(), _lib.strides4(q), _lib.strides4(k), B, H, S, D,
+            -1.0 if scale is None else float(scale), _ptr(out.get("scores")),
+            _ptr(out.get("batch_mean")), _ptr(acc_sum), _ptr(acc_sumsq), int(bool(first)),
+            _ptr(out.get("mask")), _ptr(out.get("flags")), mode_id, float(coverage),
+            int(bool(keep_diagonal)), int(text_blocks), int(bool(force_sink_col)),
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+            DeviceStatus.get(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "sa_calibration_layer")
+    return out
+
+
 _PASS_STREAMS: dict[int, tuple] = {}
 
 
@@ -379,11 +487,23 @@ def calibration_pass(
     masks_out: Optional[torch.Tensor] = None,
     chunk: int = 3,
     head_groups: int = 1,
+    want_flags: bool = False,
+    workspace: Optional[torch.Tensor] = None,
+    fused: Optional[bool] = None,
 ):
     """Pooling + pooled softmax + batch mean + coverage mask for a sequence of
     layers, each given as a (q, k) pair of bf16 [B,H,S,D] CUDA tensors.
 
-    The work goes in units of (layer, group of H/head_groups heads) and the
+    At the calibration shapes (D = 128, block 128, at most 256 blocks) each
+    layer is one fused launch (sa_calibration_layer) on the caller's stream,
+    back to back, with the layer's score and mask work overlapping its own
+    pooling; `chunk` and `head_groups` then have no effect (fused=False
+    selects the pipeline below at any shape; both give the same bits). The coverage
+    masks use row totals summed on the device (fp64, rounded); with
+    want_flags the SA_ROW_* flags of every row are returned too.
+
+    Other shapes run a pipeline over layers: the work goes in units of
+    (layer, group of H/head_groups heads) and the
     units in chunks of `chunk`: every unit of a chunk is pooled back to back
     on one side stream (HBM-bound, one persistent TMA kernel per unit), then
     the chunk's pooled softmax and batch means (two launches for the whole
@@ -391,7 +511,7 @@ def calibration_pass(
     while the next chunk pools. head_groups > 1 lets a single layer overlap
     its own pooling with its scores and masks. The result is ordered on the
     caller's current stream. Returns (masks bool [L,H,nb,nb], batch means fp32
-    [L,H,nb,nb] or None)."""
+    [L,H,nb,nb] or None), plus flags int32 [L,H,nb] with want_flags."""
     layers = list(layers)
     if not layers:
         raise ValueError("calibration_pass needs at least one layer")
@@ -400,6 +520,29 @@ def calibration_pass(
     B, H, S, D = q0.shape
     nb = math.ceil(S / block)
     L = len(layers)
+    flags = torch.empty((L, H, nb), dtype=torch.int32, device=dev) if want_flags else None
+    if fused is None:
+        fused = _fused_calibration_ok(q0, block)
+    elif fused and not _fused_calibration_ok(q0, block):
+        raise ValueError("the fused calibration layer needs D = 128, block 128 and S <= 32768")
+    if fused:
+        masks = masks_out if masks_out is not None else torch.empty(
+            (L, H, nb, nb), dtype=torch.bool, device=dev)
+        bmeans = torch.empty((L, H, nb, nb), dtype=torch.float32, device=dev) \
+            if want_batch_mean else None
+        need = int(_lib.load().sa_calibration_layer_workspace_size(B, H, S))
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            workspace = pool_scores_workspace(B, H, S, D, block, device=dev)
+        for l, (q, k) in enumerate(layers):
+            if q.shape != (B, H, S, D) or k.shape != (B, H, S, D):
+                raise ValueError("all layers must share one [B,H,S,D] shape")
+            calibration_layer(q, k, want_batch_mean=False,
+                              batch_mean_out=None if bmeans is None else bmeans[l],
+                              mask_out=masks[l], flags_out=None if flags is None else flags[l],
+                              coverage=coverage, keep_diagonal=keep_diagonal,
+                              text_blocks=text_blocks, mode=mode, force_sink_col=force_sink_col,
+                              workspace=workspace)
+        return (masks, bmeans, flags) if want_flags else (masks, bmeans)
     G = max(1, int(head_groups))
     if H % G:
         raise ValueError(f"head_groups ({G}) must divide the {H} heads")
@@ -445,9 +588,12 @@ def calibration_pass(
                   if want_batch_mean else bmeans[buf, :n])
             pooled_softmax_layers(qp[buf, :n], kp[buf, :n], batch_means_out=bm, logits_ws=logits)
             consumed[buf].record(sc)
-            coverage_mask(bm.reshape(n * hg, nb, nb), coverage=coverage, keep_diagonal=keep_diagonal,
-                          text_blocks=text_blocks, mode=mode, force_sink_col=force_sink_col,
-                          out=mask_rows[u0 * hg:u1 * hg])
+            _, f = coverage_mask(bm.reshape(n * hg, nb, nb), coverage=coverage,
+                                 keep_diagonal=keep_diagonal, text_blocks=text_blocks, mode=mode,
+                                 force_sink_col=force_sink_col, out=mask_rows[u0 * hg:u1 * hg],
+                                 want_flags=want_flags)
+            if flags is not None:
+                flags.view(L * H, nb)[u0 * hg:u1 * hg].copy_(f)
     cur.wait_stream(sp)
     cur.wait_stream(sc)
     for t in (qp, kp, logits, bmeans, masks):
@@ -456,6 +602,9 @@ def calibration_pass(
     for q, k in layers:
         q.record_stream(sp)
         k.record_stream(sp)
+    if flags is not None:
+        flags.record_stream(sc)
+        return masks, (bmeans if want_batch_mean else None), flags
     return masks, (bmeans if want_batch_mean else None)
 
 

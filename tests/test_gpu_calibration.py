@@ -197,11 +197,14 @@ def test_mix_outputs(oracle):
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
 
 
-@pytest.mark.parametrize("chunk,head_groups", [(1, 1), (2, 1), (10, 1), (2, 3), (4, 3)])
-def test_calibration_pass_matches_serial_chain(chunk, head_groups):
-    """The chunked, two-stream pass over layers (stacked pooled softmax and one
-    mask launch per chunk), also with layers split into head groups, gives
-    exactly the per-layer serial results."""
+@pytest.mark.parametrize("fused,chunk,head_groups", [(True, 3, 1), (False, 1, 1), (False, 2, 1),
+                                                     (False, 10, 1), (False, 2, 3),
+                                                     (False, 4, 3)])
+def test_calibration_pass_matches_serial_chain(fused, chunk, head_groups):
+    """The pass over layers, as one fused launch per layer or as the chunked,
+    two-stream pipeline (stacked pooled softmax and one mask launch per
+    chunk, also with layers split into head groups), gives exactly the
+    per-layer serial results, flags included."""
     from sinkattn_b200 import ops
 
     g = torch.Generator().manual_seed(8)
@@ -210,15 +213,18 @@ def test_calibration_pass_matches_serial_chain(chunk, head_groups):
         q = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
         k = torch.randn(2, 3, 1000, 128, generator=g).bfloat16().cuda()
         layers.append((q, k))
-    masks, bms = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True,
-                                      chunk=chunk, head_groups=head_groups)
+    masks, bms, flags = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True,
+                                             chunk=chunk, head_groups=head_groups,
+                                             want_flags=True, fused=fused)
     torch.cuda.synchronize()
     for l, (q, k) in enumerate(layers):
-        _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True)
-        m, _ = ops.coverage_mask(bm, force_sink_col=True)
+        qp, kp = ops.pool_means(q, k)
+        _, bm = ops.pooled_softmax(qp, kp, want_scores=False, want_batch_mean=True)
+        m, f = ops.coverage_mask(bm, force_sink_col=True, want_flags=True)
         torch.cuda.synchronize()
         assert torch.equal(bm, bms[l])
         assert torch.equal(m, masks[l])
+        assert torch.equal(f, flags[l])
 
 
 def test_pool_means_then_pooled_softmax_equals_pool_scores():
@@ -236,3 +242,37 @@ def test_pool_means_then_pooled_softmax_equals_pool_scores():
     torch.cuda.synchronize()
     assert sc.shape == sc2.shape == (2, 3, 8, 8) and bm2.shape == (3, 8, 8)
     assert torch.equal(sc, sc2) and torch.equal(bm, bm2)
+
+
+def test_calibration_pass_30_layers_vs_reference_rule(oracle):
+    """cfg3 in full: the 30-layer pass (key block 0 forced, row totals summed
+    on the device) against the reference rule applied to the same batch-mean
+    scores with the reference's own fp32 row totals (CPU torch.sum, as
+    _build_direct_mean_coverage_mask takes them on the calibrator's CPU
+    tensors). Every row that differs must carry SA_ROW_NEAR_TARGET or
+    SA_ROW_TIE_AT_CUT; the count of flagged and differing rows is reported.
+    Layer 0's batch means are checked against the oracle's pooled scores."""
+    from sinkattn_b200 import _lib, ops
+    from tests.gen import wan_qk_layers_on_device
+
+    layers = wan_qk_layers_on_device(30, torch.device("cuda"))
+    masks, bms, flags = ops.calibration_pass(layers, force_sink_col=True, want_batch_mean=True,
+                                             want_flags=True)
+    torch.cuda.synchronize()
+    q0, k0 = layers[0]
+    ref0 = oracle.pooled_block_scores(q0[:, :2].float().cpu().numpy(),
+                                      k0[:, :2].float().cpu().numpy()).mean(axis=0)
+    np.testing.assert_allclose(bms[0, :2].cpu().numpy(), ref0, rtol=1e-4, atol=1e-7)
+    del layers
+    bms_c, masks_c, flags_c = bms.cpu(), masks.cpu().numpy(), flags.cpu().numpy()
+    flagged = differing = 0
+    for l in range(30):
+        s = bms_c[l]
+        res = oracle.coverage_mask(s.numpy(), row_total=s.sum(-1).numpy(), force_sink_col=True)
+        diff = (masks_c[l] != res.mask).any(-1)
+        fl = flags_c[l] & (_lib.SA_ROW_NEAR_TARGET | _lib.SA_ROW_TIE_AT_CUT)
+        assert not (diff & (fl == 0)).any(), f"layer {l}: unflagged rows differ"
+        flagged += int((fl != 0).sum())
+        differing += int(diff.sum())
+    print(f"30-layer pass: {30 * 12 * 256} rows, {flagged} flagged, {differing} differing "
+          "(all flagged)")
