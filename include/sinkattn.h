@@ -125,10 +125,11 @@ SA_API int sa_sink_dynamic_attn_fwd(
     cudaStream_t stream);
 
 /*
- * Scratch bytes sa_pool_scores needs: the work counters of the fused kernel
- * (the first sa_calibration_layer_workspace_size-style header, 256-byte
- * rounded 4 * (H + 4) bytes), then pooled Q and K in fp32 and the fp32 pooled
- * logits, 4 * B * H * nb * (2 * D + nb) bytes with nb = ceil(S/block).
+ * Scratch bytes sa_pool_scores needs: the work counters and flags of the
+ * fused kernel (128 * (H + 5) bytes rounded up to 256, then 8 bytes per
+ * group of 16 block rows of every head, rounded up to 256), then pooled Q
+ * and K in fp32 and the fp32 pooled logits, 4 * B * H * nb * (2 * D + nb)
+ * bytes with nb = ceil(S/block).
  */
 SA_API size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int block);
 
@@ -145,14 +146,14 @@ SA_API size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int bloc
  *   (SinkMaskCalibrator.record, sparse_attention.py:580-581).
  * At least one of scores / batch_mean must be non-NULL.
  * workspace: device scratch of sa_pool_scores_workspace_size() bytes,
- *   256-byte aligned. Its first bytes are the work counters of the fused
- *   kernel: zero them once when the workspace is allocated; every call
- *   returns them to zero. Calls sharing one workspace must not overlap on
- *   the GPU.
+ *   256-byte aligned, with any contents (the fused kernel's work counters
+ *   carry a per-launch tag, so nothing needs clearing). Calls sharing one
+ *   workspace must not overlap on the GPU.
  * scale <= 0 selects 1/sqrt(D).
- * At D = 128, block = 128, nb <= 256 this runs the fused calibration-layer
- * kernel (as sa_calibration_layer) with the same results bit for bit as the
- * pool / logits / softmax chain that other shapes run. No status word: a
+ * At D = 128, block = 128, nb <= 256, H <= 128 this runs the fused
+ * calibration-layer kernel (as sa_calibration_layer), whose results agree
+ * within one ulp with the pool / logits / softmax chain that other shapes
+ * run. No status word: a
  * bounded wait that gives up (it does not in a working launch) leaves NaN
  * in the affected rows.
  */
@@ -199,7 +200,8 @@ SA_API int sa_pooled_softmax_layers(const float* qp, const float* kp, int L, int
  *   SinkMaskCalibrator.record (line 580), _accumulate_score (lines 537-549)
  *   and _build_direct_mean_coverage_mask (lines 241-376) on the batch mean.
  * The HBM-bound pooling overlaps the score work inside the launch: heads are
- * pooled in order and each head's rows are scored as soon as it is complete.
+ * pooled in order and each head's rows are scored, and their mask rows
+ * built, as soon as it is complete.
  * q, k: bf16 [B,H,S,128] strided (stride(dim) == 1, other strides multiples
  *   of 8 elements, 16-byte aligned); S <= 32768 (at most 256 blocks of 128).
  * scores: nullable fp32 [B,H,nb,nb]; batch_mean: nullable fp32 [H,nb,nb].
@@ -210,12 +212,15 @@ SA_API int sa_pooled_softmax_layers(const float* qp, const float* kp, int L, int
  *   on the batch mean, with row totals summed in fp64 and rounded;
  *   row_flags: nullable int32 [H,nb] SA_ROW_* bits (needs mask_out).
  * At least one output must be requested. The results equal sa_pool_scores
- * followed by sa_score_accumulate and sa_coverage_mask (row_total NULL) bit
- * for bit.
- * workspace: sa_calibration_layer_workspace_size() bytes, 256-byte aligned;
- *   its first 256-byte-rounded 4 * (H + 4) bytes are work counters that must
- *   be zero when the workspace is first used (every call returns them to
- *   zero). Calls sharing one workspace must not overlap on the GPU.
+ * followed by sa_score_accumulate and sa_coverage_mask (row_total NULL) on
+ * its batch mean, bit for bit. The environment variable
+ * SINKATTN_CALIB_SCORE_CTAS, when set, gives the number of CTAs that score
+ * from the start (default about a fifth of the SMs).
+ * workspace: sa_calibration_layer_workspace_size() bytes, 256-byte aligned,
+ *   with any contents: work counters and flags tagged with a per-launch
+ *   number (so nothing needs clearing), the pooled Q and K, and a batch-mean
+ *   scratch. Calls sharing one workspace must not overlap on the GPU. H is at
+ *   most 128.
  * scale <= 0 selects 1/sqrt(128). status: as sa_bsattn_fwd; the rows whose
  *   wait gave up get NaN scores and all-kept mask rows.
  */
@@ -238,8 +243,9 @@ SA_API int sa_calibration_layer(const void* q, const void* k, const int64_t q_st
  * (see sa_pool_scores_workspace_size) return SA_EINVAL. The first call on a
  * device resolves the array's address with cudaGetSymbolAddress, so make it
  * before any stream capture; the address is kept until the process exits, so
- * no call may follow a cudaDeviceReset of that device. Each call clears the
- * work counters at the start of the array (cudaMemsetAsync). All calls share
+ * no call may follow a cudaDeviceReset of that device. Nothing in the array
+ * has to start at zero: the work counters at its start carry a per-launch
+ * tag, and every other byte a call reads it writes first. All calls share
  * the array: calls that overlap on the GPU race and must be serialised by the
  * caller. Arguments and results are those of sa_pool_scores, which runs the
  * same kernels.

@@ -35,18 +35,23 @@ struct LayerArgs {
   int32_t* status;    // nullable device word for SA_DEV_WAIT_TIMEOUT
 };
 
-// Bytes of the launch's work counters at the start of the workspace.
+// Bytes of the launch's work counters at the start of the workspace, and of
+// the per-(head, row group) flags that follow them.
 size_t counter_bytes(int H);
+size_t flag_bytes(int H, int nb);
+// Workspace bytes of one launch: counters, flags, pooled Q and K, and a
+// batch-mean scratch for callers that want the mask only.
+size_t workspace_bytes(int B, int H, int S);
 
 // Whether the fused kernel takes this shape and these pointers (D = 128,
-// block = 128, at most 256 blocks, TMA-compatible strides and alignment).
+// block = 128, at most 256 blocks and 128 heads, TMA-compatible strides and
+// alignment).
 bool eligible(const void* q, const void* k, const int64_t* q_strides, const int64_t* k_strides,
               int B, int H, int S, int D, int block);
 
-// Launches the kernel. The workspace holds counter_bytes(H) of counters
-// (zero when the workspace is first used; every launch returns them to
-// zero), then the pooled Q [B,H,nb,128] and the transposed pooled K
-// [B,H,128,nb] in fp32.
+// Launches the kernel on a workspace of workspace_bytes() (any contents):
+// counters, flags, the pooled Q [B,H,nb,128] and transposed pooled K
+// [B,H,128,nb] in fp32, and the batch-mean scratch [H,nb,nb].
 int launch(const LayerArgs& a, cudaStream_t stream);
 
 }  // namespace calib

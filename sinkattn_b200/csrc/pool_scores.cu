@@ -20,10 +20,9 @@
 //                 the scale multiply (a separate rounding, as torch does)
 //   row_softmax   one warp per (head, query block): softmax of every batch's
 //                 row, optional per-batch output and the batch mean
-// Both forms take the same floating-point steps in the same order, so they
-// agree bit for bit. fp32 throughout so the scores track the reference's
-// fp32 matmul closely (the coverage mask downstream is decided on these
-// values).
+// Both forms take the same floating-point steps and agree to within one ulp.
+// fp32 throughout so the scores track the reference's fp32 matmul closely
+// (the coverage mask downstream is decided on these values).
 
 #include <math.h>
 
@@ -386,8 +385,8 @@ int launch_pool_rows(const void* q, const void* k, const int64_t q_strides[4],
 extern "C" size_t sa_pool_scores_workspace_size(int B, int H, int S, int D, int block) {
   if (B < 1 || H < 1 || S < 1 || D < 1 || block < 1) return 0;
   const size_t nb = (size_t)((S + block - 1) / block);
-  return sa::calib::counter_bytes(H) + 2 * (size_t)B * H * nb * D * sizeof(float) +
-         (size_t)B * H * nb * nb * sizeof(float);
+  return sa::calib::counter_bytes(H) + sa::calib::flag_bytes(H, (int)nb) +
+         2 * (size_t)B * H * nb * D * sizeof(float) + (size_t)B * H * nb * nb * sizeof(float);
 }
 
 namespace sa {
@@ -420,7 +419,7 @@ int pool_scores_impl(const void* q, const void* k, const int64_t q_strides[4],
     return calib::launch(a, stream);
   }
   float* qp = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
-                                       calib::counter_bytes(H));
+                                       calib::counter_bytes(H) + calib::flag_bytes(H, nb));
   float* kp = qp + (size_t)B * H * nb * D;
   float* logits = kp + (size_t)B * H * nb * D;
 
@@ -563,10 +562,12 @@ extern "C" int sa_pooled_softmax_layers(const float* qp, const float* kp, int L,
 // symbol); make that first call before any stream capture begins. The
 // address is kept for the life of the process, so no call may follow a
 // cudaDeviceReset of that device. All calls share the one array and it keeps
-// the last call's contents: each call clears the work counters at its start
-// (cudaMemsetAsync, no allocation) and writes every other byte it reads, but
-// calls whose kernels overlap on the GPU (different streams, or several host
-// threads, on one device) race on it and must be serialised by the caller.
+// the last call's contents. Nothing in it has to start at zero: the fused
+// kernel's work counters carry a per-launch tag (a counter holding another
+// launch's tag counts as zero), and every other byte a call reads it writes
+// first. Calls whose kernels overlap on the GPU (different streams, or
+// several host threads, on one device) race on it and must be serialised by
+// the caller.
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -632,7 +633,6 @@ extern "C" int sa_pool_scores_noalloc(const void* q, const void* k, const int64_
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc != SA_OK) return rc;
-  SA_CUDA_TRY(cudaMemsetAsync(scratch, 0, sa::calib::counter_bytes(H), stream));
   return pool_scores_impl(q, k, q_strides, k_strides, B, H, S, D, block, scale, scores,
                           batch_mean, scratch, kNoAllocScratchBytes, stream);
 }

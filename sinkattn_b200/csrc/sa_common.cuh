@@ -110,13 +110,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// Records a bounded wait that gave up. The status word may live in device
+// memory or in mapped page-locked host memory (the host then reads it
+// without synchronising), so it is written with a plain store made visible
+// system-wide; every writer writes the same code.
+__device__ __forceinline__ void report_timeout(int32_t* status) {
+  if (status == nullptr) return;
+  *reinterpret_cast<volatile int32_t*>(status) = SA_DEV_WAIT_TIMEOUT;
+  __threadfence_system();
+}
+
+// Whether a kernel reported a failure (read only on slow paths: it may be
+// a read of host memory).
+__device__ __forceinline__ bool status_set(const int32_t* status) {
+  return status != nullptr && *reinterpret_cast<const volatile int32_t*>(status) != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete. Gives up
-// (returns false) after kWaitNs, recording SA_DEV_WAIT_TIMEOUT in *status and
+// (returns false) after limit_ns, recording SA_DEV_WAIT_TIMEOUT in *status and
 // raising the CTA's shared abort flag; it also gives up early once another
 // role of this CTA raised the abort flag or another CTA wrote *status, so one
 // failure ends the whole grid quickly instead of every CTA timing out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag,
+                                          uint64_t limit_ns = kWaitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
@@ -124,13 +141,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 255u) == 0u) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (status != nullptr && *reinterpret_cast<volatile int32_t*>(status) != 0) {
+      if (status_set(status)) {
         if (abort_flag != nullptr) *abort_flag = 1;
         return false;
       }
-      if (global_timer_ns() - t0 > kWaitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         if (abort_flag != nullptr) *abort_flag = 1;
-        if (status != nullptr) atomicExch(status, SA_DEV_WAIT_TIMEOUT);
+        report_timeout(status);
         return false;
       }
     }
@@ -158,6 +175,24 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
       "r"(smem_u32(bar))
       : "memory");
+}
+
+// Untiled bulk copy global -> shared (the TMA engine, no tensor map),
+// completion counted on `bar` (bytes). Both addresses 16-byte aligned, size a
+// multiple of 16 bytes. No multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses (any state space)
+// before its later async-proxy (TMA / bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_all() {
+  asm volatile("fence.proxy.async;" ::: "memory");
 }
 
 // TMA prefetch of a 4-D box into L2 (no shared memory, no completion).

@@ -213,26 +213,17 @@ def pool_scores_workspace_size(B: int, H: int, S: int, D: int, block: int = BLOC
     return int(_lib.load().sa_pool_scores_workspace_size(B, H, S, D, block))
 
 
-def counter_bytes(H: int) -> int:
-    """Bytes of work counters at the start of a pool_scores / calibration_layer
-    workspace (zero when the workspace is first used; every call returns
-    them to zero)."""
-    return ((4 * (H + 4)) + 255) // 256 * 256
-
-
 def pool_scores_workspace(B: int, H: int, S: int, D: int, block: int = BLOCK,
                           device=None) -> torch.Tensor:
-    """A workspace for pool_scores (and calibration_layer) with its work
-    counters zeroed, ready for any number of calls on one stream."""
+    """A workspace for pool_scores and calibration_layer (no clearing needed:
+    the kernels' work counters carry a per-launch tag)."""
     need = pool_scores_workspace_size(B, H, S, D, block)
-    ws = torch.empty(need, dtype=torch.uint8, device=device)
-    ws[:counter_bytes(H)].zero_()
-    return ws
+    return torch.empty(need, dtype=torch.uint8, device=device)
 
 
 def _fused_calibration_ok(q: torch.Tensor, block: int) -> bool:
     B, H, S, D = q.shape
-    return D == BLOCK and block == BLOCK and math.ceil(S / BLOCK) <= 256
+    return D == BLOCK and block == BLOCK and math.ceil(S / BLOCK) <= 256 and H <= 128
 
 
 def pool_scores(
@@ -248,8 +239,8 @@ def pool_scores(
 
     q, k: bf16 [B,H,S,D] (any strides with stride(-1)=1). Returns
     (scores fp32 [B,H,nb,nb] or None, batch_mean fp32 [H,nb,nb] or None).
-    A given `workspace` must come from pool_scores_workspace (its counters
-    zero) or have been used only by earlier calls on the same stream.
+    A given `workspace` (see pool_scores_workspace) may hold anything; calls
+    sharing one must not overlap on the GPU.
     """
     dev = _require_cuda(q, k)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:

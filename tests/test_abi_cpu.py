@@ -94,10 +94,18 @@ def test_pool_scores_workspace_and_validation(lib):
     B, H, S, D = 2, 12, 32768, 128
     nb = 256
     # 256-byte-rounded work counters, then pooled Q, K and logits in fp32
+    # work counters (one 128-byte line each, H + 5 of them, rounded to 256),
+    # group flags (8 bytes per 16 block rows of each head, rounded to 256),
+    # then pooled Q, K and logits in fp32 (sa_pool_scores) or pooled Q, K and
+    # a batch-mean scratch (the fused calibration layer)
+    ctr, flags = 2304, 1536  # 17 * 128 -> 2304; 12 heads * 16 groups * 8
     assert lib.sa_pool_scores_workspace_size(B, H, S, D, 128) == \
-        256 + 4 * B * H * nb * (2 * D + nb)
-    assert lib.sa_calibration_layer_workspace_size(B, H, S) == 256 + 4 * B * H * nb * 2 * D
-    assert lib.sa_calibration_layer_workspace_size(1, 100, 128) == 512 + 4 * 100 * 2 * 128
+        ctr + flags + 4 * B * H * nb * (2 * D + nb)
+    assert lib.sa_calibration_layer_workspace_size(B, H, S) == \
+        ctr + flags + 4 * B * H * nb * 2 * D + 4 * H * nb * nb
+    # 106 counter lines = 13568; 101 heads x 1 group x 8 bytes = 808 -> 1024
+    assert lib.sa_calibration_layer_workspace_size(1, 101, 128) == \
+        13568 + 1024 + 4 * 101 * 2 * 128 + 4 * 101
     assert lib.sa_pool_scores_workspace_size(0, H, S, D, 128) == 0
     st = _i64(H * S * D, S * D, D, 1)
     rc = lib.sa_pool_scores(16, 16, st, st, B, H, S, D, 128, -1.0, 16, None, 16, 8, None)
