@@ -17,10 +17,13 @@
  *     kernel needs any, is passed in by the caller (see *_workspace_size).
  *   - Return value: SA_OK (0) or a negative SA_E* code. The message of the
  *     last failure on the calling thread is returned by sa_last_error().
- *   - `status` arguments (nullable) point to one device int32 that a kernel
- *     sets to a non-zero SA_DEV_* code when one of its bounded waits gives
- *     up; the kernel then returns early instead of spinning. The host reads
- *     it when convenient (it is never read inside these calls).
+ *   - `status` arguments (nullable) point to one int32 that a kernel sets to
+ *     a non-zero SA_DEV_* code when one of its bounded waits gives up; the
+ *     kernel then returns early instead of spinning. Kernels write it only on
+ *     failure and read it only while a wait is already slow, so it may live in
+ *     mapped page-locked host memory (sa_status_create), where the host reads
+ *     it at any time without synchronising (sa_check_status), or in device
+ *     memory. It is never read inside these calls.
  */
 #ifndef SINKATTN_H_
 #define SINKATTN_H_
@@ -42,7 +45,7 @@ extern "C" {
 #define SA_OK 0
 #define SA_EINVAL (-1)       /* bad argument (shape, stride, alignment, null) */
 #define SA_EUNSUPPORTED (-2) /* valid request this build does not implement */
-#define SA_ETIMEOUT (-3)     /* reserved: a device wait gave up (see status) */
+#define SA_ETIMEOUT (-3)     /* a device wait gave up (sa_check_status) */
 #define SA_ECUDA (-4)        /* a CUDA runtime / driver call failed */
 
 /* Device status codes written into `status` by kernels. */
@@ -408,6 +411,34 @@ SA_API int sa_mix_outputs(const void* o_s, const int64_t os_strides[4], const fl
                    const void* o_d, const int64_t od_strides[4], const float* lse_d,
                    int B, int H, int S, int D, float log_gap, void* out,
                    const int64_t o_strides[4], cudaStream_t stream);
+
+/*
+ * The status word. No counterpart in the reference, whose kernels cannot
+ * report a stalled wait.
+ * sa_status_create: one int32 in mapped, portable page-locked host memory,
+ *   set to SA_DEV_OK; returns its host address (NULL on failure, see
+ *   sa_last_error). sa_status_device_pointer gives the address kernels use
+ *   (the same address where the device uses unified addressing);
+ *   sa_status_destroy frees it.
+ * sa_check_status: reads a host-readable status word without synchronising:
+ *   SA_OK if no kernel reported a failure, else SA_ETIMEOUT (with a message)
+ *   and the word is reset to SA_DEV_OK. A launch's report becomes visible once
+ *   the launch has run, so a caller that needs a verdict on a given launch
+ *   synchronises its stream first.
+ */
+SA_API int32_t* sa_status_create(void);
+SA_API int sa_status_device_pointer(int32_t* status, int32_t** device_ptr);
+SA_API int sa_status_destroy(int32_t* status);
+SA_API int sa_check_status(int32_t* status);
+
+/*
+ * Test support for failure detection: one warp waits on an mbarrier that
+ * nobody arrives on, with a limit of limit_ns (1 us .. 1 s). The wait gives
+ * up, the kernel writes SA_DEV_WAIT_TIMEOUT into *status (device-writable)
+ * and returns; no copy or MMA is in flight, so the context stays usable. No
+ * counterpart in the reference.
+ */
+SA_API int sa_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

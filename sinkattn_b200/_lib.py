@@ -90,6 +90,11 @@ _SIGNATURES = {
         [_vp, _vp, _i, _i, _i, _i, _f, _i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     ),
     "sa_mean_pool_seq": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "sa_status_create": (_vp, []),
+    "sa_status_device_pointer": (_i, [_vp, _vp]),
+    "sa_status_destroy": (_i, [_vp]),
+    "sa_check_status": (_i, [_vp]),
+    "sa_selftest_wait_timeout": (_i, [_vp, ctypes.c_uint64, _vp]),
     "sa_mix_outputs": (
         _i,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp],

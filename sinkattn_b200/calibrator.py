@@ -107,8 +107,13 @@ class DeviceSinkMaskCalibrator:
         self.score_counts[layer_idx] += 1
 
     def _build_mean_and_masks(self, config=None):
-        """_build_mean_and_masks (sparse_attention.py:551-573)."""
+        """_build_mean_and_masks (sparse_attention.py:551-573). Raises
+        RuntimeError if any kernel that fed the statistics reported a bounded
+        wait that gave up."""
         config = self.config if config is None else config
+        for t in self.score_sums.values():
+            ops.DeviceStatus.check(t.device)
+            break
         mean_scores, std_scores, sink_masks, counts = {}, {}, {}, {}
         for layer_idx in sorted(self.score_sums.keys()):
             key = str(layer_idx)
@@ -226,6 +231,9 @@ class DeviceZImageSinkMaskCalibrator:
         """build_package (sink_sparse_zimage.py:321-354): presence-weighted
         statistics, masks from the mean, package format version 3."""
         export_config = self.config if config_override is None else _zimg_config(config_override)
+        for t in self.score_sums.values():
+            ops.DeviceStatus.check(t.device)
+            break
         mean_scores, std_scores, sink_masks, counts = {}, {}, {}, {}
         for layer_idx in sorted(self.score_sums.keys()):
             key = str(layer_idx)

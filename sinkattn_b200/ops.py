@@ -57,30 +57,65 @@ def _as_kernel_layout(t: torch.Tensor) -> torch.Tensor:
 
 
 class DeviceStatus:
-    """One int32 per device that kernels set when a bounded wait gives up."""
+    """The status word kernels write when a bounded wait gives up, one per
+    device, in mapped page-locked host memory (sa_status_create): kernels
+    write it only on failure, and the host reads it at any time without
+    synchronising. The reference-facing drop-ins call raise_if_set() on entry,
+    so a failed launch is reported at the next call; check() synchronises
+    first, for a verdict on every launch issued so far."""
 
-    _flags: dict[int, torch.Tensor] = {}
+    _words: dict[int, tuple[int, int]] = {}  # device -> (host address, device address)
 
     @classmethod
-    def get(cls, device: torch.device) -> torch.Tensor:
-        idx = device.index if device.index is not None else torch.cuda.current_device()
-        t = cls._flags.get(idx)
-        if t is None:
-            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
-            cls._flags[idx] = t
-        return t
+    def _word(cls, idx: int) -> tuple[int, int]:
+        w = cls._words.get(idx)
+        if w is None:
+            lib = _lib.load()
+            host = lib.sa_status_create()
+            if not host:
+                raise RuntimeError(f"sa_status_create failed: {_lib.last_error()}")
+            dev_ptr = _lib.ctypes.c_void_p()
+            _lib.check(lib.sa_status_device_pointer(host, _lib.ctypes.byref(dev_ptr)),
+                       "sa_status_device_pointer")
+            w = (int(host), int(dev_ptr.value))
+            cls._words[idx] = w
+        return w
+
+    @staticmethod
+    def _index(device: Optional[torch.device]) -> int:
+        if device is None or device.index is None:
+            return torch.cuda.current_device()
+        return device.index
+
+    @classmethod
+    def pointer(cls, device: torch.device) -> int:
+        """The address kernels on `device` write their status to."""
+        return cls._word(cls._index(device))[1]
+
+    @classmethod
+    def value(cls, device: Optional[torch.device] = None) -> int:
+        """The word as the host sees it now (no synchronisation)."""
+        return int(_lib.ctypes.c_int32.from_address(cls._word(cls._index(device))[0]).value)
+
+    @classmethod
+    def raise_if_set(cls, device: Optional[torch.device] = None) -> None:
+        """Raise RuntimeError (and reset the word) if a kernel already
+        reported a failure; no synchronisation."""
+        idxs = [cls._index(device)] if device is not None else list(cls._words)
+        for idx in idxs:
+            host = cls._word(idx)[0]
+            rc = _lib.load().sa_check_status(host)
+            if rc != _lib.SA_OK:
+                raise RuntimeError(f"sinkattn_b200 on cuda:{idx}: {_lib.last_error()}")
 
     @classmethod
     def check(cls, device: Optional[torch.device] = None) -> None:
-        """Synchronise and raise if any kernel on `device` reported a timeout."""
-        devs = [device] if device is not None else [torch.device("cuda", i) for i in cls._flags]
-        for d in devs:
-            t = cls.get(d)
-            v = int(t.item())
-            if v != _lib.SA_DEV_OK:
-                t.zero_()
-                raise RuntimeError(f"sinkattn_b200 device status {v} on {d} "
-                                   "(a bounded wait in a kernel gave up)")
+        """Synchronise and raise if any kernel on `device` (all devices used
+        so far when None) reported a timeout."""
+        idxs = [cls._index(device)] if device is not None else list(cls._words)
+        for idx in idxs:
+            torch.cuda.synchronize(idx)
+            cls.raise_if_set(torch.device("cuda", idx))
 
 
 def bsattn_fwd(
@@ -146,7 +181,7 @@ def bsattn_fwd(
             _ptr(head_mask_type), scale,
             out.data_ptr(), _lib.strides4(out),
             _ptr(lse) if return_lse else None,
-            DeviceStatus.get(dev).data_ptr(),
+            DeviceStatus.pointer(dev),
             _stream(dev),
         )
     _lib.check(rc, "sa_bsattn_fwd")
@@ -203,7 +238,7 @@ def sink_dynamic_attn(
             math.log(float(max(1, int(sample_gap)))),
             -1.0 if softmax_scale is None else float(softmax_scale),
             out.data_ptr(), _lib.strides4(out), _ptr(lse),
-            DeviceStatus.get(dev).data_ptr(), _stream(dev),
+            DeviceStatus.pointer(dev), _stream(dev),
         )
     _lib.check(rc, "sa_sink_dynamic_attn_fwd")
     return out, lse
@@ -350,7 +385,7 @@ def block_stats(q: torch.Tensor, k: torch.Tensor, mode: str = "exact",
         rc = lib.sa_block_stats(q.data_ptr(), k.data_ptr(), _lib.strides4(q), _lib.strides4(k),
                                 B, H, S, D, m, sc, out.data_ptr(),
                                 workspace.data_ptr() if need else None, ws_bytes,
-                                DeviceStatus.get(dev).data_ptr(), _stream(dev))
+                                DeviceStatus.pointer(dev), _stream(dev))
     _lib.check(rc, "sa_block_stats")
     return out
 
@@ -434,7 +469,7 @@ def calibration_layer(
             _ptr(out.get("mask")), _ptr(out.get("flags")), mode_id, float(coverage),
             int(bool(keep_diagonal)), int(text_blocks), int(bool(force_sink_col)),
             workspace.data_ptr(), workspace.numel() * workspace.element_size(),
-            DeviceStatus.get(dev).data_ptr(), _stream(dev))
+            DeviceStatus.pointer(dev), _stream(dev))
     _lib.check(rc, "sa_calibration_layer")
     return out
 

@@ -43,6 +43,27 @@ HEAD_MASK_TYPE_MODE = "per_head"
 _BLOCK = 128
 
 
+def _reports_device_failures(fn):
+    """Checks, on entry, that no earlier kernel on the call's device
+    reported a bounded wait that gave up (ops.DeviceStatus, read from host
+    memory without synchronising) and raises RuntimeError if one did, so a
+    stalled launch surfaces at the next call instead of passing on wrong
+    outputs. Calls whose first tensor argument is not on a GPU go straight
+    through (they raise their own error)."""
+    import functools
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        for a in args:
+            if isinstance(a, torch.Tensor):
+                if a.is_cuda:
+                    ops.DeviceStatus.raise_if_set(a.device)
+                break
+        return fn(*args, **kwargs)
+
+    return wrapper
+
+
 def _hmt_host(head_mask_type: torch.Tensor) -> list[int]:
     # small int32 [H]; cached on the tensor's identity and version counter
     key = (head_mask_type.data_ptr(), head_mask_type._version, head_mask_type.numel())
@@ -56,6 +77,7 @@ def _hmt_host(head_mask_type: torch.Tensor) -> list[int]:
 _HMT_CACHE: dict = {}
 
 
+@_reports_device_failures
 def block_sparse_attn_func(
     q_unpad,
     k_unpad,
@@ -141,6 +163,7 @@ def block_sparse_attn_func(
     return out
 
 
+@_reports_device_failures
 def _block_sparse_attn(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -169,6 +192,7 @@ def _bf16(t: torch.Tensor) -> torch.Tensor:
     return t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
 
 
+@_reports_device_failures
 def _compute_pooled_qk_block_scores(q, k, v, config) -> torch.Tensor:
     """sparse_attention.py:118-142, [B,H,nb,nb] fp32.
 
@@ -186,6 +210,7 @@ def _compute_pooled_qk_block_scores(q, k, v, config) -> torch.Tensor:
     return scores
 
 
+@_reports_device_failures
 def _compute_exact_block_mass_scores(q, k, config) -> torch.Tensor:
     """sparse_attention.py:145-227: per query block, the mean over its rows of
     each key block's share of the row's softmax mass, [B,H,nq,nk] fp32, from
@@ -217,6 +242,7 @@ def _ceil_div(a: int, b: int) -> int:
     return (a + b - 1) // b
 
 
+@_reports_device_failures
 def _build_direct_mean_coverage_mask(mean_scores: torch.Tensor, config) -> torch.Tensor:
     """sparse_attention.py:268-376 on the GPU. The fp32 row totals (line 334,
     301) and selected sums (line 339) are taken with the same torch reduction
@@ -258,6 +284,7 @@ def _build_direct_mean_coverage_mask(mean_scores: torch.Tensor, config) -> torch
     return mask if mean_scores.is_cuda else mask.to(mean_scores.device)
 
 
+@_reports_device_failures
 def _mean_pool_sequence_preserve_prefix(x: torch.Tensor, pool_size: int, *, prefix_tokens: int = 0):
     """sparse_attention.py:97-115 (bf16 in/out, fp32 accumulation)."""
     if pool_size <= 1:
@@ -265,6 +292,7 @@ def _mean_pool_sequence_preserve_prefix(x: torch.Tensor, pool_size: int, *, pref
     return ops.mean_pool_seq(x, int(pool_size), int(prefix_tokens))
 
 
+@_reports_device_failures
 def _mean_pool_sequence(x: torch.Tensor, pool_size: int):
     """sparse_attention.py:88-94 for bf16 tensors (Z-Image pooled branch)."""
     if pool_size <= 1:
@@ -272,6 +300,7 @@ def _mean_pool_sequence(x: torch.Tensor, pool_size: int):
     return ops.mean_pool_seq(x, int(pool_size), 0)
 
 
+@_reports_device_failures
 def _mix_attention_outputs(sink_out, sink_lse, dynamic_out, dynamic_lse, config, dynamic_sample_gap=None):
     """sparse_attention.py:898-919 (adaptive mode) as one fused kernel."""
     if config.mixing_mode != "adaptive":
@@ -282,6 +311,7 @@ def _mix_attention_outputs(sink_out, sink_lse, dynamic_out, dynamic_lse, config,
     return ops.mix_outputs(sink_out, sink_lse, dynamic_out, dynamic_lse, gap)
 
 
+@_reports_device_failures
 def fused_wan_inner_forward(self, q, k, v):
     """WanSinkSparseInnerAttention.forward (wanx/runtime/sink_sparse_wan.py:181-282)
     with the sink call, the pooled K/V dynamic call and the adaptive mix fused
@@ -350,6 +380,7 @@ def _rms_like(norm) -> bool:
     return "layernorm" not in norm.__class__.__name__.lower() and getattr(norm, "bias", None) is None
 
 
+@_reports_device_failures
 def fused_prepare_attention_tensors(attn, hidden_states, encoder_hidden_states=None,
                                     rotary_emb=None):
     """_prepare_attention_tensors (wanx/runtime/sink_sparse_wan.py:285-315) for

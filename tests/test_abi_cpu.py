@@ -263,7 +263,9 @@ def header_signatures() -> dict[str, tuple[str, list[str]]]:
     return sigs
 
 
-_C_KINDS = {"int": "i32", "int32_t": "i32", "int64_t": "i64", "size_t": "size", "float": "f32"}
+# uint64_t and size_t are one ctypes type on LP64 (c_ulong)
+_C_KINDS = {"int": "i32", "int32_t": "i32", "int64_t": "i64", "uint64_t": "size",
+            "size_t": "size", "float": "f32"}
 
 
 def _c_kind(decl: str, is_return: bool = False) -> str:
@@ -305,3 +307,24 @@ def test_install_skips_absent_routes_unless_named(monkeypatch):
     assert ra.install() == []
     with pytest.raises(ImportError):
         ra.install(modules=["sinkattn_absent_route.runtime"])
+
+
+def test_status_word_check_and_selftest_validation(lib):
+    """sa_check_status reads any host int32: a non-zero code is reported as
+    SA_ETIMEOUT with a message and the word is reset; the self-test refuses a
+    limit outside [1 us, 1 s] before it launches anything."""
+    from sinkattn_b200 import _lib
+
+    word = ctypes.c_int32(0)
+    assert lib.sa_check_status(ctypes.addressof(word)) == _lib.SA_OK
+    word.value = 1  # SA_DEV_WAIT_TIMEOUT, as a kernel writes it
+    assert lib.sa_check_status(ctypes.addressof(word)) == _lib.SA_ETIMEOUT
+    assert "bounded wait" in _lib.last_error()
+    assert word.value == 0
+    assert lib.sa_check_status(ctypes.addressof(word)) == _lib.SA_OK
+    assert lib.sa_check_status(None) == _lib.SA_EINVAL
+    assert lib.sa_status_destroy(None) == _lib.SA_OK
+    assert lib.sa_selftest_wait_timeout(ctypes.addressof(word), 10, None) == _lib.SA_EINVAL
+    assert "limit" in _lib.last_error()
+    assert lib.sa_selftest_wait_timeout(ctypes.addressof(word), 2 * 10**9, None) == _lib.SA_EINVAL
+    assert lib.sa_selftest_wait_timeout(None, 10**6, None) == _lib.SA_EINVAL
