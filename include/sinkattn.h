@@ -214,18 +214,18 @@ SA_API int sa_pooled_softmax_layers(const float* qp, const float* kp, int L, int
  *   (mode, coverage, keep_diagonal, text_blocks, force_sink_col as there)
  *   on the batch mean, with row totals summed in fp64 and rounded;
  *   row_flags: nullable int32 [H,nb] SA_ROW_* bits (needs mask_out).
- * At least one output must be requested. The results equal sa_pool_scores
- * followed by sa_score_accumulate and sa_coverage_mask (row_total NULL) on
- * its batch mean, bit for bit. The environment variable
- * SINKATTN_CALIB_SCORE_CTAS, when set, gives the number of CTAs that score
- * from the start (default about a fifth of the SMs).
+ * At least one output must be requested. The scores and batch mean equal
+ * those of the three-kernel chain (pooling, pooled logits, softmax) to
+ * within one ulp; the sums and the mask are exactly what
+ * sa_score_accumulate and sa_coverage_mask (row_total NULL) give on this
+ * launch's batch mean.
  * workspace: sa_calibration_layer_workspace_size() bytes, 256-byte aligned,
  *   with any contents: work counters and flags tagged with a per-launch
  *   number (so nothing needs clearing), the pooled Q and K, and a batch-mean
  *   scratch. Calls sharing one workspace must not overlap on the GPU. H is at
  *   most 128.
- * scale <= 0 selects 1/sqrt(128). status: as sa_bsattn_fwd; the rows whose
- *   wait gave up get NaN scores and all-kept mask rows.
+ * scale <= 0 selects 1/sqrt(128). status: as sa_bsattn_fwd; once a wait
+ *   gives up, the launch's outputs are not valid.
  */
 SA_API size_t sa_calibration_layer_workspace_size(int B, int H, int S);
 SA_API int sa_calibration_layer(const void* q, const void* k, const int64_t q_strides[4],

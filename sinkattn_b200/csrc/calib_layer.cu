@@ -10,31 +10,30 @@
 //   [mask  = coverage rule on mean]                          (lines 241-376)
 //
 // The pooling reads the layer's Q and K once and is HBM-bound; the rest is
-// small but latency-bound, so it runs on other SMs and warps while the
-// pooling streams, head by head. CTAs (one per SM) take a role by the order
-// in which they start:
-//   * pooling CTAs (the first to start). Warps 0-2 each own a fixed share of
-//     the (head, batch, q|k, block) items, in head-major order, stream each
-//     item's 128 x 128 bf16 tile through two 32 KB TMA stages, write its fp32
-//     block mean (Q row-major [B,H,nb,128], K transposed [B,H,128,nb]) and
-//     count it in shared memory (a CTA-scope release only). Warp 3 publishes
-//     those counts per head to global memory about every half microsecond
-//     behind one GPU-scope fence: the fence sits in a warp with no TMA load
-//     in flight, so the streaming warps never wait on it. Warps 4-10 take
-//     coverage rows whose batch mean is already published. When the CTA's
-//     items are done, warps 3-10 join the score work below.
-//   * score CTAs (the rest, about a fifth). Warps 3-10 take (head, 16 query
-//     rows) items once every item of the head is counted, bulk-copy the
-//     head's pooled K (four 32 KB channel chunks) and the rows' pooled Q into
-//     shared memory, and compute the logits (each thread 4 rows x 4 keys),
-//     the softmax per batch element (warp = row), the batch mean and the
-//     optional running sums, then publish the 16 rows' batch mean. When no
-//     item is left they take coverage rows (warp = row, coverage_row.cuh).
+// small but latency-bound, so it runs beside the pooling on every SM while
+// the pooling streams, head by head. One CTA per SM, all alike:
+//   * warps 0-2 pool. The (head, batch, q|k, block) items, in head-major
+//     order, are dealt round robin to the pooling warps of all CTAs; each
+//     block streams as two 64-token halves through the warp's two 16 KB TMA
+//     stages. A copy engine moves about 60 GB/s into one SM's shared memory,
+//     so the HBM stream needs the TMA units of (nearly) every SM. The warp
+//     writes the fp32 block mean (row-major [B,H,nb,128], one float4 per
+//     lane) and counts it in shared memory (a CTA-scope release only).
+//   * warp 3 publishes those counts per head to global memory about every
+//     half microsecond behind one GPU-scope fence: the fence sits in a warp
+//     with no TMA load in flight, so the streaming warps never wait on it.
+//   * warps 4-11 take, as a group, (head, 16 query rows) score items in
+//     order, each once every item of its head is counted, and after the last
+//     item is taken, coverage tasks of eight rows, each once its rows' batch
+//     mean is published. An item streams the head's pooled K (TMA,
+//     16-channel chunks) and the rows' pooled Q into shared memory and computes the
+//     logits (each thread 8 rows x 4 keys), the softmax per batch element
+//     (warp = row), the batch mean and the optional running sums, then
+//     publishes the rows' batch mean. A coverage row is one warp
+//     (coverage_row.cuh).
 // So only the last head's score items and coverage rows run after the HBM
-// read ends, spread over every SM. Roles go by start order, so a score CTA
-// never holds an SM that a pooling CTA still has to start on; pooling warps
-// never wait on other CTAs, and coverage rows taken while pooling are only
-// rows that are already published, so every wait ends.
+// read ends. Pooling warps never wait on other CTAs, and the task warps take
+// only work whose inputs are complete or in progress, so every wait ends.
 //
 // Counters live in the caller's workspace, each on its own 128-byte line.
 // The work counters are 64-bit words whose high half is the launch's epoch
@@ -66,58 +65,64 @@
 namespace sa {
 namespace calib {
 
-constexpr int kPoolWarps = 3;               // warps 0-2 of a pooling CTA
-constexpr int kScoreWarp0 = 3;              // warps 3-10: signal / score / coverage
+constexpr int kPoolWarps = 3;               // warps 0-2: pooling
+constexpr int kSignalWarp = 3;              // warp 3: publishes the head counts
+constexpr int kScoreWarp0 = 4;              // warps 4-11: score items and coverage rows
 constexpr int kScoreWarps = 8;
 constexpr int kScoreThreads = kScoreWarps * 32;
-constexpr int kThreads = (kPoolWarps + kScoreWarps) * 32;
+constexpr int kThreads = (kScoreWarp0 + kScoreWarps) * 32;
 constexpr int kRows = 16;                   // query rows per score item
 constexpr int kD = 128;
-constexpr int kStageBytes = 128 * 128 * 2;  // one bf16 128 x 128 tile
+constexpr int kHalf = 64;                   // tokens per pooling stage
+constexpr int kStageBytes = kHalf * 128 * 2;  // 64 x 128 bf16 = 16 KB
 constexpr int kMaxBlocks = 256;
 constexpr int kMaxHeads = 128;
-constexpr int kKChunks = 4;                 // pooled-K channel chunks of a score item
-constexpr int kKChunkD = kD / kKChunks;     // 32 channels = 32 KB at 256 blocks
+constexpr int kKChunks = 8;                 // pooled-K channel chunks of one batch element
+constexpr int kKChunkD = kD / kKChunks;     // 16 channels = 16 KB at 256 blocks
+constexpr int kKBufs = 2;                   // chunk buffers per batch element of a pair
+constexpr int kKBufBytes = kKChunkD * kMaxBlocks * 4;
 
 // counters, one per 128-byte line; [0..3] epoch-tagged, [4] holds the epoch
 // once the head counts are cleared, [5 + h] pooling items finished of head h
 constexpr int kCtrStride = 128 / 8;  // 64-bit words per line
-constexpr int kRoleCtr = 0, kScoreCtr = 1, kCovCtr = 2, kDoneCtr = 3, kReady = 4, kHead0 = 5;
+constexpr int kStartCtr = 0, kScoreCtr = 1, kCovCtr = 2, kDoneCtr = 3, kReady = 4, kHead0 = 5;
 size_t counter_bytes(int H) { return (((size_t)(kHead0 + H) * 128) + 255) & ~size_t(255); }
 // "batch mean published" flag of every (head, group of kRows rows)
 size_t flag_bytes(int H, int nb) {
   return (((size_t)H * ((nb + kRows - 1) / kRows) * 8) + 255) & ~size_t(255);
 }
 
-// Shared memory. The pooling stages and the score items' pooled-K chunks and
-// pooled-Q rows share the first 192 KB (a CTA pools first, then scores).
+// Shared memory of one CTA (NPAD = keys rounded up to a power of two).
 template <int NPAD>
 struct Layout {
-  static constexpr size_t stages = 0;                                   // pooling: 6 x 32 KB
-  static constexpr size_t kslots = 0;                                   // scores: 4 x 32 KB
-  static constexpr size_t qs = kslots + (size_t)kKChunks * kKChunkD * kMaxBlocks * 4;  // [2][16][128]
-  static constexpr size_t bars = stages + (size_t)kPoolWarps * 2 * kStageBytes;
-  static constexpr size_t ebuf = bars + 128;                            // [16][NPAD] fp32
-  static constexpr size_t cov = ebuf + (size_t)kRows * NPAD * 4;        // [8][2*NPAD] u32
-  static constexpr size_t hcnt = cov + (size_t)kScoreWarps * 2 * NPAD * 4;  // [kMaxHeads] int
-  static constexpr size_t hpub = hcnt + (size_t)kMaxHeads * 4;          // [kMaxHeads] int
-  static constexpr size_t ctl = hpub + (size_t)kMaxHeads * 4;           // 16 ints
-  static constexpr size_t total = ctl + 64 + 1024;                      // + base alignment
+  static constexpr size_t stages = 0;                                      // [3][2] x 16 KB
+  static constexpr size_t kslots = stages + (size_t)kPoolWarps * 2 * kStageBytes;  // [2][2] x 16 KB
+  static constexpr size_t qs = kslots + (size_t)2 * kKBufs * kKBufBytes;  // [2][16][128] fp32
+  // logits / probabilities of a pair [2][16][NPAD] fp32; coverage rows use
+  // the same bytes between items: [8][NPAD] fp32 values, [8][2*NPAD] words
+  static constexpr size_t lbuf = qs + (size_t)2 * kRows * kD * 4;
+  static constexpr size_t rowbuf = lbuf;
+  static constexpr size_t cov = rowbuf + (size_t)kScoreWarps * NPAD * 4;
+  static constexpr size_t bars = lbuf + (size_t)2 * kRows * 256 * 4;
+  static constexpr size_t hcnt = bars + 128;                               // [kMaxHeads] int
+  static constexpr size_t hpub = hcnt + (size_t)kMaxHeads * 4;             // [kMaxHeads] int
+  static constexpr size_t ctl = hpub + (size_t)kMaxHeads * 4;              // 16 ints
+  static constexpr size_t total = ctl + 64 + 1024;                         // + base alignment
 };
 static_assert(Layout<256>::total <= 232448, "shared memory layout exceeds 227 KB");
-static_assert(Layout<256>::qs + (size_t)2 * kRows * kD * 4 <= Layout<256>::bars,
-              "pooled-Q buffers overlap the barriers");
-// barriers: [2w, 2w+1] pooling warp w's stages, [6 + c] pooled-K chunk slot
-// c, [10 + q] pooled-Q buffer q
-// ctl: [0] score item, [1] its head is complete, [2] role (1 = pool),
-//      [3] pooling warps done, [4] ticket, [5] pooling published
+static_assert(Layout<256>::cov + (size_t)kScoreWarps * 2 * 256 * 4 <= Layout<256>::bars,
+              "coverage scratch overlaps the barriers");
+static_assert(Layout<256>::kslots % 1024 == 0, "swizzled pooled-K buffers need 1 KB alignment");
+// barriers: [2w, 2w+1] pooling warp w's stages, [6 + 2 bsel + buf] pooled-K
+// buffer buf of the pair's batch element bsel, [10 + bsel] its pooled-Q rows
+// ctl: [0] claimed item or task, [1] its inputs are complete, [3] pooling
+//      warps done, [5] pooling published
 
 struct Params {
   int B, H, S, nb, G;   // G = score items (groups of kRows rows) per head
-  int pool_ctas;        // CTAs that pool first (the first to start)
   float scale;
   float* qp;            // [B,H,nb,128]
-  float* kpt;           // [B,H,128,nb]
+  float* kp;            // [B,H,nb,128]
   float* bm_scratch;    // [H,nb,nb] batch mean when the caller wants a mask only
   unsigned long long* ctr;
   unsigned long long* gflag;  // [H*G]
@@ -146,9 +151,10 @@ __device__ __forceinline__ uint32_t epoch_count(unsigned long long v, uint32_t e
 
 // Adds 1 to an epoch-tagged counter and returns this launch's count before
 // the add. A counter left at another epoch is claimed for this one; only the
-// claimer sees 0.
-__device__ __forceinline__ uint32_t epoch_add(unsigned long long* c, uint32_t epoch) {
-  unsigned long long cur = atomicAdd(c, 1ull);
+// claimer sees 0. The add is split so that a caller can issue the atomic
+// early and look at its result (epoch_add_finish) only where it needs it.
+__device__ __forceinline__ uint32_t epoch_add_finish(unsigned long long* c, uint32_t epoch,
+                                                     unsigned long long cur) {
   while ((uint32_t)(cur >> 32) != epoch) {
     // another epoch: this add went to the stale value cur + 1
     const unsigned long long stale = cur + 1ull;
@@ -158,6 +164,9 @@ __device__ __forceinline__ uint32_t epoch_add(unsigned long long* c, uint32_t ep
     cur = (uint32_t)(prev >> 32) == epoch ? atomicAdd(c, 1ull) : prev - 1ull;
   }
   return (uint32_t)cur;
+}
+__device__ __forceinline__ uint32_t epoch_add(unsigned long long* c, uint32_t epoch) {
+  return epoch_add_finish(c, epoch, atomicAdd(c, 1ull));
 }
 
 __device__ __forceinline__ void score_bar() {
@@ -207,15 +216,14 @@ __device__ __forceinline__ void coverage_of_row(const Params& p, int r, float* r
 template <int NPAD>
 __global__ void __launch_bounds__(kThreads, 1)
     calib_layer_kernel(const __grid_constant__ CUtensorMap tm_q,
-                       const __grid_constant__ CUtensorMap tm_k, const Params p) {
+                       const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_kp, const Params p) {
   using L = Layout<NPAD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bars);
   float* qs = reinterpret_cast<float*>(smem + L::qs);
-  float* ebuf = reinterpret_cast<float*>(smem + L::ebuf);
-  uint32_t* covs = reinterpret_cast<uint32_t*>(smem + L::cov);
   int* hcnt = reinterpret_cast<int*>(smem + L::hcnt);
   int* hpub = reinterpret_cast<int*>(smem + L::hpub);
   volatile int* ctl = reinterpret_cast<volatile int*>(smem + L::ctl);
@@ -225,7 +233,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int per_head = 2 * p.B * nb;  // pooling items of one head
   const int n_pool = p.H * per_head;
   const int n_score = p.H * p.G;
-  const int n_rows = p.H * nb;        // coverage rows
 
   for (int i = threadIdx.x; i < p.H; i += kThreads) {
     hcnt[i] = 0;
@@ -234,216 +241,213 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 12; ++i) mbar_init(&bars[i], 1);
     fence_barrier_init();
-    const uint32_t ticket = epoch_add(&p.ctr[kRoleCtr * kCtrStride], p.epoch);
-    if (ticket == 0u) {
-      // the first CTA clears the head counts, then publishes the epoch
+    if (epoch_add(&p.ctr[kStartCtr * kCtrStride], p.epoch) == 0u) {
+      // the first CTA to start clears the head counts, then publishes the epoch
       volatile unsigned long long* c = p.ctr;
       for (int h = 0; h < p.H; ++h) c[(kHead0 + h) * kCtrStride] = 0ull;
       __threadfence();
       c[kReady * kCtrStride] = (unsigned long long)p.epoch;
     }
-    ctl[2] = ticket < (uint32_t)p.pool_ctas ? 1 : 0;
     ctl[3] = 0;
-    ctl[4] = (int)ticket;
     ctl[5] = 0;
   }
   __syncthreads();
-  const bool pool_role = ctl[2] != 0;
 
   if (warp < kPoolWarps) {
-    if (pool_role) {
-      // ------------------------------------------------------------- pooling
-      uint8_t* stage0 = smem + L::stages + (size_t)warp * 2 * kStageBytes;
-      uint64_t* full = &bars[2 * warp];
-      if (lane == 0) {
-        prefetch_tensormap(&tm_q);
-        prefetch_tensormap(&tm_k);
+    // --------------------------------------------------------------- pooling
+    // Items (head, batch, q|k, block) in head-major order, dealt to the warps
+    // of all CTAs round robin; each block streams as two 64-token halves
+    // through this warp's two 16 KB stages.
+    uint8_t* stage0 = smem + L::stages + (size_t)warp * 2 * kStageBytes;
+    uint64_t* full = &bars[2 * warp];
+    if (lane == 0) {
+      prefetch_tensormap(&tm_q);
+      prefetch_tensormap(&tm_k);
+    }
+    const int stride = gridDim.x * kPoolWarps;
+    const int first = blockIdx.x * kPoolWarps + warp;
+    auto issue = [&](int it, int half, int st) {
+      const int h = it / per_head;
+      const int r = it - h * per_head;
+      const int b = r / (2 * nb);
+      const int r2 = r - b * 2 * nb;
+      const int t = r2 / nb;
+      const int j = r2 - t * nb;
+      mbar_arrive_expect_tx(&full[st], kStageBytes);
+      tma_load_4d(t ? &tm_k : &tm_q, &full[st], stage0 + (size_t)st * kStageBytes, 0,
+                  j * 128 + half * kHalf, h, b);
+    };
+    // halves n = 0, 1, 2, ...: item first + (n / 2) * stride, half n % 2
+    const int n_mine = first < n_pool ? 2 * ((n_pool - 1 - first) / stride + 1) : 0;
+    if (lane == 0 && n_mine > 0) issue(first, 0, 0);
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+    uint2 last = make_uint2(0u, 0u);  // the block's final token (ragged blocks)
+    for (int n = 0; n < n_mine; ++n) {
+      const int st = n & 1;
+      const int item = first + (n >> 1) * stride;
+      const int half = n & 1;
+      __syncwarp();  // every lane is done reading stage st ^ 1 (half n - 1)
+      if (lane == 0 && n + 1 < n_mine) {
+        fence_proxy_async_smem();
+        issue(first + ((n + 1) >> 1) * stride, (n + 1) & 1, st ^ 1);
       }
-      // this warp's share: items first, first + stride, ... (head-major order)
-      const int stride = p.pool_ctas * kPoolWarps;
-      auto issue = [&](int it, int st) {
-        const int h = it / per_head;
-        const int r = it - h * per_head;
-        const int b = r / (2 * nb);
-        const int r2 = r - b * 2 * nb;
-        const int t = r2 / nb;
-        const int j = r2 - t * nb;
-        mbar_arrive_expect_tx(&full[st], kStageBytes);
-        tma_load_4d(t ? &tm_k : &tm_q, &full[st], stage0 + (size_t)st * kStageBytes, 0, j * 128,
-                    h, b);
-      };
-      int item = ctl[4] * kPoolWarps + warp;
-      int next = item + stride;
-      if (lane == 0 && item < n_pool) issue(item, 0);
-      for (int k = 0; item < n_pool; ++k) {
-        const int st = k & 1;
-        __syncwarp();  // every lane is done reading stage st ^ 1 (item k - 1)
-        if (lane == 0 && next < n_pool) {
-          fence_proxy_async_smem();
-          issue(next, st ^ 1);
-        }
-        if (!mbar_wait_drain(&full[st], (uint32_t)(k >> 1) & 1u)) {
-          if (lane == 0) report_timeout(p.status);
-          break;
-        }
-        const uint8_t* tile = stage0 + (size_t)st * kStageBytes + lane * 8;
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-        float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+      if (!mbar_wait_drain(&full[st], (uint32_t)(n >> 1) & 1u)) {
+        if (lane == 0) report_timeout(p.status);
+        break;
+      }
+      const int h = item / per_head;
+      const int r = item - h * per_head;
+      const int b = r / (2 * nb);
+      const int r2 = r - b * 2 * nb;
+      const int t = r2 / nb;
+      const int j = r2 - t * nb;
+      const int valid = min(128, p.S - j * 128);
+      const uint8_t* tile = stage0 + (size_t)st * kStageBytes + lane * 8;
+      // even rows into a*, odd rows into b*, in row order across both halves
 #pragma unroll 8
-        for (int r = 0; r < 128; r += 2) {
-          const uint2 u = *reinterpret_cast<const uint2*>(tile + r * 256);
-          const uint2 w = *reinterpret_cast<const uint2*>(tile + (r + 1) * 256);
-          a0 += __uint_as_float(u.x << 16); a1 += __uint_as_float(u.x & 0xffff0000u);
-          a2 += __uint_as_float(u.y << 16); a3 += __uint_as_float(u.y & 0xffff0000u);
-          b0 += __uint_as_float(w.x << 16); b1 += __uint_as_float(w.x & 0xffff0000u);
-          b2 += __uint_as_float(w.y << 16); b3 += __uint_as_float(w.y & 0xffff0000u);
-        }
-        a0 += b0; a1 += b1; a2 += b2; a3 += b3;
-        const int h = item / per_head;
-        const int r = item - h * per_head;
-        const int b = r / (2 * nb);
-        const int r2 = r - b * 2 * nb;
-        const int t = r2 / nb;
-        const int j = r2 - t * nb;
-        const int valid = min(128, p.S - j * 128);
-        if (valid < 128) {
-          // rows past S arrived zero-filled; the final token stands in for them
-          const uint2 u = *reinterpret_cast<const uint2*>(tile + (valid - 1) * 256);
-          const float wgt = (float)(128 - valid);
-          a0 += wgt * __uint_as_float(u.x << 16); a1 += wgt * __uint_as_float(u.x & 0xffff0000u);
-          a2 += wgt * __uint_as_float(u.y << 16); a3 += wgt * __uint_as_float(u.y & 0xffff0000u);
-        }
-        const float inv = 1.0f / 128.0f;
-        const int64_t bh = (int64_t)b * p.H + h;
-        if (t == 0) {
-          float* outp = p.qp + (bh * nb + j) * kD + lane * 4;
-          *reinterpret_cast<float4*>(outp) = make_float4(a0 * inv, a1 * inv, a2 * inv, a3 * inv);
-        } else {
-          float* col = p.kpt + (bh * kD + lane * 4) * nb + j;
-          col[0] = a0 * inv;
-          col[nb] = a1 * inv;
-          col[2 * nb] = a2 * inv;
-          col[3 * nb] = a3 * inv;
-        }
-        // count the item in shared memory (CTA-scope release); warp 3
-        // publishes the counts with the GPU-scope fence
-        __syncwarp();
-        if (lane == 0) {
-          __threadfence_block();
-          atomicAdd(&hcnt[h], 1);
-        }
-        item = next;
-        next += stride;
+      for (int rr = 0; rr < kHalf; rr += 2) {
+        const uint2 u = *reinterpret_cast<const uint2*>(tile + rr * 256);
+        const uint2 w = *reinterpret_cast<const uint2*>(tile + (rr + 1) * 256);
+        a0 += __uint_as_float(u.x << 16); a1 += __uint_as_float(u.x & 0xffff0000u);
+        a2 += __uint_as_float(u.y << 16); a3 += __uint_as_float(u.y & 0xffff0000u);
+        b0 += __uint_as_float(w.x << 16); b1 += __uint_as_float(w.x & 0xffff0000u);
+        b2 += __uint_as_float(w.y << 16); b3 += __uint_as_float(w.y & 0xffff0000u);
       }
+      if (valid < 128 && (valid - 1) / kHalf == half)
+        last = *reinterpret_cast<const uint2*>(tile + ((valid - 1) % kHalf) * 256);
+      if (half == 0) continue;
+      a0 += b0; a1 += b1; a2 += b2; a3 += b3;
+      if (valid < 128) {
+        // rows past S arrived zero-filled; the final token stands in for them
+        const float wgt = (float)(128 - valid);
+        a0 += wgt * __uint_as_float(last.x << 16); a1 += wgt * __uint_as_float(last.x & 0xffff0000u);
+        a2 += wgt * __uint_as_float(last.y << 16); a3 += wgt * __uint_as_float(last.y & 0xffff0000u);
+      }
+      const float inv = 1.0f / 128.0f;
+      const int64_t bh = (int64_t)b * p.H + h;
+      float* outp = (t ? p.kp : p.qp) + (bh * nb + j) * kD + lane * 4;
+      *reinterpret_cast<float4*>(outp) = make_float4(a0 * inv, a1 * inv, a2 * inv, a3 * inv);
+      a0 = a1 = a2 = a3 = b0 = b1 = b2 = b3 = 0.f;
+      // count the item in shared memory (CTA-scope release); the signal warp
+      // publishes the counts with the GPU-scope fence
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
-        atomicAdd(const_cast<int*>(&ctl[3]), 1);
+        atomicAdd(&hcnt[h], 1);
       }
     }
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      atomicAdd(const_cast<int*>(&ctl[3]), 1);
+    }
+  } else if (warp == kSignalWarp) {
+    // ----------------------------------------------------- publish head counts
+    if (lane == 0) {
+      spin_until([&] { return ld_acquire(&p.ctr[kReady * kCtrStride]) ==
+                              (unsigned long long)p.epoch; },
+                 p.status, 64);
+      for (;;) {
+        const int done = ctl[3];
+        __threadfence();  // acquire the counts (and the pooled values behind them)
+        bool any = false;
+        for (int h = 0; h < p.H; ++h)
+          any |= *reinterpret_cast<volatile int*>(&hcnt[h]) != hpub[h];
+        if (any) {
+          __threadfence();
+          for (int h = 0; h < p.H; ++h) {
+            const int c = *reinterpret_cast<volatile int*>(&hcnt[h]);
+            if (c != hpub[h]) {
+              atomicAdd(&p.ctr[(kHead0 + h) * kCtrStride], (unsigned long long)(c - hpub[h]));
+              hpub[h] = c;
+            }
+          }
+        }
+        if (done == kPoolWarps) break;
+        __nanosleep(400);
+      }
+      ctl[5] = 1;
+    }
+    __syncwarp();
   } else {
     const int sw = warp - kScoreWarp0;  // 0..7
     const int tid = threadIdx.x - kScoreWarp0 * 32;
-    float* rowbuf = ebuf + (size_t)sw * NPAD;
-    uint32_t* skey = covs + (size_t)sw * 2 * NPAD;
-    if (pool_role) {
-      if (warp == kScoreWarp0) {
-        // ----------------------------------------------- publish head counts
-        if (lane == 0) {
-          spin_until([&] { return ld_acquire(&p.ctr[kReady * kCtrStride]) ==
-                                  (unsigned long long)p.epoch; },
-                     p.status, 64);
-          for (;;) {
-            const int done = ctl[3];
-            __threadfence();  // acquire the counts (and the pooled values behind them)
-            bool any = false;
-            for (int h = 0; h < p.H; ++h)
-              any |= *reinterpret_cast<volatile int*>(&hcnt[h]) != hpub[h];
-            if (any) {
-              __threadfence();
-              for (int h = 0; h < p.H; ++h) {
-                const int c = *reinterpret_cast<volatile int*>(&hcnt[h]);
-                if (c != hpub[h]) {
-                  atomicAdd(&p.ctr[(kHead0 + h) * kCtrStride], (unsigned long long)(c - hpub[h]));
-                  hpub[h] = c;
-                }
-              }
-            }
-            if (done == kPoolWarps) break;
-            __nanosleep(400);
-          }
-          ctl[5] = 1;
-        }
-        __syncwarp();
-      } else if (p.mask != nullptr) {
-        // ------------------------------ coverage rows that are published already
-        for (;;) {
-          int r = -1;
-          int ok = 0;
-          if (lane == 0) {
-            unsigned long long* c = &p.ctr[kCovCtr * kCtrStride];
-            unsigned long long cur = ld_acquire(c);
-            for (int tries = 0; tries < 8 && ctl[5] == 0; ++tries) {
-              const uint32_t row = epoch_count(cur, p.epoch);
-              if (row >= (uint32_t)n_rows) break;
-              const int g = (int)(row / nb) * p.G + (int)(row % nb) / kRows;
-              if (ld_acquire(&p.gflag[g]) != (unsigned long long)p.epoch) break;
-              const unsigned long long want = ((unsigned long long)p.epoch << 32) | (row + 1u);
-              const unsigned long long prev = atomicCAS(c, cur, want);
-              if (prev == cur) {
-                r = (int)row;
-                ok = 1;
-                break;
-              }
-              cur = prev;
-            }
-          }
-          // the row and its verdict go to the whole warp: coverage_row is
-          // warp-collective
-          r = __shfl_sync(0xffffffffu, r, 0);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (r < 0) {
-            // nothing published yet: look again later, or stop once pooling is done
-            if (__shfl_sync(0xffffffffu, (int)ctl[5], 0) != 0) break;
-            __nanosleep(1000);
-            continue;
-          }
-          coverage_of_row<NPAD>(p, r, rowbuf, skey, lane, ok != 0);
-        }
-      }
-      // warps 3-10 turn to score items once this CTA's pooling is published
-      asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
-    }
-
-    // ------------------------------------------------------------ score items
-    uint64_t* kbar = &bars[6];
-    uint64_t* qbar = &bars[10];
-    uint32_t kpar = 0u, qpar = 0u;  // parity of the next completion of each slot / buffer
+    float* rowbuf = reinterpret_cast<float*>(smem + L::rowbuf) + (size_t)sw * NPAD;
+    uint32_t* skey = reinterpret_cast<uint32_t*>(smem + L::cov) + (size_t)sw * 2 * NPAD;
+    // ---------------------------------------------------------------- tasks
+    // A score item is (head h, kRows query rows) over every batch element,
+    // a pair of batch elements at a time. Score warp w computes logits of
+    // batch element w / 4 of the pair, rows 8 ((w / 2) % 2) .. +7, and keys
+    // lane + 32 (w % 2 + 2 j): per 4 channels a lane reads 8 broadcast Q
+    // float4 and 4 K float4 for 128 fmaf, each sum in channel order. Pooled K
+    // ([B,H,nb,128] fp32, the layout the pooling writes with whole-sector
+    // stores) streams through kKBufs TMA buffers of kKChunkD channels per
+    // batch element, each [nb keys][16 channels] with the 64-byte swizzle,
+    // so the lanes' key rows fall in distinct banks.
+    constexpr int KJ = NPAD >= 64 ? NPAD / 64 : 1;  // keys per lane
+    uint64_t* kbar = &bars[6];                 // [bsel * kKBufs + buf]
+    uint64_t* qbar = &bars[6 + 2 * kKBufs];    // [bsel]
+    uint32_t kpar = 0u, qpar = 0u;  // parity of the next completion of each buffer
     const uint32_t kbytes = (uint32_t)(kKChunkD * nb * 4);
     const float invb = 1.0f / (float)p.B;
-    // thread tile: rows r0 .. r0 + 3 and keys kb .. kb + 3
+    const int npairs = (p.B + 1) / 2;
+    const int gb = sw >> 2;                // logits: batch element of the pair
+    const int grow = 8 * ((sw >> 1) & 1);  // logits: first of the 8 rows
+    const int kh = sw & 1;                 // logits: key interleave
+    // output thread tile: rows r0 .. r0 + 3 and keys kb .. kb + 3
     const int r0 = 4 * (sw >> 1);
     const int kb = 4 * (32 * (sw & 1) + lane);
-    const bool vec4 = (nb & 3) == 0;
-    auto kslot = [&](int c) -> float* {
-      return reinterpret_cast<float*>(smem + L::kslots + (size_t)c * kKChunkD * kMaxBlocks * 4);
+    float* lbuf = reinterpret_cast<float*>(smem + L::lbuf);
+    auto kslot = [&](int bsel, int buf) -> uint8_t* {
+      return smem + L::kslots + (size_t)(bsel * kKBufs + buf) * kKBufBytes;
     };
     auto wait_copy = [&](uint64_t* bar, uint32_t parity) {
-      if (!mbar_wait_drain(bar, parity) && tid == 0) report_timeout(p.status);
+      if (!mbar_wait_drain(bar, parity) && lane == 0) report_timeout(p.status);
     };
-    // the stage region was last written by TMA and read by generic loads
-    if (tid == 0) fence_proxy_async_all();
+    auto item_rows = [&](int s, int& h, int& i0, int& nrows) {
+      h = s / p.G;
+      i0 = (s - h * p.G) * kRows;
+      nrows = min(kRows, nb - i0);
+    };
+    auto head_ready = [&](int s) {
+      return ld_acquire(&p.ctr[(kHead0 + s / p.G) * kCtrStride]) >=
+             (unsigned long long)per_head;
+    };
+    auto issue_k = [&](int h, int b, int bsel, int c) {
+      uint64_t* bar = &kbar[bsel * kKBufs + c % kKBufs];
+      mbar_arrive_expect_tx(bar, kbytes);
+      tma_load_2d(&tm_kp, bar, kslot(bsel, c % kKBufs), c * kKChunkD, (b * p.H + h) * nb);
+    };
+    // Q rows and the first kKBufs K chunks of pair bp. The head's data was
+    // written by other CTAs (generic stores, seen through an acquire of its
+    // count). The buffers were last read by this CTA's generic loads before a
+    // barrier, as in a producer / consumer pipeline.
+    auto issue_pair = [&](int s, int bp) {
+      int h, i0, nrows;
+      item_rows(s, h, i0, nrows);
+      fence_proxy_async_global();
+      for (int bsel = 0; bsel < 2; ++bsel) {
+        const int b = 2 * bp + bsel;
+        if (b >= p.B) break;
+        const int64_t bh = (int64_t)b * p.H + h;
+        const uint32_t qbytes = (uint32_t)nrows * kD * 4;
+        mbar_arrive_expect_tx(&qbar[bsel], qbytes);
+        bulk_load(qs + bsel * kRows * kD, p.qp + (bh * nb + i0) * kD, qbytes, &qbar[bsel]);
+        for (int c = 0; c < kKBufs; ++c) issue_k(h, b, bsel, c);
+      }
+    };
+    if (tid == 0) prefetch_tensormap(&tm_kp);
+    // phase 1: score items, claimed in order with one fetch-and-add each
     for (;;) {
       if (tid == 0) {
         const int s = (int)epoch_add(&p.ctr[kScoreCtr * kCtrStride], p.epoch);
-        int ok = 0;
-        if (s < n_score) {
-          const unsigned long long* cnt = &p.ctr[(kHead0 + s / p.G) * kCtrStride];
+        int ok = 1;
+        if (s < n_score)
           ok = spin_until([&] {
-                 return ld_acquire(&p.ctr[kReady * kCtrStride]) == (unsigned long long)p.epoch &&
-                        ld_acquire(cnt) >= (unsigned long long)per_head;
+                 return ld_acquire(&p.ctr[kReady * kCtrStride]) ==
+                            (unsigned long long)p.epoch && head_ready(s);
                }, p.status, 256) ? 1 : 0;
-        }
         ctl[0] = s;
         ctl[1] = ok;
       }
@@ -452,10 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ok = ctl[1];
       score_bar();
       if (s >= n_score) break;
-      const int h = s / p.G;
-      const int g = s - h * p.G;
-      const int i0 = g * kRows;
-      const int nrows = min(kRows, nb - i0);
+      int h, i0, nrows;
+      item_rows(s, h, i0, nrows);
       if (!ok) {
         // a wait gave up (status set): the item's outputs are marked invalid
         for (int e = tid; e < nrows * nb; e += kScoreThreads) {
@@ -471,110 +473,141 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
       }
-      const uint32_t qbytes = (uint32_t)nrows * kD * 4;
-      auto issue_q = [&](int b) {
-        const int64_t bh = (int64_t)b * p.H + h;
-        mbar_arrive_expect_tx(&qbar[b & 1], qbytes);
-        bulk_load(qs + (b & 1) * kRows * kD, p.qp + (bh * nb + i0) * kD, qbytes, &qbar[b & 1]);
-      };
-      auto issue_k = [&](int b, int c) {
-        const int64_t bh = (int64_t)b * p.H + h;
-        mbar_arrive_expect_tx(&kbar[c], kbytes);
-        bulk_load(kslot(c), p.kpt + (bh * kD + c * kKChunkD) * nb, kbytes, &kbar[c]);
-      };
-      if (tid == 0) {
-        // the head's data was written by other CTAs (generic stores, seen
-        // through the acquire above); the slots were last read by this CTA's
-        // generic loads
-        fence_proxy_async_all();
-        issue_q(0);
-        for (int c = 0; c < kKChunks; ++c) issue_k(0, c);
-      }
+      // ------------------------------------------------------- score item
+      if (tid == 0) issue_pair(s, 0);
       float bacc[4][4];
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int e = 0; e < 4; ++e) bacc[a][e] = 0.f;
-      for (int b = 0; b < p.B; ++b) {
-        const int64_t bh = (int64_t)b * p.H + h;
-        if (tid == 0 && b + 1 < p.B) {
-          fence_proxy_async_all();
-          issue_q(b + 1);  // its buffer was last read by batch element b - 1
+      for (int bp = 0; bp < npairs; ++bp) {
+        // ---------------------------------------------------- logits of the pair
+        const bool active = 2 * bp + gb < p.B;
+        float acc[8][KJ];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+          for (int j = 0; j < KJ; ++j) acc[r][j] = 0.f;
+        if (active) {
+          wait_copy(&qbar[gb], (qpar >> gb) & 1u);
+          qpar ^= 1u << gb;
         }
-        wait_copy(&qbar[b & 1], (qpar >> (b & 1)) & 1u);
-        qpar ^= 1u << (b & 1);
-        const float* q0 = qs + (b & 1) * kRows * kD + r0 * kD;
-        float acc[4][4];
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[a][e] = 0.f;
+        const float* qrow = qs + (gb * kRows + grow) * kD;
         for (int c = 0; c < kKChunks; ++c) {
-          wait_copy(&kbar[c], (kpar >> c) & 1u);
-          kpar ^= 1u << c;
-          if (kb < nb) {
-            const float* ks = kslot(c) + kb;
-#pragma unroll 2
-            for (int dd = 0; dd < kKChunkD; dd += 4) {
-              const int d = c * kKChunkD + dd;
-              float qv[4][4];
+          const int slot = gb * kKBufs + c % kKBufs;
+          if (active) {
+            wait_copy(&kbar[slot], (kpar >> slot) & 1u);
+            kpar ^= 1u << slot;
+            const uint8_t* ks = kslot(gb, c % kKBufs);
 #pragma unroll
-              for (int a = 0; a < 4; ++a) {
-                const float4 q4 = *reinterpret_cast<const float4*>(q0 + a * kD + d);
-                qv[a][0] = q4.x; qv[a][1] = q4.y; qv[a][2] = q4.z; qv[a][3] = q4.w;
+            for (int cq = 0; cq < kKChunkD / 4; ++cq) {
+              float kv[KJ][4];
+#pragma unroll
+              for (int j = 0; j < KJ; ++j) {
+                const int key = lane + 32 * (kh + 2 * j);
+                const float4 x = *reinterpret_cast<const float4*>(
+                    ks + key * (kKChunkD * 4) + ((cq ^ ((key >> 1) & 3)) << 4));
+                kv[j][0] = x.x; kv[j][1] = x.y; kv[j][2] = x.z; kv[j][3] = x.w;
               }
+              const int d = c * kKChunkD + cq * 4;
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                float kv[4];
-                if (vec4) {
-                  const float4 k4 = *reinterpret_cast<const float4*>(ks + (dd + i) * nb);
-                  kv[0] = k4.x; kv[1] = k4.y; kv[2] = k4.z; kv[3] = k4.w;
-                } else {
+              for (int r = 0; r < 8; ++r) {
+                const float4 q4 = *reinterpret_cast<const float4*>(qrow + r * kD + d);
+                const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-                  for (int e = 0; e < 4; ++e) kv[e] = ks[(dd + i) * nb + e];
-                }
+                for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int a = 0; a < 4; ++a)
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) acc[a][e] = fmaf(qv[a][i], kv[e], acc[a][e]);
+                  for (int j = 0; j < KJ; ++j) acc[r][j] = fmaf(qv[i], kv[j][i], acc[r][j]);
               }
             }
           }
-          score_bar();  // every thread is done with slot c
-          if (tid == 0 && b + 1 < p.B) {
-            fence_proxy_async_all();
-            issue_k(b + 1, c);
+          score_bar();  // every warp is done with this chunk's buffers
+          if (tid == 0) {
+            if (c + kKBufs < kKChunks) {
+              for (int bsel = 0; bsel < 2 && 2 * bp + bsel < p.B; ++bsel)
+                issue_k(h, 2 * bp + bsel, bsel, c + kKBufs);
+            } else if (c == kKChunks - 1 && bp + 1 < npairs) {
+              issue_pair(s, bp + 1);
+            }
           }
         }
+        if (active) {
+          float* lrow = lbuf + (gb * kRows + grow) * NPAD;
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+          for (int r = 0; r < 8; ++r)
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (kb + e < nb) ebuf[(r0 + a) * NPAD + kb + e] = acc[a][e] * p.scale;
-        score_bar();
-        for (int rr = sw; rr < nrows; rr += kScoreWarps) {  // softmax of row rr
-          float* x = ebuf + rr * NPAD;
-          float m = -INFINITY;
-          for (int c = lane; c < nb; c += 32) m = fmaxf(m, x[c]);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          float ssum = 0.f;
-          for (int c = lane; c < nb; c += 32) ssum += expf(x[c] - m);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-          const float inv = 1.0f / ssum;
-          for (int c = lane; c < nb; c += 32) x[c] = expf(x[c] - m) * inv;
+            for (int j = 0; j < KJ; ++j) {
+              const int key = lane + 32 * (kh + 2 * j);
+              if (key < nb) lrow[r * NPAD + key] = acc[r][j] * p.scale;
+            }
         }
         score_bar();
+        // ------------------- softmax of every row of the pair (warp = row)
+        // a warp's four rows go together, so their reduction chains overlap
+        {
+          constexpr int E = NPAD / 32;
+          constexpr int RW = 2 * kRows / kScoreWarps;  // rows per warp
+          float v[RW][E];
+          float m[RW], ssum[RW];
+          bool act[RW];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-          if (r0 + a >= nrows) continue;
+          for (int q = 0; q < RW; ++q) {
+            const int x = sw + kScoreWarps * q;
+            act[q] = 2 * bp + x / kRows < p.B && x % kRows < nrows;
+            const float* row = lbuf + (size_t)x * NPAD;
+            m[q] = -INFINITY;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (kb + e >= nb) continue;
-            const float pv = ebuf[(r0 + a) * NPAD + kb + e];
-            if (p.scores != nullptr) p.scores[(bh * nb + i0 + r0 + a) * nb + kb + e] = pv;
-            bacc[a][e] += pv;
+            for (int j = 0; j < E; ++j) {
+              const int c = lane + 32 * j;
+              v[q][j] = (act[q] && c < nb) ? row[c] : -INFINITY;
+              m[q] = fmaxf(m[q], v[q][j]);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int q = 0; q < RW; ++q) m[q] = fmaxf(m[q], __shfl_xor_sync(0xffffffffu, m[q], o));
+#pragma unroll
+          for (int q = 0; q < RW; ++q) {
+            ssum[q] = 0.f;
+#pragma unroll
+            for (int j = 0; j < E; ++j) {
+              if (act[q] && lane + 32 * j < nb) {
+                v[q][j] = expf(v[q][j] - m[q]);
+                ssum[q] += v[q][j];
+              }
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int q = 0; q < RW; ++q) ssum[q] += __shfl_xor_sync(0xffffffffu, ssum[q], o);
+#pragma unroll
+          for (int q = 0; q < RW; ++q) {
+            if (!act[q]) continue;
+            float* row = lbuf + (size_t)(sw + kScoreWarps * q) * NPAD;
+            const float inv = 1.0f / ssum[q];
+#pragma unroll
+            for (int j = 0; j < E; ++j)
+              if (lane + 32 * j < nb) row[lane + 32 * j] = v[q][j] * inv;
+          }
+        }
+        score_bar();
+        // ------------------------------------ probabilities out, batch sum
+        for (int bsel = 0; bsel < 2; ++bsel) {
+          const int b = 2 * bp + bsel;
+          if (b >= p.B) break;
+          const int64_t bh = (int64_t)b * p.H + h;
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            if (r0 + a >= nrows) continue;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (kb + e >= nb) continue;
+              const float pv = lbuf[(bsel * kRows + r0 + a) * NPAD + kb + e];
+              if (p.scores != nullptr) p.scores[(bh * nb + i0 + r0 + a) * nb + kb + e] = pv;
+              bacc[a][e] += pv;
+            }
           }
         }
         score_bar();
@@ -611,23 +644,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-
-    // ------------------------------------------------ coverage rows, any left
+    // phase 2: coverage tasks of up to kScoreWarps rows of one group, once
+    // every score item is taken (each is then finished by its taker, which
+    // waits only on the pooling), so every wait below ends
     if (p.mask != nullptr) {
+      const int tph = (nb + kScoreWarps - 1) / kScoreWarps;  // tasks per head
+      const int n_tasks = p.H * tph;
       for (;;) {
-        int r = 0, ok = 0;
-        if (lane == 0) {
-          r = (int)epoch_add(&p.ctr[kCovCtr * kCtrStride], p.epoch);
-          if (r < n_rows) {
-            const int g = (r / nb) * p.G + (r % nb) / kRows;
-            ok = spin_until([&] { return ld_acquire(&p.gflag[g]) == (unsigned long long)p.epoch; },
+        if (tid == 0) {
+          const int t = (int)epoch_add(&p.ctr[kCovCtr * kCtrStride], p.epoch);
+          int ok = 1;
+          if (t < n_tasks) {
+            const int h = t / tph, row0 = (t - h * tph) * kScoreWarps;
+            const int g = h * p.G + row0 / kRows;
+            ok = spin_until([&] { return ld_acquire(&p.gflag[g]) ==
+                                         (unsigned long long)p.epoch; },
                             p.status, 128) ? 1 : 0;
           }
+          ctl[0] = t;
+          ctl[1] = ok;
         }
-        r = __shfl_sync(0xffffffffu, r, 0);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (r >= n_rows) break;
-        coverage_of_row<NPAD>(p, r, rowbuf, skey, lane, ok != 0);
+        score_bar();
+        const int t = ctl[0];
+        const int ok = ctl[1];
+        score_bar();
+        if (t >= n_tasks) break;
+        const int h = t / tph, row0 = (t - h * tph) * kScoreWarps;
+        if (row0 + sw < nb)
+          coverage_of_row<NPAD>(p, h * nb + row0 + sw, rowbuf, skey, lane, ok != 0);
+        score_bar();  // the scratch is shared with the next task's reads
       }
     }
   }
@@ -639,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (epoch_add(&p.ctr[kDoneCtr * kCtrStride], p.epoch) == gridDim.x - 1) {
       __threadfence();
       volatile unsigned long long* c = p.ctr;
-      c[kRoleCtr * kCtrStride] = 0ull;
+      c[kStartCtr * kCtrStride] = 0ull;
       c[kScoreCtr * kCtrStride] = 0ull;
       c[kCovCtr * kCtrStride] = 0ull;
       c[kReady * kCtrStride] = 0ull;
@@ -682,14 +727,14 @@ bool eligible(const void* q, const void* k, const int64_t* q_strides, const int6
 }
 
 template <int NPAD>
-int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const Params& p, int grid,
-             cudaStream_t stream) {
+int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mkp,
+             const Params& p, int grid, cudaStream_t stream) {
   const int smem = (int)Layout<NPAD>::total;
   if (int rc = func_attr_once((const void*)calib_layer_kernel<NPAD>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       rc != SA_OK)
     return rc;
-  calib_layer_kernel<NPAD><<<grid, kThreads, smem, stream>>>(mq, mk, p);
+  calib_layer_kernel<NPAD><<<grid, kThreads, smem, stream>>>(mq, mk, mkp, p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
@@ -711,7 +756,7 @@ int launch(const LayerArgs& a, cudaStream_t stream) {
     cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)a.S, (cuuint64_t)a.H, (cuuint64_t)a.B};
     cuuint64_t gst[3] = {(cuuint64_t)strides[t][2] * 2, (cuuint64_t)strides[t][1] * 2,
                          (cuuint64_t)strides[t][0] * 2};
-    cuuint32_t box[4] = {128, 128, 1, 1};
+    cuuint32_t box[4] = {128, (cuuint32_t)kHalf, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(&maps[t], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(bases[t]),
                      dims, gst, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -719,6 +764,25 @@ int launch(const LayerArgs& a, cudaStream_t stream) {
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       set_error("cuTensorMapEncodeTiled (calibration layer) failed (CUresult %d)", (int)r);
+      return SA_ECUDA;
+    }
+  }
+  // pooled K [B*H*nb rows][128] fp32 in the workspace, read by the score
+  // items in boxes of 16 channels x nb keys with the 64-byte swizzle
+  CUtensorMap mkp;
+  {
+    const size_t off = counter_bytes(a.H) + flag_bytes(a.H, nb) + (size_t)a.B * a.H * nb * kD * 4;
+    cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)a.B * a.H * nb};
+    cuuint64_t gst[1] = {(cuuint64_t)kD * 4};
+    cuuint32_t box[2] = {(cuuint32_t)kKChunkD, (cuuint32_t)nb};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&mkp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                     reinterpret_cast<uint8_t*>(a.workspace) + off, dims, gst, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled (calibration layer, pooled K) failed (CUresult %d)",
+                (int)r);
       return SA_ECUDA;
     }
   }
@@ -735,8 +799,8 @@ int launch(const LayerArgs& a, cudaStream_t stream) {
   p.gflag = reinterpret_cast<unsigned long long*>(ws);
   ws += flag_bytes(a.H, nb);
   p.qp = reinterpret_cast<float*>(ws);
-  p.kpt = p.qp + (size_t)a.B * a.H * nb * kD;
-  p.bm_scratch = p.kpt + (size_t)a.B * a.H * nb * kD;
+  p.kp = p.qp + (size_t)a.B * a.H * nb * kD;
+  p.bm_scratch = p.kp + (size_t)a.B * a.H * nb * kD;
   p.epoch = next_epoch();
   p.scores = a.scores;
   p.bmean = a.batch_mean;
@@ -760,17 +824,10 @@ int launch(const LayerArgs& a, cudaStream_t stream) {
   int64_t want = (n_pool + kPoolWarps - 1) / kPoolWarps;
   if (n_score > want) want = n_score;
   const int grid = (int)(want < sms ? want : sms);
-  // score CTAs: about a fifth of the grid (SINKATTN_CALIB_SCORE_CTAS sets the
-  // number, for tuning); at least one CTA pools
-  int score_ctas = (grid * 22 + 50) / 100;
-  if (const char* env = getenv("SINKATTN_CALIB_SCORE_CTAS")) score_ctas = atoi(env);
-  if (score_ctas > grid - 1) score_ctas = grid - 1;
-  if (score_ctas < 0) score_ctas = 0;
-  p.pool_ctas = grid - score_ctas;
-  if (nb <= 32) return launch_t<32>(maps[0], maps[1], p, grid, stream);
-  if (nb <= 64) return launch_t<64>(maps[0], maps[1], p, grid, stream);
-  if (nb <= 128) return launch_t<128>(maps[0], maps[1], p, grid, stream);
-  return launch_t<256>(maps[0], maps[1], p, grid, stream);
+  if (nb <= 32) return launch_t<32>(maps[0], maps[1], mkp, p, grid, stream);
+  if (nb <= 64) return launch_t<64>(maps[0], maps[1], mkp, p, grid, stream);
+  if (nb <= 128) return launch_t<128>(maps[0], maps[1], mkp, p, grid, stream);
+  return launch_t<256>(maps[0], maps[1], mkp, p, grid, stream);
 }
 
 }  // namespace calib

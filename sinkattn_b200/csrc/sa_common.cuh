@@ -177,6 +177,23 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// TMA: 2-D tiled load global -> shared, completion counted on `bar` (bytes).
+// No multicast.
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses of global memory (an
+// acquire of data other CTAs stored) before its later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Untiled bulk copy global -> shared (the TMA engine, no tensor map),
 // completion counted on `bar` (bytes). Both addresses 16-byte aligned, size a
 // multiple of 16 bytes. No multicast.

@@ -93,7 +93,6 @@ def test_pool_scores_workspace_and_validation(lib):
 
     B, H, S, D = 2, 12, 32768, 128
     nb = 256
-    # 256-byte-rounded work counters, then pooled Q, K and logits in fp32
     # work counters (one 128-byte line each, H + 5 of them, rounded to 256),
     # group flags (8 bytes per 16 block rows of each head, rounded to 256),
     # then pooled Q, K and logits in fp32 (sa_pool_scores) or pooled Q, K and
