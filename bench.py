@@ -11,8 +11,12 @@ Bernoulli(0.2), seed 1). `value` is whole-job kept-block TFLOP/s
 max-over-ranks device time of the K timed steps. Inputs (603 MB) exceed L2.
 
 Multi-GPU (torchrun): the work shards by (batch, head) unit with no
-collective on the data path. Weak scaling: every rank runs its own Wan layer
-(24 units, seed = rank), so the job has 24*N units.
+collective on the data path. Strong scaling: the job is one Wan layer (24
+units) on every N, split over the ranks (12, 6, 3 units per rank at N = 2, 4,
+8); `value` is the layer's kept-block FLOPs over the slowest rank's time. At
+N > 1 the line also carries the weak-scaling figure (every rank runs the
+whole layer) and the same layer under Ulysses sequence parallelism (sequence
+shards -> all-to-all -> units -> kernel -> all-to-all back).
 
 Extra figures in the same JSON line: the density of the coverage-rule mask on
 the stated generator (~0.83) and its TFLOP/s, the calibration pass (pooling
@@ -191,6 +195,16 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(x: int, world: int, device) -> int:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return int(t.item())
+
+
 def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
@@ -361,16 +375,17 @@ def run_ours(args):
     barrier(world)
     trace("process group up")
     from sinkattn_b200 import _lib, ops
-    from sinkattn_b200.reference_api import _block_sparse_attn
+    from sinkattn_b200.sharding import partition_units
     from tests.gen import cfg1_mask, wan_qk
 
     _lib.load()
     peaks, peak_kind = load_peaks()
     stream = torch.cuda.current_stream(dev)
 
-    # inputs: Wan layout (BSHD memory viewed as BHSD), seed = rank
+    # inputs: Wan layout (BSHD memory viewed as BHSD), the same layer on every
+    # rank; rank r computes its share of the (batch, head) units
     trace("generating inputs")
-    qh, kh, vh = wan_qk(seed=rank, dtype=torch.bfloat16)  # [B,H,S,D] on CPU
+    qh, kh, vh = wan_qk(seed=0, dtype=torch.bfloat16)  # [B,H,S,D] on CPU
     trace("inputs generated")
     q_bshd = qh.permute(0, 2, 1, 3).contiguous()
     k_bshd = kh.permute(0, 2, 1, 3).contiguous()
@@ -380,11 +395,22 @@ def run_ours(args):
     k = k_bshd.to(dev).permute(0, 2, 1, 3)
     v = v_bshd.to(dev).permute(0, 2, 1, 3)
     mask20 = cfg1_mask(H, NB, NB, seed=1).unsqueeze(0).expand(B, -1, -1, -1).contiguous().to(dev)
-    flops20 = kept_flops(mask20)
+    flops20 = kept_flops(mask20)  # the whole layer: the job's fixed work
     out = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=dev).permute(0, 2, 1, 3)
     lse = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+    units = partition_units(B * H, world, rank)
+    segs = unit_segments(units, H)
+    flops20_r = sum(kept_flops(mask20[b0:b1, h0:h1]) for b0, b1, h0, h1 in segs)
+
+    def attn_units(mask):
+        for b0, b1, h0, h1 in segs:
+            sl = (slice(b0, b1), slice(h0, h1))
+            ops.bsattn_fwd(q[sl], k[sl], v[sl], mask[sl], out=out[sl], lse=lse[sl])
 
     def step20():
+        attn_units(mask20)
+
+    def step20_full():
         ops.bsattn_fwd(q, k, v, mask20, out=out, lse=lse)
 
     # calibration layer on this layer's Q/K, one fused launch: pool -> pooled
@@ -404,11 +430,11 @@ def run_ours(args):
     flops83 = kept_flops(mask83)
 
     def step83():
-        ops.bsattn_fwd(q, k, v, mask83, out=out, lse=lse)
+        attn_units(mask83)
 
     for i in range(max(3, args.warmup)):
         for name, fn in (("attn rho21", step20), ("attn coverage-mask", step83),
-                         ("calibration", step_calib)):
+                         ("calibration", step_calib), ("attn full layer", step20_full)):
             fn()
             if _TRACE:
                 torch.cuda.synchronize()
@@ -424,27 +450,125 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier(world)
     max_ms = max_over_ranks(total_ms, world, dev)
+    min_ms = -max_over_ranks(-total_ms, world, dev)
     ms_step = max_ms / args.steps
-    value = flops20 * world * args.steps / (max_ms / 1e3) / 1e12
-    avg_launch_ms = statistics.mean(per_ms)
-    achieved = flops20 / (avg_launch_ms / 1e3) / 1e12
+    value = flops20 * args.steps / (max_ms / 1e3) / 1e12
+    avg_launch_ms = statistics.mean(per_ms) / len(segs)
+    achieved = flops20_r / len(segs) / (avg_launch_ms / 1e3) / 1e12
+    frac_r = flops20_r / (total_ms / args.steps / 1e3) / 1e12 / float(
+        peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    frac_min = -max_over_ranks(-frac_r, world, dev)
+    replicas = None
+    if world > 1:
+        # weak-scaling figure: every rank runs the whole layer
+        barrier(world)
+        t_rep, _ = time_steps(step20_full, args.steps, stream)
+        barrier(world)
+        t_rep = max_over_ranks(t_rep, world, dev)
+        replicas = {"value": flops20 * world * args.steps / (t_rep / 1e3) / 1e12, "unit": UNIT,
+                    "ms_per_step": t_rep / args.steps, "scaling": "weak",
+                    "note": "every rank runs the whole layer (24 units); value = all ranks' "
+                            "kept-block FLOPs over the max-over-ranks time"}
 
     trace("headline timed")
     # ---- coverage-rule mask (rho ~ 0.83) ----------------------------------
     barrier(world)
     t83, per83 = time_steps(step83, args.steps, stream)
     t83 = max_over_ranks(t83, world, dev)
-    # ---- calibration pass ---------------------------------------------------
-    tcal, percal = time_steps(step_calib, args.steps, stream)
-    tcal = max_over_ranks(tcal, world, dev)
+    calib_legs = None
+    if world == 1:
+        calib_legs = calibration_legs(args, q, k, v, ws, step_calib, stream, dev, peaks)
+    ulysses = None
+    if world > 1:
+        ulysses = ulysses_leg(args, q, k, v, mask20, world, rank, dev, stream)
+
+    trace("e2e")
+    te2e, h2d, d2h, hg = e2e_leg(args, q_bshd, k_bshd, v_bshd, mask20, segs, dev, stream, world)
+    e2e_value = flops20 * args.steps / (te2e / 1e3) / 1e12
+
+    trace("e2e timed")
+    # ---- CPU baseline (rank 0, N=1 only) ------------------------------------
+    cpu = cpu_cal = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu, cpu_cal = cpu_legs()
+
+    traffic = load_traffic().get("bsattn_fwd_wan_rho21")
+    if traffic is not None:
+        # the committed capture is of the whole layer (24 units)
+        traffic = traffic * len(units) / (B * H) / len(segs)
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded BASELINE cfg2 generator: N(0,1) + 0.5*PE3D, V ~ N(0,1))",
+        "config": {"workload": "wan_sink_attention_layer (cfg2: B=2,H=12,S=32768,D=128)",
+                   "global_batch": B, "seq_len": S, "heads": H, "head_dim": D,
+                   "parallelism": f"(b,h)-unit sharding x{world}: the layer's 24 units split "
+                                  f"over the ranks, no collective",
+                   "mask": "col0|diag|bernoulli(0.2) seed 1",
+                   "density": float(mask20.float().mean().item()),
+                   "l2": "inputs 603 MB > L2 (no flush)"},
+        "layer_latency_ms": ms_step,
+        "per_gpu": {"units": len(units), "launches_per_step": len(segs),
+                    "ms_slowest": max_ms / args.steps, "ms_fastest": min_ms / args.steps,
+                    "frac_min": frac_min, "frac_rank0": frac_r},
+        "replicas": replicas,
+        "coverage_rule_mask": {"density": density83, "ms_per_step": t83 / args.steps,
+                               "value": flops83 * args.steps / (t83 / 1e3) / 1e12,
+                               "unit": UNIT},
+        **(calib_legs or {}),
+        "ulysses": ulysses,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
+                "chunk_heads": hg,
+                "api": "sinkattn_b200.reference_api._block_sparse_attn",
+                "note": "pinned host buffers [B,S,H,D]; each rank moves its own units in "
+                        "chunks of (batch element, chunk_heads heads) as 2-D copies: H2D of "
+                        "chunk c+1 overlaps the call on chunk c, D2H of c overlaps the later "
+                        "H2D copies; bytes are the whole job's"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "sa::attn::bsattn_fwd_kernel",
+                     "peak_kind": f"bf16_tflops ({peak_kind}, burst)",
+                     "algorithmic_flops_per_launch": flops20_r / len(segs)},
+        "gpu_launches": args.steps * len(segs),
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+        "cpu_baseline_calibration": cpu_cal,
+    }
+    from sinkattn_b200.ops import DeviceStatus
+
+    DeviceStatus.check(dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def calibration_legs(args, q, k, v, ws, step_calib, stream, dev, peaks):
+    """The calibration figures of one GPU: the fused calibration layer, the
+    same without the mask, the device calibrator's record, and the 30-layer
+    calibration pass with its check against the reference row totals."""
+    from sinkattn_b200 import _lib, ops
+
+    # The attention legs before this one hold the GPU at its power cap; right
+    # after them the SM clocks run lower for a while (measured: the
+    # calibration kernel about 17% slower). These legs start from 2 s idle.
+    torch.cuda.synchronize()
+    time.sleep(2.0)
+    # ---- calibration layer ----------------------------------------------------
+    tcal, _ = time_steps(step_calib, args.steps, stream)
     calib_bytes = 2 * B * H * S * D * 2 + H * NB * NB  # read Q,K (bf16) + write mask
-    pool_only = {}
 
     def step_pool_only():
         ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
 
+    step_pool_only()
     tpool, _ = time_steps(step_pool_only, args.steps, stream)
-    tpool = max_over_ranks(tpool, world, dev)
 
     # the device calibrator's record (reference default config with the mean
     # rule): one fused launch that also adds to the layer's running sums
@@ -458,7 +582,6 @@ def run_ours(args):
 
     step_record()
     trec, _ = time_steps(step_record, args.steps, stream)
-    trec = max_over_ranks(trec, world, dev)
 
     trace("calibration layer timed")
     # ---- cfg3: the 30-layer calibration pass, layers pipelined on two streams
@@ -475,7 +598,6 @@ def run_ours(args):
     torch.cuda.synchronize()
     pass_steps = max(3, min(10, args.steps // 10))
     tpass, _ = time_steps(step_pass, pass_steps, stream)
-    tpass = max_over_ranks(tpass, world, dev)
     pass_ms = tpass / pass_steps
     pass_bytes = 30 * calib_bytes
     density30 = float(masks30.float().mean().item())
@@ -495,7 +617,64 @@ def run_ours(args):
     del layers, bms30, ref30
 
     trace("calibration pass timed")
-    # ---- end to end through the reference-facing API (host buffers) ---------
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    pool_bytes = 2 * B * H * S * D * 2
+    return {
+        "calibration_layer": {"ms_per_layer": tcal / args.steps,
+                              "pool_scores_ms": tpool / args.steps,
+                              "calibrator_record_ms": trec / args.steps,
+                              "bytes": calib_bytes,
+                              "gbs": calib_bytes / (tcal / args.steps / 1e3) / 1e9,
+                              "frac_of_hbm": calib_bytes / (tcal / args.steps / 1e3) / 1e9 / hbm,
+                              "pool_scores_frac_of_hbm": pool_bytes
+                              / (tpool / args.steps / 1e3) / 1e9 / hbm,
+                              "note": "one fused launch (pool -> pooled logits -> softmax -> "
+                                      "batch mean -> coverage mask); pool_scores_ms: the same "
+                                      "without the mask (scores' batch mean only); "
+                                      "calibrator_record_ms: DeviceSinkMaskCalibrator.record, "
+                                      "mean rule, with the running sums; timed after 2 s idle "
+                                      "following the attention legs"},
+        "calibration_pass_30_layers": {
+            "ms_per_pass": pass_ms, "ms_per_layer": pass_ms / 30,
+            "bytes_per_pass": pass_bytes,
+            "gbs": pass_bytes / (pass_ms / 1e3) / 1e9,
+            "frac_of_hbm": pass_bytes / (pass_ms / 1e3) / 1e9 / hbm,
+            "mask_density": density30,
+            "vs_reference_totals": pass_check,
+            "note": "cfg3: 30 layers x Q,K [2,12,32768,128] bf16 (GPU-generated, seed=layer); "
+                    "one fused launch per layer (pool -> pooled logits -> softmax -> batch "
+                    "mean -> coverage mask, sink column forced, device row totals); "
+                    "vs_reference_totals: rows whose mask differs from the rule with the "
+                    "reference's CPU fp32 row totals, all of which must be flagged"},
+    }
+
+
+def unit_segments(units, heads):
+    """(b0, b1, h0, h1) rectangles covering a contiguous run of (batch, head)
+    units u = b * heads + h: whole batch elements as one rectangle, a partial
+    batch element as its own."""
+    segs = []
+    u, end = (units[0], units[-1] + 1) if units else (0, 0)
+    while u < end:
+        b, h = divmod(u, heads)
+        if h == 0 and end - u >= heads:
+            nb_ = (end - u) // heads
+            segs.append((b, b + nb_, 0, heads))
+            u += nb_ * heads
+        else:
+            h1 = min(heads, h + end - u)
+            segs.append((b, b + 1, h, h1))
+            u += h1 - h
+    return segs
+
+
+def e2e_leg(args, q_bshd, k_bshd, v_bshd, mask20, segs, dev, stream, world):
+    """End to end through the reference-facing API with pinned host buffers:
+    each rank copies in and out only its own units. Returns the
+    max-over-ranks ms of the K steps, the whole job's H2D and D2H bytes per
+    step, and the heads per chunk."""
+    from sinkattn_b200.reference_api import _block_sparse_attn
+
     qp = q_bshd.pin_memory()
     kp = k_bshd.pin_memory()
     vp = v_bshd.pin_memory()
@@ -512,9 +691,10 @@ def run_ours(args):
     # buffers is a strided 2-D region (S rows of hg*D elements, pitch H*D), so
     # each tensor of a chunk is one cudaMemcpy2DAsync.
     hg = max(1, min(H, args.e2e_chunk_heads))
-    while H % hg:
+    while any((s1 - s0) % hg for _, _, s0, s1 in segs):
         hg -= 1
-    chunks = [(b, h0) for b in range(B) for h0 in range(0, H, hg)]
+    chunks = [(b, h0) for b0, b1, s0, s1 in segs for b in range(b0, b1)
+              for h0 in range(s0, s1, hg)]
     s_h2d, s_cmp, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in chunks]
     ev_out = [torch.cuda.Event() for _ in chunks]
@@ -555,102 +735,72 @@ def run_ours(args):
     te2e, _ = time_steps(step_e2e, args.steps, stream)
     barrier(world)
     te2e = max_over_ranks(te2e, world, dev)
-    e2e_value = flops20 * world * args.steps / (te2e / 1e3) / 1e12
-    h2d = 3 * B * S * H * D * 2 * world
-    d2h = (B * S * H * D * 2 + B * H * S * 2) * world
+    n_heads = sum((b1 - b0) * (h1 - h0) for b0, b1, h0, h1 in segs)
+    h2d = sum_over_ranks(3 * S * n_heads * D * 2, world, dev)
+    d2h = sum_over_ranks(S * n_heads * D * 2 + n_heads * S * 2, world, dev)
+    return te2e, h2d, d2h, hg
 
-    trace("e2e timed")
-    # ---- CPU baseline (rank 0, N=1 only) ------------------------------------
-    cpu = cpu_cal = None
-    if rank == 0 and world == 1 and not args.skip_cpu:
-        threads = os.cpu_count() or 1
-        torch.set_num_threads(threads)
-        cq, ck, cv, cm = make_cpu_sample()
-        cpu_attention_sample(cq, ck, cv, cm, [(0, 0)], 2)
-        dt, fl = cpu_attention_sample(cq, ck, cv, cm, [(0, 0), (0, 1)], 32)
-        cpu = {"value": fl / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": "2 (b,h) units x 32 query blocks x 256 key blocks, rho~0.21, "
-                         "dense masked fp32 torch attention (the benchmark's reference)"}
-        ct, cb = cpu_calibration_sample(2)
-        cpu_cal = {"value": cb / ct / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-                   "ms_per_layer": 1e3 * ct / 2,
-                   "sample": "2 cfg3 layers (seeds 0, 1) after 1 untimed: torch fp32 128-token "
-                             "block means of Q and K, pooled softmax, batch mean, then the "
-                             "oracle's coverage mask (0.85, key block 0 kept)"}
 
-    traffic = load_traffic().get("bsattn_fwd_wan_rho21")
-    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded BASELINE cfg2 generator: N(0,1) + 0.5*PE3D, V ~ N(0,1))",
-        "config": {"workload": "wan_sink_attention_layer (cfg2: B=2,H=12,S=32768,D=128)",
-                   "global_batch": B * world, "seq_len": S, "heads": H, "head_dim": D,
-                   "parallelism": f"(b,h)-units x{world}, no collective",
-                   "mask": "col0|diag|bernoulli(0.2) seed 1",
-                   "density": float(mask20.float().mean().item()),
-                   "l2": "inputs 603 MB > L2 (no flush)"},
-        "layer_latency_ms": ms_step,
-        "coverage_rule_mask": {"density": density83, "ms_per_step": t83 / args.steps,
-                               "value": flops83 * world * args.steps / (t83 / 1e3) / 1e12,
-                               "unit": UNIT},
-        "calibration_layer": {"ms_per_layer": tcal / args.steps,
-                              "pool_scores_ms": tpool / args.steps,
-                              "calibrator_record_ms": trec / args.steps,
-                              "bytes": calib_bytes * world,
-                              "gbs": calib_bytes * world / (tcal / args.steps / 1e3) / 1e9,
-                              "frac_of_hbm": calib_bytes / (tcal / args.steps / 1e3) / 1e9
-                              / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
-                              "pool_scores_frac_of_hbm": 2 * B * H * S * D * 2
-                              / (tpool / args.steps / 1e3) / 1e9
-                              / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
-                              "note": "one layer per rank, one fused launch (pool -> pooled "
-                                      "logits -> softmax -> batch mean -> coverage mask); "
-                                      "pool_scores_ms: the same without the mask (scores' "
-                                      "batch mean only); calibrator_record_ms: "
-                                      "DeviceSinkMaskCalibrator.record, mean rule, with the "
-                                      "running sums; bytes and gbs whole-job, frac per GPU"},
-        "calibration_pass_30_layers": {
-            "ms_per_pass": pass_ms, "ms_per_layer": pass_ms / 30,
-            "bytes_per_pass": pass_bytes * world,
-            "gbs": pass_bytes * world / (pass_ms / 1e3) / 1e9,
-            "frac_of_hbm": pass_bytes / (pass_ms / 1e3) / 1e9
-            / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
-            "mask_density": density30,
-            "vs_reference_totals": pass_check,
-            "note": "cfg3: 30 layers x Q,K [2,12,32768,128] bf16 (GPU-generated, seed=layer); "
-                    "one fused launch per layer (pool -> pooled logits -> softmax -> batch "
-                    "mean -> coverage mask, sink column forced, device row totals); "
-                    "vs_reference_totals: rows whose mask differs from the rule with the "
-                    "reference's CPU fp32 row totals, all of which must be flagged"},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
-                "chunk_heads": hg,
-                "api": "sinkattn_b200.reference_api._block_sparse_attn",
-                "note": "pinned host buffers [B,S,H,D]; chunks of (batch element, chunk_heads "
-                        "heads) as 2-D copies: H2D of chunk c+1 overlaps the call on chunk c, "
-                        "D2H of c overlaps the later H2D copies"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
-                     "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "sa::attn::bsattn_fwd_kernel",
-                     "peak_kind": f"bf16_tflops ({peak_kind}, burst)",
-                     "algorithmic_flops_per_launch": flops20},
-        "gpu_launches": args.steps * world,
-        "clocks": clk.summary(),
-        "cpu_baseline": cpu,
-        "cpu_baseline_calibration": cpu_cal,
-    }
-    from sinkattn_b200.ops import DeviceStatus
+def cpu_legs():
+    """The CPU baselines on all host threads: dense masked fp32 torch
+    attention on 2 units x 32 query blocks, and the calibration path of two
+    cfg3 layers."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cq, ck, cv, cm = make_cpu_sample()
+    cpu_attention_sample(cq, ck, cv, cm, [(0, 0)], 2)
+    dt, fl = cpu_attention_sample(cq, ck, cv, cm, [(0, 0), (0, 1)], 32)
+    cpu = {"value": fl / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": "2 (b,h) units x 32 query blocks x 256 key blocks, rho~0.21, "
+                     "dense masked fp32 torch attention (the benchmark's reference)"}
+    ct, cb = cpu_calibration_sample(2)
+    cpu_cal = {"value": cb / ct / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+               "ms_per_layer": 1e3 * ct / 2,
+               "sample": "2 cfg3 layers (seeds 0, 1) after 1 untimed: torch fp32 128-token "
+                         "block means of Q and K, pooled softmax, batch mean, then the "
+                         "oracle's coverage mask (0.85, key block 0 kept)"}
+    return cpu, cpu_cal
 
-    DeviceStatus.check(dev)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
 
-        dist.destroy_process_group()
-    return 0
+def ulysses_leg(args, q, k, v, mask20, world, rank, dev, stream):
+    """The same layer under sequence parallelism: each rank starts from its
+    [B, S/P, H, D] sequence shard, one all-to-all per tensor turns the shards
+    into whole-sequence (b, h) units, the kernel runs, and the inverse
+    all-to-all returns the output in the sequence layout. Times the whole
+    exchange + attention + exchange, and the kernel alone on the same units."""
+    from sinkattn_b200.sharding import (_local_units_attention, sequence_to_units,
+                                        ulysses_sink_attention, units_per_rank)
+
+    Sr = S // world
+    sl = slice(rank * Sr, (rank + 1) * Sr)
+    qs, ks, vs = (x.permute(0, 2, 1, 3)[:, sl].contiguous() for x in (q, k, v))
+    n_per = units_per_rank(B * H, world)
+    steps = max(3, min(20, args.steps))
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        total, _ = time_steps(fn, steps, stream)
+        barrier(world)
+        return max_over_ranks(total / steps, world, dev)
+
+    res = {"units_per_rank": n_per, "steps": steps,
+           "exchange_mb_per_rank": 4 * B * Sr * H * D * 2 * (world - 1) / world / 1e6,
+           "ms_layer": {}}
+    for chunks in sorted({1, n_per}):
+        res["ms_layer"][str(chunks)] = timed(
+            lambda: ulysses_sink_attention(qs, ks, vs, mask20, chunks=chunks))
+    units = [sequence_to_units(x) for x in (qs, ks, vs)]
+    m = mask20.reshape(B * H, NB, NB)
+    ids = [rank * n_per + i for i in range(n_per)]
+    mu = torch.stack([m[i] if i < B * H else torch.ones_like(m[0]) for i in ids]).contiguous()
+    res["ms_attention_only"] = timed(lambda: _local_units_attention(*units, mu, ops_attn))
+    best = min(res["ms_layer"].values())
+    res["exchange_overhead"] = best / res["ms_attention_only"]
+    del qs, ks, vs, units
+    return res
 
 
 def run_case(args):

@@ -175,3 +175,35 @@ def test_exchange_errors_when_a_rank_leaves(tmp_path):
     outcome, seconds = (tmp_path / "rank0.txt").read_text().split("\n")[:2]
     assert outcome.startswith("error"), outcome
     assert float(seconds) < 60
+
+
+def test_bench_unit_segments_cover_each_unit_once():
+    """bench.py's strong-scaling split: for every world size the rank's units
+    become (b0, b1, h0, h1) rectangles that cover each of its units once,
+    span whole batch elements or lie inside one, and give views whose LSE
+    slice stays contiguous (the kernel's LSE has no strides)."""
+    import bench
+    from sinkattn_b200.sharding import partition_units
+
+    B, H, S = 2, 12, 256
+    lse = torch.empty(B, H, S)
+    out = torch.empty(B, S, H, 128).permute(0, 2, 1, 3)
+    for world in (1, 2, 3, 4, 5, 8):
+        seen = []
+        for rank in range(world):
+            units = partition_units(B * H, world, rank)
+            segs = bench.unit_segments(units, H)
+            got = []
+            for b0, b1, h0, h1 in segs:
+                assert b1 - b0 == 1 or (h0, h1) == (0, H)
+                got += [b * H + h for b in range(b0, b1) for h in range(h0, h1)]
+                sl = (slice(b0, b1), slice(h0, h1))
+                assert lse[sl].is_contiguous()
+                o = out[sl]
+                assert o.stride() == out.stride()
+                assert o.data_ptr() == out[b0, h0].data_ptr()
+            assert got == units
+            seen += got
+        assert sorted(seen) == list(range(B * H))
+    assert bench.unit_segments(list(range(24)), 12) == [(0, 2, 0, 12)]
+    assert bench.unit_segments(list(range(9, 15)), 12) == [(0, 1, 9, 12), (1, 2, 0, 3)]
