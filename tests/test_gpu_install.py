@@ -34,6 +34,7 @@ pytestmark = pytest.mark.gpu
 MAX_ABS = 2e-2
 MEAN_REL = 1e-2
 
+
 @pytest.fixture
 def installed(reference):
     """install() with every rebound name restored afterwards."""
@@ -57,12 +58,14 @@ def installed(reference):
         for mod, attr, val in saved:
             setattr(mod, attr, val)
 
+
 def _check(out, ref, what):
     err = (out.float() - ref).abs()
     max_abs = float(err.max())
     mean_rel = float(err.mean() / ref.abs().mean())
     assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (what, max_abs, mean_rel)
     return max_abs, mean_rel
+
 
 def _expected_wan_inner(orig_pool, orig_mix, cfg, q, k, v, mask, gap):
     """The reference's pooled_kv / adaptive inner attention in fp32."""
@@ -80,6 +83,7 @@ def _expected_wan_inner(orig_pool, orig_mix, cfg, q, k, v, mask, gap):
             out[b, h] = orig_mix(so, sl.unsqueeze(-1), do, dl.unsqueeze(-1), cfg,
                                  dynamic_sample_gap=gap)
     return out
+
 
 def test_wan_inner_attention_fused_and_unfused(installed):
     """The Wan runtime default (pooled_kv, adaptive mix, band 1) at a ragged
@@ -121,6 +125,7 @@ def test_wan_inner_attention_fused_and_unfused(installed):
 
     ops.DeviceStatus.check(q.device)
 
+
 class _WanAttn(torch.nn.Module):
     """The attributes WanSinkSparseAttnProcessor2_0 reads from diffusers'
     Attention for Wan self-attention."""
@@ -140,6 +145,7 @@ class _WanAttn(torch.nn.Module):
         self.to_out = torch.nn.ModuleList([torch.nn.Linear(dim, dim, dtype=torch.bfloat16),
                                            torch.nn.Dropout(0.0)])
         self.inner_attention = inner
+
 
 def test_wan_processor_end_to_end(installed):
     """WanSinkSparseAttnProcessor2_0.__call__ on hidden states with a rotary
@@ -183,6 +189,7 @@ def test_wan_processor_end_to_end(installed):
     err = (got.float() - ref).abs()
     assert float(err.mean()) <= 2e-2 * scale, (float(err.mean()), scale)
     assert float(err.max()) <= 40 * 2e-2 * scale, (float(err.max()), scale)
+
 
 def test_zimage_static_processor(installed):
     """ZImageStaticSinkProcessor.__call__ on a padded batch of two images
