@@ -767,7 +767,9 @@ def ulysses_leg(args, q, k, v, mask20, world, rank, dev, stream):
     [B, S/P, H, D] sequence shard, one all-to-all per tensor turns the shards
     into whole-sequence (b, h) units, the kernel runs, and the inverse
     all-to-all returns the output in the sequence layout. Times the whole
-    exchange + attention + exchange, and the kernel alone on the same units."""
+    exchange + attention + exchange, over NCCL all-to-alls and over NVLink
+    peer memory (UlyssesPeerExchange), and the kernel alone on the same
+    units."""
     from sinkattn_b200.sharding import (_local_units_attention, sequence_to_units,
                                         ulysses_sink_attention, units_per_rank)
 
@@ -789,17 +791,26 @@ def ulysses_leg(args, q, k, v, mask20, world, rank, dev, stream):
     res = {"units_per_rank": n_per, "steps": steps,
            "exchange_mb_per_rank": 4 * B * Sr * H * D * 2 * (world - 1) / world / 1e6,
            "ms_layer": {}}
-    for chunks in sorted({1, n_per}):
-        res["ms_layer"][str(chunks)] = timed(
-            lambda: ulysses_sink_attention(qs, ks, vs, mask20, chunks=chunks))
+    res["ms_layer"]["1"] = timed(lambda: ulysses_sink_attention(qs, ks, vs, mask20))
     units = [sequence_to_units(x) for x in (qs, ks, vs)]
     m = mask20.reshape(B * H, NB, NB)
     ids = [rank * n_per + i for i in range(n_per)]
     mu = torch.stack([m[i] if i < B * H else torch.ones_like(m[0]) for i in ids]).contiguous()
     res["ms_attention_only"] = timed(lambda: _local_units_attention(*units, mu, ops_attn))
-    best = min(res["ms_layer"].values())
-    res["exchange_overhead"] = best / res["ms_attention_only"]
-    del qs, ks, vs, units
+    res["exchange_overhead_nccl"] = min(res["ms_layer"].values()) / res["ms_attention_only"]
+    # the exchange over NVLink peer memory: dispatch / combine kernels
+    # writing into the owners' CUDA-IPC-mapped buffers
+    from sinkattn_b200.sharding import UlyssesPeerExchange
+
+    ex = UlyssesPeerExchange(B, S, H, device=dev)
+    o_ref, l_ref = ulysses_sink_attention(qs, ks, vs, mask20)
+    o_p, l_p = ex(qs, ks, vs, mask20)
+    torch.cuda.synchronize()
+    res["peer_equals_nccl"] = bool(torch.equal(o_p, o_ref) and torch.equal(l_p, l_ref))
+    res["ms_layer_peer"] = timed(lambda: ex(qs, ks, vs, mask20))
+    res["exchange_overhead"] = res["ms_layer_peer"] / res["ms_attention_only"]
+    ex.close()
+    del qs, ks, vs, units, o_ref, l_ref
     return res
 
 

@@ -413,6 +413,45 @@ SA_API int sa_mix_outputs(const void* o_s, const int64_t os_strides[4], const fl
                    const int64_t o_strides[4], cudaStream_t stream);
 
 /*
+ * Sequence-parallel (Ulysses) exchange over NVLink peer memory, and the CUDA
+ * IPC helpers that map the peers' buffers. No counterpart in the reference,
+ * which runs on one GPU (wanx/runtime/inference.py:65-69); they carry its
+ * attention call across ranks in a sequence-parallel DiT
+ * (sinkattn_b200/sharding.py). "Units" are the (batch, head) pairs u = b*H +
+ * h; rank r owns units r*n_per .. r*n_per + n_per - 1 (n_per*P >= B*H).
+ *
+ * sa_ipc_alloc / sa_ipc_free: cudaMalloc / cudaFree of a buffer to share.
+ * sa_ipc_get_handle: the 64-byte CUDA IPC handle of a buffer from
+ *   sa_ipc_alloc. sa_ipc_open_handle: maps another process's buffer into this
+ *   one (peer access enabled); sa_ipc_close unmaps it.
+ *
+ * sa_ulysses_dispatch: T (1..3) tensors, this rank's sequence shard
+ *   [B, Sr, H, 128] bf16 each (element strides src_strides[4t..4t+3], last 1,
+ *   others multiples of 8; 16-byte aligned), are written into the receive
+ *   buffers dst[r] (r < P <= 8, device addresses, peers' included) of the
+ *   units' owners: dst[owner] is [T][n_per][P*Sr][128] bf16, and the row of
+ *   shard position s lands at sequence position rank*Sr + s of its unit.
+ *   Rows of units past B*H are not written.
+ * sa_ulysses_combine: this rank's units' attention output [n_per][P*Sr][128]
+ *   bf16 (contiguous) and LSE [n_per][P*Sr] fp32 (nullable) are written into
+ *   out_dst[p] ([B][Sr][H][128] bf16) and lse_dst[p] ([B][H][Sr] fp32) of the
+ *   rank p owning each row's stretch of the sequence.
+ * Neither waits on another rank: the caller orders them against the peers'
+ * use of the same buffers (stream-ordered collectives before and after).
+ */
+SA_API int sa_ipc_alloc(size_t bytes, void** ptr);
+SA_API int sa_ipc_free(void* ptr);
+SA_API int sa_ipc_get_handle(void* ptr, uint8_t handle[64]);
+SA_API int sa_ipc_open_handle(const uint8_t handle[64], void** ptr);
+SA_API int sa_ipc_close(void* ptr);
+SA_API int sa_ulysses_dispatch(int T, const void* const* src, const int64_t* src_strides, int B,
+                               int Sr, int H, int D, int P, int rank, int n_per,
+                               void* const* dst, cudaStream_t stream);
+SA_API int sa_ulysses_combine(const void* out_units, const float* lse_units, int B, int Sr, int H,
+                              int D, int P, int rank, int n_per, void* const* out_dst,
+                              float* const* lse_dst, cudaStream_t stream);
+
+/*
  * The status word. No counterpart in the reference, whose kernels cannot
  * report a stalled wait.
  * sa_status_create: one int32 in mapped, portable page-locked host memory,

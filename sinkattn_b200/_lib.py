@@ -90,6 +90,13 @@ _SIGNATURES = {
         [_vp, _vp, _i, _i, _i, _i, _f, _i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     ),
     "sa_mean_pool_seq": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "sa_ipc_alloc": (_i, [ctypes.c_size_t, _vp]),
+    "sa_ipc_free": (_i, [_vp]),
+    "sa_ipc_get_handle": (_i, [_vp, _vp]),
+    "sa_ipc_open_handle": (_i, [_vp, _vp]),
+    "sa_ipc_close": (_i, [_vp]),
+    "sa_ulysses_dispatch": (_i, [_i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp]),
+    "sa_ulysses_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "sa_status_create": (_vp, []),
     "sa_status_device_pointer": (_i, [_vp, _vp]),
     "sa_status_destroy": (_i, [_vp]),

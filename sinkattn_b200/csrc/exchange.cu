@@ -1,0 +1,232 @@
+// exchange.cu — the Ulysses sequence-parallel exchange over NVLink peer
+// memory, and the CUDA IPC helpers that give each rank its peers' buffers.
+//
+// In a sequence-parallel DiT every rank holds a [B, S/P, H, D] shard of Q, K
+// and V; attention needs whole sequences. The (batch, head) pairs ("units")
+// are split over the ranks, n_per each, and:
+//   dispatch: every rank writes each row of its shard straight into the
+//     receive buffer of the unit's owner, at the row's place in the whole
+//     sequence. The receive buffer is [T][n_per][S][D], so each unit's
+//     sequence is contiguous and the attention kernel reads it as it lies.
+//   combine: every rank writes the output rows and LSE of its units straight
+//     into the [B, S/P, H, D] output and [B, H, S/P] LSE of the rank that owns
+//     that stretch of the sequence.
+// One pass over the data each way, with 16-byte loads and 16-byte stores
+// (NVLink for remote rows, HBM for the rank's own), and no pack or unpack
+// copies. The kernels do not wait on other ranks: the caller orders them
+// against the peers' use of the same buffers with stream-ordered
+// collectives (sinkattn_b200/sharding.py). Every thread ends with a
+// system-scope fence, so its remote stores are performed before the kernel
+// completes.
+
+#include <string.h>
+
+#include "sa_common.cuh"
+
+namespace sa {
+namespace xchg {
+
+constexpr int kD = 128;
+constexpr int kMaxRanks = 8;
+constexpr int kMaxTensors = 3;
+constexpr int kPieces = kD * 2 / 16;  // 16-byte pieces of one bf16 row
+
+struct DispatchParams {
+  const uint8_t* src[kMaxTensors];
+  int64_t st[kMaxTensors][3];  // element strides of b, s, h (d is unit stride)
+  uint8_t* dst[kMaxRanks];     // each rank's receive buffer [T][n_per][S][D]
+  int T, B, Sr, H, P, rank, n_per;
+};
+
+__global__ void __launch_bounds__(256) dispatch_kernel(const DispatchParams p) {
+  const int64_t rows = (int64_t)p.T * p.B * p.Sr * p.H;
+  const int64_t S = (int64_t)p.P * p.Sr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * kPieces;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int piece = (int)(i % kPieces);
+    int64_t row = i / kPieces;  // (t, b, s, h), h fastest
+    const int h = (int)(row % p.H);
+    row /= p.H;
+    const int s = (int)(row % p.Sr);
+    row /= p.Sr;
+    const int b = (int)(row % p.B);
+    const int t = (int)(row / p.B);
+    const uint4 v = *reinterpret_cast<const uint4*>(
+        p.src[t] + ((b * p.st[t][0] + s * p.st[t][1] + h * p.st[t][2]) * 2 + piece * 16));
+    const int u = b * p.H + h;
+    const int owner = u / p.n_per, j = u - owner * p.n_per;
+    uint8_t* d = p.dst[owner] +
+                 ((((int64_t)t * p.n_per + j) * S + (int64_t)p.rank * p.Sr + s) * kD * 2 + piece * 16);
+    *reinterpret_cast<uint4*>(d) = v;
+  }
+  __threadfence_system();
+}
+
+struct CombineParams {
+  const uint8_t* out;    // [n_per][S][D] bf16, this rank's units
+  const float* lse;      // [n_per][S] fp32
+  uint8_t* out_dst[kMaxRanks];  // each rank's [B][Sr][H][D] bf16
+  float* lse_dst[kMaxRanks];    // each rank's [B][H][Sr] fp32 (nullable as a whole)
+  int B, Sr, H, P, rank, n_per;
+};
+
+__global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
+  const int U = p.B * p.H;
+  const int64_t S = (int64_t)p.P * p.Sr;
+  const int64_t rows = (int64_t)p.n_per * S;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * (kPieces + 1);
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / (kPieces + 1);
+    const int piece = (int)(i - row * (kPieces + 1));  // kPieces: the LSE value
+    const int j = (int)(row / S);
+    const int64_t s = row - (int64_t)j * S;
+    const int u = p.rank * p.n_per + j;
+    if (u >= U) continue;  // a padding unit
+    const int b = u / p.H, h = u - (u / p.H) * p.H;
+    const int owner = (int)(s / p.Sr);
+    const int64_t sl = s - (int64_t)owner * p.Sr;
+    if (piece < kPieces) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p.out + (row * kD * 2 + piece * 16));
+      *reinterpret_cast<uint4*>(p.out_dst[owner] +
+                                ((((int64_t)b * p.Sr + sl) * p.H + h) * kD * 2 + piece * 16)) = v;
+    } else if (p.lse_dst[0] != nullptr) {
+      p.lse_dst[owner][((int64_t)b * p.H + h) * p.Sr + sl] = p.lse[row];
+    }
+  }
+  __threadfence_system();
+}
+
+int grid_for(int64_t work) {
+  const int64_t want = (work + 255) / 256;
+  const int64_t cap = (int64_t)sm_count_current_device() * 8;
+  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+}  // namespace xchg
+}  // namespace sa
+
+using sa::xchg::kD;
+using sa::xchg::kMaxRanks;
+using sa::xchg::kMaxTensors;
+
+extern "C" int sa_ipc_alloc(size_t bytes, void** ptr) {
+  SA_CHECK_ARG(ptr != nullptr && bytes > 0, "sa_ipc_alloc: null pointer or zero size");
+  *ptr = nullptr;
+  SA_CUDA_TRY(cudaMalloc(ptr, bytes));
+  return SA_OK;
+}
+
+extern "C" int sa_ipc_free(void* ptr) {
+  if (ptr == nullptr) return SA_OK;
+  SA_CUDA_TRY(cudaFree(ptr));
+  return SA_OK;
+}
+
+extern "C" int sa_ipc_get_handle(void* ptr, uint8_t handle[64]) {
+  SA_CHECK_ARG(ptr != nullptr && handle != nullptr, "sa_ipc_get_handle: null pointer argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  SA_CUDA_TRY(cudaIpcGetMemHandle(&h, ptr));
+  memcpy(handle, &h, 64);
+  return SA_OK;
+}
+
+extern "C" int sa_ipc_open_handle(const uint8_t handle[64], void** ptr) {
+  SA_CHECK_ARG(ptr != nullptr && handle != nullptr, "sa_ipc_open_handle: null pointer argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, 64);
+  *ptr = nullptr;
+  SA_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return SA_OK;
+}
+
+extern "C" int sa_ipc_close(void* ptr) {
+  if (ptr == nullptr) return SA_OK;
+  SA_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return SA_OK;
+}
+
+extern "C" int sa_ulysses_dispatch(int T, const void* const* src, const int64_t* src_strides,
+                                   int B, int Sr, int H, int D, int P, int rank, int n_per,
+                                   void* const* dst, cudaStream_t stream) {
+  SA_CHECK_ARG(src != nullptr && src_strides != nullptr && dst != nullptr,
+               "sa_ulysses_dispatch: null pointer argument");
+  SA_CHECK_ARG(T >= 1 && T <= kMaxTensors, "sa_ulysses_dispatch: 1 to %d tensors, got %d",
+               kMaxTensors, T);
+  SA_CHECK_ARG(D == kD, "sa_ulysses_dispatch: head dim must be 128, got %d", D);
+  SA_CHECK_ARG(P >= 1 && P <= kMaxRanks, "sa_ulysses_dispatch: 1 to %d ranks, got %d",
+               kMaxRanks, P);
+  SA_CHECK_ARG(rank >= 0 && rank < P, "sa_ulysses_dispatch: rank %d outside 0..%d", rank, P - 1);
+  SA_CHECK_ARG(B >= 1 && Sr >= 1 && H >= 1, "sa_ulysses_dispatch: empty shard");
+  SA_CHECK_ARG(n_per >= 1 && (int64_t)n_per * P >= (int64_t)B * H,
+               "sa_ulysses_dispatch: %d units per rank cannot hold %d units", n_per, B * H);
+  sa::xchg::DispatchParams p = {};
+  for (int t = 0; t < T; ++t) {
+    SA_CHECK_ARG(src[t] != nullptr && ((uintptr_t)src[t] % 16) == 0,
+                 "sa_ulysses_dispatch: tensor %d null or not 16-byte aligned", t);
+    const int64_t* st = src_strides + 4 * t;  // [B, S, H, D] element strides
+    SA_CHECK_ARG(st[3] == 1 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0,
+                 "sa_ulysses_dispatch: tensor %d needs stride(dim) 1 and strides multiple "
+                 "of 8 elements", t);
+    p.src[t] = reinterpret_cast<const uint8_t*>(src[t]);
+    p.st[t][0] = st[0];
+    p.st[t][1] = st[1];
+    p.st[t][2] = st[2];
+  }
+  for (int r = 0; r < P; ++r) {
+    SA_CHECK_ARG(dst[r] != nullptr && ((uintptr_t)dst[r] % 16) == 0,
+                 "sa_ulysses_dispatch: receive buffer of rank %d null or not 16-byte aligned", r);
+    p.dst[r] = reinterpret_cast<uint8_t*>(dst[r]);
+  }
+  p.T = T;
+  p.B = B;
+  p.Sr = Sr;
+  p.H = H;
+  p.P = P;
+  p.rank = rank;
+  p.n_per = n_per;
+  const int64_t work = (int64_t)T * B * Sr * H * sa::xchg::kPieces;
+  sa::xchg::dispatch_kernel<<<sa::xchg::grid_for(work), 256, 0, stream>>>(p);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_ulysses_combine(const void* out_units, const float* lse_units, int B, int Sr,
+                                  int H, int D, int P, int rank, int n_per,
+                                  void* const* out_dst, float* const* lse_dst,
+                                  cudaStream_t stream) {
+  SA_CHECK_ARG(out_units != nullptr && out_dst != nullptr,
+               "sa_ulysses_combine: null pointer argument");
+  SA_CHECK_ARG((lse_units == nullptr) == (lse_dst == nullptr),
+               "sa_ulysses_combine: lse_units and lse_dst go together");
+  SA_CHECK_ARG(D == kD, "sa_ulysses_combine: head dim must be 128, got %d", D);
+  SA_CHECK_ARG(P >= 1 && P <= kMaxRanks, "sa_ulysses_combine: 1 to %d ranks, got %d",
+               kMaxRanks, P);
+  SA_CHECK_ARG(rank >= 0 && rank < P, "sa_ulysses_combine: rank %d outside 0..%d", rank, P - 1);
+  SA_CHECK_ARG(B >= 1 && Sr >= 1 && H >= 1, "sa_ulysses_combine: empty shard");
+  SA_CHECK_ARG(n_per >= 1 && (int64_t)n_per * P >= (int64_t)B * H,
+               "sa_ulysses_combine: %d units per rank cannot hold %d units", n_per, B * H);
+  SA_CHECK_ARG(((uintptr_t)out_units % 16) == 0, "sa_ulysses_combine: out_units not 16-byte aligned");
+  sa::xchg::CombineParams p = {};
+  p.out = reinterpret_cast<const uint8_t*>(out_units);
+  p.lse = lse_units;
+  for (int r = 0; r < P; ++r) {
+    SA_CHECK_ARG(out_dst[r] != nullptr && ((uintptr_t)out_dst[r] % 16) == 0,
+                 "sa_ulysses_combine: output of rank %d null or not 16-byte aligned", r);
+    p.out_dst[r] = reinterpret_cast<uint8_t*>(out_dst[r]);
+    if (lse_dst != nullptr) {
+      SA_CHECK_ARG(lse_dst[r] != nullptr, "sa_ulysses_combine: LSE of rank %d null", r);
+      p.lse_dst[r] = lse_dst[r];
+    }
+  }
+  p.B = B;
+  p.Sr = Sr;
+  p.H = H;
+  p.P = P;
+  p.rank = rank;
+  p.n_per = n_per;
+  const int64_t work = (int64_t)n_per * P * Sr * (sa::xchg::kPieces + 1);
+  sa::xchg::combine_kernel<<<sa::xchg::grid_for(work), 256, 0, stream>>>(p);
+  SA_CUDA_TRY(cudaGetLastError());
+  return SA_OK;
+}

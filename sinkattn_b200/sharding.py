@@ -5,13 +5,21 @@ rank can run any subset of units with no communication. Two layouts use this:
 
 * unit sharding (`partition_units`): ranks take disjoint sets of units of a
   job whose inputs they already hold; no data-path collective.
-* Ulysses exchange (`sequence_to_units` / `units_to_sequence`): in a
-  sequence-parallel DiT the activations arrive sharded by sequence
-  ([B, S/P, H, D] per rank). One all-to-all turns them into full-sequence
-  units ([U/P, S, D] per rank), the local kernel runs, and the inverse
-  all-to-all restores the sequence layout. 12 heads do not divide over 8
-  ranks, so (batch, head) units are the sharded dimension (2*12 = 24 units,
-  3 per rank at P = 8); a unit count that does not divide is padded.
+* Ulysses exchange: in a sequence-parallel DiT the activations arrive
+  sharded by sequence ([B, S/P, H, D] per rank). The exchange turns them
+  into full-sequence units ([U/P, S, D] per rank), the local kernel runs,
+  and the inverse exchange restores the sequence layout. 12 heads do not
+  divide over 8 ranks, so (batch, head) units are the sharded dimension
+  (2*12 = 24 units, 3 per rank at P = 8); a unit count that does not divide
+  is padded. Two implementations:
+  - UlyssesPeerExchange (CUDA): the dispatch and combine kernels
+    (csrc/exchange.cu) write every row straight into the owner's buffer
+    over NVLink peer memory, mapped once with CUDA IPC; no pack or unpack
+    copies and no NCCL data traffic, three 4-byte all-reduces per call to
+    order the ranks.
+  - ulysses_sink_attention (`sequence_to_units` / `units_to_sequence`): the
+    same exchange as torch.distributed all-to-alls, for any backend (the
+    CPU tests run it over gloo).
 
 The reference is single-GPU (wanx/runtime/inference.py:65-69); this module is
 the multi-GPU plumbing around its unchanged per-call semantics.
@@ -227,3 +235,176 @@ def ulysses_sink_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         out.record_stream(comm)
         lse_seq.record_stream(comm)
     return out, lse_seq[..., 0].permute(0, 2, 1).contiguous()
+
+
+def _device_view(ptr: int, nbytes: int, device) -> torch.Tensor:
+    """A uint8 tensor over `nbytes` of device memory at `ptr` (memory this
+    module allocated with sa_ipc_alloc; the tensor does not own it)."""
+
+    class _Mem:
+        pass
+
+    m = _Mem()
+    m.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                  "version": 3, "strides": None}
+    return torch.as_tensor(m, device=device)
+
+
+class UlyssesPeerExchange:
+    """Sink attention on sequence-sharded inputs with the exchange over NVLink
+    peer memory.
+
+    Made once per (B, S, H) on every rank of `group` (a collective call):
+    each rank allocates its receive buffer [3, n_per, S, 128] (Q, K, V of its
+    units), its output [B, S/P, H, 128] and LSE [B, H, S/P], and maps the
+    peers' buffers with CUDA IPC. A call then runs, on the current stream:
+
+        fence; dispatch (Q, K, V rows -> owners); fence;
+        attention on the rank's units (the receive buffer as it lies);
+        combine (output rows and LSE -> sequence owners); fence
+
+    where a fence is a 4-byte all-reduce: every rank is past the previous
+    step, so a buffer is written only when its owner is done with it, and
+    read only when every writer is done. The returned output and LSE are
+    this object's buffers: valid until the next call, which overwrites them,
+    so read them on the same stream before calling again.
+    At most 8 ranks; D = 128; S divisible by the world size.
+    """
+
+    def __init__(self, B: int, S: int, H: int, D: int = 128, group=None, device=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 1 <= self.world <= 8:
+            raise ValueError(f"UlyssesPeerExchange supports 1 to 8 ranks, got {self.world}")
+        if D != 128 or S % self.world:
+            raise ValueError(f"need D = 128 and S divisible by {self.world}; got D={D}, S={S}")
+        self.B, self.S, self.H, self.D = B, S, H, D
+        self.Sr = S // self.world
+        self.n_per = units_per_rank(B * H, self.world)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        lib = _lib.load()
+        self._lib = lib
+        sizes = {"recv": 3 * self.n_per * S * D * 2, "out": B * self.Sr * H * D * 2,
+                 "lse": B * H * self.Sr * 4}
+        self._own: dict[str, int] = {}
+        self._opened: list[int] = []
+        handles = {}
+        with torch.cuda.device(self.device):
+            for name, nbytes in sizes.items():
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.sa_ipc_alloc(nbytes, ctypes.byref(ptr)), "sa_ipc_alloc")
+                self._own[name] = int(ptr.value)
+                h = (ctypes.c_uint8 * 64)()
+                _lib.check(lib.sa_ipc_get_handle(ptr, h), "sa_ipc_get_handle")
+                handles[name] = bytes(h)
+            views = {n: _device_view(p, sizes[n], self.device) for n, p in self._own.items()}
+            for v in views.values():
+                v.zero_()  # padding units read zeros
+            self.recv = views["recv"].view(torch.bfloat16).view(3, self.n_per, S, D)
+            self.out = views["out"].view(torch.bfloat16).view(B, self.Sr, H, D)
+            self.lse = views["lse"].view(torch.float32).view(B, H, self.Sr)
+            everyone = [None] * self.world
+            dist.all_gather_object(everyone, handles, group=group)
+            ptrs = {n: [0] * self.world for n in sizes}
+            for r in range(self.world):
+                for n in sizes:
+                    if r == self.rank:
+                        ptrs[n][r] = self._own[n]
+                        continue
+                    p = ctypes.c_void_p()
+                    h = (ctypes.c_uint8 * 64).from_buffer_copy(everyone[r][n])
+                    _lib.check(lib.sa_ipc_open_handle(h, ctypes.byref(p)), "sa_ipc_open_handle")
+                    ptrs[n][r] = int(p.value)
+                    self._opened.append(int(p.value))
+            VP = ctypes.c_void_p * self.world
+            self._recv_ptrs = VP(*ptrs["recv"])
+            self._out_ptrs = VP(*ptrs["out"])
+            self._lse_ptrs = VP(*ptrs["lse"])
+            self._attn_out = torch.empty(1, self.n_per, S, D, dtype=torch.bfloat16,
+                                         device=self.device)
+            self._attn_lse = torch.empty(1, self.n_per, S, dtype=torch.float32, device=self.device)
+            self._flag = torch.zeros(1, device=self.device)
+            self._masks: Optional[tuple] = None
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def _fence(self):
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _unit_masks(self, block_mask: torch.Tensor) -> torch.Tensor:
+        # the rank's units' mask rows (padding units all true), cached per mask
+        key = (block_mask.data_ptr(), tuple(block_mask.shape), block_mask._version)
+        if self._masks is None or self._masks[0] != key:
+            B, H, U = self.B, self.H, self.B * self.H
+            m = block_mask.expand(B, H, *block_mask.shape[-2:]).reshape(U, *block_mask.shape[-2:])
+            ids = [self.rank * self.n_per + i for i in range(self.n_per)]
+            mu = torch.stack([m[i] if i < U else torch.ones_like(m[0]) for i in ids])
+            self._masks = (key, mu.unsqueeze(0).contiguous())
+        return self._masks[1]
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                 block_mask: torch.Tensor):
+        """q, k, v: [B, S/P, H, 128] bf16 (this rank's shard, any strides with
+        stride(-1) == 1); block_mask: bool [B or 1, H, nq, nk] over the full
+        sequence, the same on every rank. Returns (out [B, S/P, H, 128] bf16,
+        lse [B, H, S/P] fp32), this object's buffers."""
+        import ctypes
+
+        from . import _lib, ops
+
+        shape = (self.B, self.Sr, self.H, self.D)
+        for x in (q, k, v):
+            if tuple(x.shape) != shape or x.dtype != torch.bfloat16 or x.device != self.device:
+                raise ValueError(f"expected bf16 {shape} on {self.device}, got "
+                                 f"{x.dtype} {tuple(x.shape)} on {x.device}")
+        mu = self._unit_masks(block_mask)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        src = (ctypes.c_void_p * 3)(q.data_ptr(), k.data_ptr(), v.data_ptr())
+        st = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride())
+        self._fence()
+        _lib.check(self._lib.sa_ulysses_dispatch(3, src, st, self.B, self.Sr, self.H, self.D,
+                                                 self.world, self.rank, self.n_per,
+                                                 self._recv_ptrs, ctypes.c_void_p(stream)),
+                   "sa_ulysses_dispatch")
+        self._fence()
+        r = self.recv
+        ops.bsattn_fwd(r[0].unsqueeze(0), r[1].unsqueeze(0), r[2].unsqueeze(0), mu,
+                       out=self._attn_out, lse=self._attn_lse)
+        _lib.check(self._lib.sa_ulysses_combine(self._attn_out.data_ptr(), self._attn_lse.data_ptr(),
+                                                self.B, self.Sr, self.H, self.D, self.world,
+                                                self.rank, self.n_per, self._out_ptrs,
+                                                self._lse_ptrs, ctypes.c_void_p(stream)),
+                   "sa_ulysses_combine")
+        self._fence()
+        return self.out, self.lse
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (a collective call:
+        every rank must be done with every buffer first)."""
+        import torch.distributed as dist
+
+        if not self._own:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self._lib.sa_ipc_close(p)
+            self._opened = []
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            self.recv = self.out = self.lse = None
+            for p in self._own.values():
+                self._lib.sa_ipc_free(p)
+        self._own = {}

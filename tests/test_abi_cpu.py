@@ -327,3 +327,32 @@ def test_status_word_check_and_selftest_validation(lib):
     assert "limit" in _lib.last_error()
     assert lib.sa_selftest_wait_timeout(ctypes.addressof(word), 2 * 10**9, None) == _lib.SA_EINVAL
     assert lib.sa_selftest_wait_timeout(None, 10**6, None) == _lib.SA_EINVAL
+
+
+def test_ulysses_exchange_validation(lib):
+    """The exchange entry points refuse what they cannot run before any
+    launch."""
+    from sinkattn_b200 import _lib
+
+    st = _i64(*([4 * 3 * 128, 3 * 128, 128, 1] * 3))
+    src = (ctypes.c_void_p * 3)(256, 256, 256)
+    dst = (ctypes.c_void_p * 9)(*([512] * 9))
+
+    def dispatch(T=3, D=128, P=2, rank=0, n_per=3, B=2, H=3):
+        return lib.sa_ulysses_dispatch(T, src, st, B, 4, H, D, P, rank, n_per, dst, None)
+
+    assert dispatch(D=64) == _lib.SA_EINVAL and "128" in _lib.last_error()
+    assert dispatch(P=9) == _lib.SA_EINVAL and "ranks" in _lib.last_error()
+    assert dispatch(rank=2) == _lib.SA_EINVAL and "rank" in _lib.last_error()
+    assert dispatch(T=4) == _lib.SA_EINVAL and "tensors" in _lib.last_error()
+    assert dispatch(n_per=2) == _lib.SA_EINVAL and "units" in _lib.last_error()
+    bad = _i64(*([4 * 3 * 128, 3 * 128, 100, 1] * 3))
+    assert lib.sa_ulysses_dispatch(3, src, bad, 2, 4, 3, 128, 2, 0, 3, dst, None) == _lib.SA_EINVAL
+    assert lib.sa_ulysses_combine(256, None, 2, 4, 3, 128, 2, 0, 3, dst, dst, None) == \
+        _lib.SA_EINVAL and "together" in _lib.last_error()
+    assert lib.sa_ulysses_combine(256, None, 2, 4, 3, 128, 2, 5, 3, dst, None, None) == \
+        _lib.SA_EINVAL
+    ptr = ctypes.c_void_p()
+    assert lib.sa_ipc_alloc(0, ctypes.byref(ptr)) == _lib.SA_EINVAL
+    assert lib.sa_ipc_get_handle(None, None) == _lib.SA_EINVAL
+    assert lib.sa_ipc_free(None) == _lib.SA_OK and lib.sa_ipc_close(None) == _lib.SA_OK

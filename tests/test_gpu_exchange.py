@@ -1,0 +1,80 @@
+"""The Ulysses dispatch and combine kernels (csrc/exchange.cu) on one GPU.
+
+The kernels write into whatever device addresses they are given: for a
+real exchange those are the peers' buffers mapped with CUDA IPC; here every
+simulated rank's buffers are ordinary allocations on the one GPU, and the
+kernel is called once per simulated rank, one after the other. That checks
+every index the kernels compute against the layout written out with torch:
+  dispatch: rank p's shard row (b, s, h) -> owner of unit u = b*H + h, at
+            [t, u % n_per, p*Sr + s];
+  combine:  owner r's unit row (j, s) -> rank s // Sr, at [b, s % Sr, h]
+            (output) and [b, h, s % Sr] (LSE); padding units are skipped.
+The exchange across real GPUs is in test_gpu_multi.py.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("B,H,P,Sr", [(2, 3, 3, 64), (1, 5, 2, 100), (2, 12, 8, 32)])
+def test_dispatch_and_combine_layouts(B, H, P, Sr):
+    from sinkattn_b200 import _lib
+
+    lib = _lib.load()
+    D = 128
+    U = B * H
+    n_per = -(-U // P)
+    S = P * Sr
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + H * 10 + P)
+    # each rank's Q, K, V shards; K as a strided view (H padded to H + 1)
+    shards = []
+    for p in range(P):
+        q = torch.randn(B, Sr, H, D, device="cuda", generator=g).bfloat16()
+        k = torch.randn(B, Sr, H + 1, D, device="cuda", generator=g).bfloat16()[:, :, :H]
+        v = torch.randn(B, Sr, H, D, device="cuda", generator=g).bfloat16()
+        shards.append((q, k, v))
+    recv = [torch.zeros(3, n_per, S, D, dtype=torch.bfloat16, device="cuda") for _ in range(P)]
+    dst = (ctypes.c_void_p * P)(*[r.data_ptr() for r in recv])
+    for p, (q, k, v) in enumerate(shards):
+        src = (ctypes.c_void_p * 3)(q.data_ptr(), k.data_ptr(), v.data_ptr())
+        st = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride())
+        _lib.check(lib.sa_ulysses_dispatch(3, src, st, B, Sr, H, D, P, p, n_per, dst, _stream()),
+                   "sa_ulysses_dispatch")
+    torch.cuda.synchronize()
+    for t in range(3):
+        full = torch.cat([shards[p][t] for p in range(P)], dim=1)  # [B, S, H, D]
+        for u in range(U):
+            b, h = divmod(u, H)
+            r, j = divmod(u, n_per)
+            assert torch.equal(recv[r][t, j], full[b, :, h]), (t, u)
+    # padding units were not written
+    for r in range(P):
+        for j in range(n_per):
+            if r * n_per + j >= U:
+                assert not recv[r][:, j].any()
+
+    outs = [torch.randn(n_per, S, D, device="cuda", generator=g).bfloat16() for _ in range(P)]
+    lses = [torch.randn(n_per, S, device="cuda", generator=g) for _ in range(P)]
+    out_dst = [torch.zeros(B, Sr, H, D, dtype=torch.bfloat16, device="cuda") for _ in range(P)]
+    lse_dst = [torch.zeros(B, H, Sr, device="cuda") for _ in range(P)]
+    od = (ctypes.c_void_p * P)(*[o.data_ptr() for o in out_dst])
+    ld = (ctypes.c_void_p * P)(*[o.data_ptr() for o in lse_dst])
+    for r in range(P):
+        _lib.check(lib.sa_ulysses_combine(outs[r].data_ptr(), lses[r].data_ptr(), B, Sr, H, D, P,
+                                          r, n_per, od, ld, _stream()), "sa_ulysses_combine")
+    torch.cuda.synchronize()
+    for u in range(U):
+        b, h = divmod(u, H)
+        r, j = divmod(u, n_per)
+        for p in range(P):
+            assert torch.equal(out_dst[p][b, :, h], outs[r][j, p * Sr:(p + 1) * Sr]), (u, p)
+            assert torch.equal(lse_dst[p][b, h], lses[r][j, p * Sr:(p + 1) * Sr]), (u, p)

@@ -1,6 +1,6 @@
-"""Two-GPU checks over NCCL (skipped with fewer than 2 GPUs): the Ulysses
-exchange around the CUDA kernel equals the single-GPU result, and unit
-sharding covers a job exactly."""
+"""Two-GPU checks (skipped with fewer than 2 GPUs): the Ulysses exchange
+around the CUDA kernel, over NCCL all-to-alls and over NVLink peer memory,
+equals the single-GPU result, and unit sharding covers a job exactly."""
 from __future__ import annotations
 
 import datetime
@@ -54,6 +54,16 @@ def _worker(rank, world, port, result_dir):
         out3, lse3 = ulysses_sink_attention(qs, ks, vs, mask.to(dev), chunks=3)
         torch.cuda.synchronize()
         assert torch.equal(out3, out) and torch.equal(lse3, lse)
+        # the same exchange over NVLink peer memory (dispatch / combine
+        # kernels into CUDA-IPC-mapped buffers), twice on the same buffers
+        from sinkattn_b200.sharding import UlyssesPeerExchange
+
+        ex = UlyssesPeerExchange(B, S, H, device=dev)
+        for _ in range(2):
+            out_p, lse_p = ex(qs, ks, vs, mask.to(dev))
+            torch.cuda.synchronize()
+            assert torch.equal(out_p, out) and torch.equal(lse_p, lse)
+        ex.close()
         torch.save({"out": out.cpu(), "lse": lse.cpu()}, os.path.join(result_dir, f"r{rank}.pt"))
         dist.barrier()
     finally:
