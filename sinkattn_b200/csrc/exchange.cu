@@ -38,26 +38,49 @@ struct DispatchParams {
   int T, B, Sr, H, P, rank, n_per;
 };
 
-__global__ void __launch_bounds__(256) dispatch_kernel(const DispatchParams p) {
-  const int64_t rows = (int64_t)p.T * p.B * p.Sr * p.H;
+// Source and destination of 16-byte piece i (row (t, b, s, h), h fastest).
+__device__ __forceinline__ void dispatch_piece(const DispatchParams& p, int64_t i,
+                                               const uint8_t*& from, uint8_t*& to) {
   const int64_t S = (int64_t)p.P * p.Sr;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * kPieces;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int piece = (int)(i % kPieces);
-    int64_t row = i / kPieces;  // (t, b, s, h), h fastest
-    const int h = (int)(row % p.H);
-    row /= p.H;
-    const int s = (int)(row % p.Sr);
-    row /= p.Sr;
-    const int b = (int)(row % p.B);
-    const int t = (int)(row / p.B);
-    const uint4 v = *reinterpret_cast<const uint4*>(
-        p.src[t] + ((b * p.st[t][0] + s * p.st[t][1] + h * p.st[t][2]) * 2 + piece * 16));
-    const int u = b * p.H + h;
-    const int owner = u / p.n_per, j = u - owner * p.n_per;
-    uint8_t* d = p.dst[owner] +
-                 ((((int64_t)t * p.n_per + j) * S + (int64_t)p.rank * p.Sr + s) * kD * 2 + piece * 16);
-    *reinterpret_cast<uint4*>(d) = v;
+  const int piece = (int)(i % kPieces);
+  int64_t row = i / kPieces;
+  const int h = (int)(row % p.H);
+  row /= p.H;
+  const int s = (int)(row % p.Sr);
+  row /= p.Sr;
+  const int b = (int)(row % p.B);
+  const int t = (int)(row / p.B);
+  from = p.src[t] + ((b * p.st[t][0] + s * p.st[t][1] + h * p.st[t][2]) * 2 + piece * 16);
+  const int u = b * p.H + h;
+  const int owner = u / p.n_per, j = u - owner * p.n_per;
+  to = p.dst[owner] +
+       ((((int64_t)t * p.n_per + j) * S + (int64_t)p.rank * p.Sr + s) * kD * 2 + piece * 16);
+}
+
+// Each thread moves kUnroll pieces per step, loads first, so that several
+// loads are in flight before the (local or NVLink) stores.
+constexpr int kUnroll = 4;
+
+__global__ void __launch_bounds__(256) dispatch_kernel(const DispatchParams p) {
+  const int64_t n = (int64_t)p.T * p.B * p.Sr * p.H * kPieces;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n;
+       i0 += stride * kUnroll) {
+    uint4 v[kUnroll];
+    uint8_t* to[kUnroll];
+#pragma unroll
+    for (int e = 0; e < kUnroll; ++e) {
+      const int64_t i = i0 + e * stride;
+      to[e] = nullptr;
+      if (i < n) {
+        const uint8_t* from;
+        dispatch_piece(p, i, from, to[e]);
+        v[e] = *reinterpret_cast<const uint4*>(from);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kUnroll; ++e)
+      if (to[e] != nullptr) *reinterpret_cast<uint4*>(to[e]) = v[e];
   }
   __threadfence_system();
 }
@@ -73,31 +96,48 @@ struct CombineParams {
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   const int U = p.B * p.H;
   const int64_t S = (int64_t)p.P * p.Sr;
-  const int64_t rows = (int64_t)p.n_per * S;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * (kPieces + 1);
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / (kPieces + 1);
-    const int piece = (int)(i - row * (kPieces + 1));  // kPieces: the LSE value
-    const int j = (int)(row / S);
-    const int64_t s = row - (int64_t)j * S;
-    const int u = p.rank * p.n_per + j;
-    if (u >= U) continue;  // a padding unit
-    const int b = u / p.H, h = u - (u / p.H) * p.H;
-    const int owner = (int)(s / p.Sr);
-    const int64_t sl = s - (int64_t)owner * p.Sr;
-    if (piece < kPieces) {
-      const uint4 v = *reinterpret_cast<const uint4*>(p.out + (row * kD * 2 + piece * 16));
-      *reinterpret_cast<uint4*>(p.out_dst[owner] +
-                                ((((int64_t)b * p.Sr + sl) * p.H + h) * kD * 2 + piece * 16)) = v;
-    } else if (p.lse_dst[0] != nullptr) {
-      p.lse_dst[owner][((int64_t)b * p.H + h) * p.Sr + sl] = p.lse[row];
+  const int64_t n = (int64_t)p.n_per * S * (kPieces + 1);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n;
+       i0 += stride * kUnroll) {
+    uint4 v[kUnroll];
+    float l[kUnroll];
+    uint8_t* to[kUnroll];
+    float* lto[kUnroll];
+#pragma unroll
+    for (int e = 0; e < kUnroll; ++e) {
+      const int64_t i = i0 + e * stride;
+      to[e] = nullptr;
+      lto[e] = nullptr;
+      if (i >= n) continue;
+      const int64_t row = i / (kPieces + 1);
+      const int piece = (int)(i - row * (kPieces + 1));  // kPieces: the LSE value
+      const int j = (int)(row / S);
+      const int64_t s = row - (int64_t)j * S;
+      const int u = p.rank * p.n_per + j;
+      if (u >= U) continue;  // a padding unit
+      const int b = u / p.H, h = u - (u / p.H) * p.H;
+      const int owner = (int)(s / p.Sr);
+      const int64_t sl = s - (int64_t)owner * p.Sr;
+      if (piece < kPieces) {
+        v[e] = *reinterpret_cast<const uint4*>(p.out + (row * kD * 2 + piece * 16));
+        to[e] = p.out_dst[owner] + ((((int64_t)b * p.Sr + sl) * p.H + h) * kD * 2 + piece * 16);
+      } else if (p.lse_dst[0] != nullptr) {
+        l[e] = p.lse[row];
+        lto[e] = p.lse_dst[owner] + ((int64_t)b * p.H + h) * p.Sr + sl;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kUnroll; ++e) {
+      if (to[e] != nullptr) *reinterpret_cast<uint4*>(to[e]) = v[e];
+      if (lto[e] != nullptr) *lto[e] = l[e];
     }
   }
   __threadfence_system();
 }
 
 int grid_for(int64_t work) {
-  const int64_t want = (work + 255) / 256;
+  const int64_t want = (work + 256 * kUnroll - 1) / (256 * kUnroll);
   const int64_t cap = (int64_t)sm_count_current_device() * 8;
   return (int)(want < cap ? (want > 0 ? want : 1) : cap);
 }

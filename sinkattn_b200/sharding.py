@@ -255,17 +255,20 @@ class UlyssesPeerExchange:
     peer memory.
 
     Made once per (B, S, H) on every rank of `group` (a collective call):
-    each rank allocates its receive buffer [3, n_per, S, 128] (Q, K, V of its
-    units), its output [B, S/P, H, 128] and LSE [B, H, S/P], and maps the
-    peers' buffers with CUDA IPC. A call then runs, on the current stream:
+    each rank allocates two receive buffers [3, n_per, S, 128] (Q, K, V of its
+    units; calls alternate between them), its output [B, S/P, H, 128] and
+    LSE [B, H, S/P], and maps the peers' buffers with CUDA IPC. A call then
+    runs, on the current stream:
 
-        fence; dispatch (Q, K, V rows -> owners); fence;
+        dispatch (Q, K, V rows -> owners); fence;
         attention on the rank's units (the receive buffer as it lies);
         combine (output rows and LSE -> sequence owners); fence
 
     where a fence is a 4-byte all-reduce: every rank is past the previous
-    step, so a buffer is written only when its owner is done with it, and
-    read only when every writer is done. The returned output and LSE are
+    step, so a buffer is read only when every writer is done. A receive
+    buffer is written again two calls later, after its owner's attention on
+    it has passed the previous call's fences; an output is written after its
+    owner has passed the dispatch of the same call. The returned output and LSE are
     this object's buffers: valid until the next call, which overwrites them,
     so read them on the same stream before calling again.
     At most 8 ranks; D = 128; S divisible by the world size.
@@ -292,8 +295,8 @@ class UlyssesPeerExchange:
             else torch.device(device)
         lib = _lib.load()
         self._lib = lib
-        sizes = {"recv": 3 * self.n_per * S * D * 2, "out": B * self.Sr * H * D * 2,
-                 "lse": B * H * self.Sr * 4}
+        slot = 3 * self.n_per * S * D * 2
+        sizes = {"recv": 2 * slot, "out": B * self.Sr * H * D * 2, "lse": B * H * self.Sr * 4}
         self._own: dict[str, int] = {}
         self._opened: list[int] = []
         handles = {}
@@ -308,7 +311,8 @@ class UlyssesPeerExchange:
             views = {n: _device_view(p, sizes[n], self.device) for n, p in self._own.items()}
             for v in views.values():
                 v.zero_()  # padding units read zeros
-            self.recv = views["recv"].view(torch.bfloat16).view(3, self.n_per, S, D)
+            self._recv2 = views["recv"].view(torch.bfloat16).view(2, 3, self.n_per, S, D)
+            self._slot = 0
             self.out = views["out"].view(torch.bfloat16).view(B, self.Sr, H, D)
             self.lse = views["lse"].view(torch.float32).view(B, H, self.Sr)
             everyone = [None] * self.world
@@ -325,7 +329,7 @@ class UlyssesPeerExchange:
                     ptrs[n][r] = int(p.value)
                     self._opened.append(int(p.value))
             VP = ctypes.c_void_p * self.world
-            self._recv_ptrs = VP(*ptrs["recv"])
+            self._recv_ptrs = [VP(*[q + k * slot for q in ptrs["recv"]]) for k in range(2)]
             self._out_ptrs = VP(*ptrs["out"])
             self._lse_ptrs = VP(*ptrs["lse"])
             self._attn_out = torch.empty(1, self.n_per, S, D, dtype=torch.bfloat16,
@@ -371,13 +375,14 @@ class UlyssesPeerExchange:
         stream = torch.cuda.current_stream(self.device).cuda_stream
         src = (ctypes.c_void_p * 3)(q.data_ptr(), k.data_ptr(), v.data_ptr())
         st = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride())
-        self._fence()
+        k_ = self._slot
+        self._slot ^= 1
         _lib.check(self._lib.sa_ulysses_dispatch(3, src, st, self.B, self.Sr, self.H, self.D,
                                                  self.world, self.rank, self.n_per,
-                                                 self._recv_ptrs, ctypes.c_void_p(stream)),
+                                                 self._recv_ptrs[k_], ctypes.c_void_p(stream)),
                    "sa_ulysses_dispatch")
         self._fence()
-        r = self.recv
+        r = self._recv2[k_]
         ops.bsattn_fwd(r[0].unsqueeze(0), r[1].unsqueeze(0), r[2].unsqueeze(0), mu,
                        out=self._attn_out, lse=self._attn_lse)
         _lib.check(self._lib.sa_ulysses_combine(self._attn_out.data_ptr(), self._attn_lse.data_ptr(),
@@ -404,7 +409,7 @@ class UlyssesPeerExchange:
             torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         with torch.cuda.device(self.device):
-            self.recv = self.out = self.lse = None
+            self._recv2 = self.out = self.lse = None
             for p in self._own.values():
                 self._lib.sa_ipc_free(p)
         self._own = {}
