@@ -487,6 +487,9 @@ def run_ours(args):
     e2e_value = flops20 * args.steps / (te2e / 1e3) / 1e12
 
     trace("e2e timed")
+    # ---- cfg5: the full DiT step (sequence parallel at N > 1) ---------------
+    dit = None if args.skip_dit else dit_leg(args, world, rank, dev, stream)
+    trace("dit timed")
     # ---- CPU baseline (rank 0, N=1 only) ------------------------------------
     cpu = cpu_cal = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -519,6 +522,7 @@ def run_ours(args):
                                "unit": UNIT},
         **(calib_legs or {}),
         "ulysses": ulysses,
+        "dit_step_cfg5": dit,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": te2e / args.steps,
                 "chunk_heads": hg,
@@ -739,6 +743,61 @@ def e2e_leg(args, q_bshd, k_bshd, v_bshd, mask20, segs, dev, stream, world):
     h2d = sum_over_ranks(3 * S * n_heads * D * 2, world, dev)
     d2h = sum_over_ranks(S * n_heads * D * 2 + n_heads * S * 2, world, dev)
     return te2e, h2d, d2h, hg
+
+
+def dit_leg(args, world, rank, dev, stream):
+    """BASELINE cfg5: one step of a random-weight Wan2.1-1.3B-shaped DiT (30
+    blocks, latent [2,16,21,60,104] = 32760 tokens, text 512 x 4096, weights
+    N(0,0.02) seed 0; tests/wan_dit.py) whose self-attention runs the
+    reference's WanSinkSparseAttnProcessor2_0 with install() in place, each
+    layer with its cfg3 calibration-pass mask and the Wan runtime default
+    (pooled K/V gap 30, adaptive mix). At N > 1 the activations are
+    sequence-sharded (S/N tokens per rank) and the attention goes through the
+    peer-memory Ulysses exchange. Returns the max-over-ranks step time."""
+    ref_dir = Path(os.environ.get("SINKATTN_REFERENCE", ROOT / "baseline" / "_ref"))
+    if not (ref_dir / "wanx").exists():
+        return {"unavailable": f"reference processors not installed under {ref_dir}"}
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    from sinkattn_b200 import ops
+    from sinkattn_b200 import reference_api as ra
+    from tests import wan_dit
+    from tests.gen import wan_qk_layers_on_device
+
+    ra.install()
+    layers = wan_qk_layers_on_device(30, dev)
+    masks = ops.calibration_pass(layers, force_sink_col=True)[0]
+    del layers
+    torch.cuda.empty_cache()
+    model, ex = wan_dit.build(masks, dev, world=world, rank=rank)
+    x, t, text, rot = wan_dit.inputs(dev)
+    shard = (rank, world) if world > 1 else None
+
+    def step():
+        with torch.no_grad():
+            model(x, t, text, rot, shard=shard)
+
+    steps = 3
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    total, per = time_steps(step, steps, stream)
+    barrier(world)
+    ms = max_over_ranks(total / steps, world, dev)
+    tokens = x.shape[0] * rot.shape[2]
+    res = {"ms_per_step": ms, "tokens_per_s": tokens / (ms / 1e3), "layers": len(model.blocks),
+           "tokens": tokens, "ranks": world, "steps": steps,
+           "mask_density": float(masks.float().mean().item()),
+           "parallelism": ("sequence parallel, Ulysses exchange over NVLink peer memory"
+                           if world > 1 else "one GPU"),
+           "attention": "reference WanSinkSparseAttnProcessor2_0 with install(): fused Q/K "
+                        "RMSNorm + RoPE producer, fused sink + pooled-K/V dynamic kernel"}
+    if ex is not None:
+        ex.close()
+    del model, x, text, rot, masks
+    torch.cuda.empty_cache()
+    return res
 
 
 def cpu_legs():
@@ -1105,6 +1164,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    ap.add_argument("--skip-dit", action="store_true", help="omit the cfg5 full-DiT leg")
     ap.add_argument("--e2e-chunk-heads", type=int, default=1,
                     help="heads per host<->device chunk of the end-to-end leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",

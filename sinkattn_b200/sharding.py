@@ -345,23 +345,34 @@ class UlyssesPeerExchange:
 
         dist.all_reduce(self._flag, group=self.group)
 
+    def unit_masks(self, block_mask: torch.Tensor) -> torch.Tensor:
+        """This rank's units' rows of a [B or 1, H, nq, nk] mask, as the
+        [1, n_per, nq, nk] mask its attention call takes (padding units all
+        true)."""
+        B, H, U = self.B, self.H, self.B * self.H
+        m = block_mask.expand(B, H, *block_mask.shape[-2:]).reshape(U, *block_mask.shape[-2:])
+        ids = [self.rank * self.n_per + i for i in range(self.n_per)]
+        mu = torch.stack([m[i] if i < U else torch.ones_like(m[0]) for i in ids])
+        return mu.unsqueeze(0).contiguous()
+
     def _unit_masks(self, block_mask: torch.Tensor) -> torch.Tensor:
-        # the rank's units' mask rows (padding units all true), cached per mask
+        # cached for the last mask seen
         key = (block_mask.data_ptr(), tuple(block_mask.shape), block_mask._version)
         if self._masks is None or self._masks[0] != key:
-            B, H, U = self.B, self.H, self.B * self.H
-            m = block_mask.expand(B, H, *block_mask.shape[-2:]).reshape(U, *block_mask.shape[-2:])
-            ids = [self.rank * self.n_per + i for i in range(self.n_per)]
-            mu = torch.stack([m[i] if i < U else torch.ones_like(m[0]) for i in ids])
-            self._masks = (key, mu.unsqueeze(0).contiguous())
+            self._masks = (key, self.unit_masks(block_mask))
         return self._masks[1]
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                 block_mask: torch.Tensor):
+                 block_mask: Optional[torch.Tensor] = None, unit_masks=None,
+                 attn_fn: Optional[Callable] = None):
         """q, k, v: [B, S/P, H, 128] bf16 (this rank's shard, any strides with
         stride(-1) == 1); block_mask: bool [B or 1, H, nq, nk] over the full
-        sequence, the same on every rank. Returns (out [B, S/P, H, 128] bf16,
-        lse [B, H, S/P] fp32), this object's buffers."""
+        sequence, the same on every rank, or unit_masks (from unit_masks()).
+        attn_fn(q, k, v, mask, out) runs the attention of the rank's units
+        ([1, n_per, S, 128] views, mask [1, n_per, nq, nk]) into `out` and
+        returns the LSE [1, n_per, S] fp32 or None; by default the sink
+        attention kernel. Returns (out [B, S/P, H, 128] bf16, lse [B, H, S/P]
+        fp32 or None), this object's buffers."""
         import ctypes
 
         from . import _lib, ops
@@ -371,7 +382,7 @@ class UlyssesPeerExchange:
             if tuple(x.shape) != shape or x.dtype != torch.bfloat16 or x.device != self.device:
                 raise ValueError(f"expected bf16 {shape} on {self.device}, got "
                                  f"{x.dtype} {tuple(x.shape)} on {x.device}")
-        mu = self._unit_masks(block_mask)
+        mu = unit_masks if unit_masks is not None else self._unit_masks(block_mask)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         src = (ctypes.c_void_p * 3)(q.data_ptr(), k.data_ptr(), v.data_ptr())
         st = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride())
@@ -383,15 +394,23 @@ class UlyssesPeerExchange:
                    "sa_ulysses_dispatch")
         self._fence()
         r = self._recv2[k_]
-        ops.bsattn_fwd(r[0].unsqueeze(0), r[1].unsqueeze(0), r[2].unsqueeze(0), mu,
-                       out=self._attn_out, lse=self._attn_lse)
-        _lib.check(self._lib.sa_ulysses_combine(self._attn_out.data_ptr(), self._attn_lse.data_ptr(),
-                                                self.B, self.Sr, self.H, self.D, self.world,
-                                                self.rank, self.n_per, self._out_ptrs,
-                                                self._lse_ptrs, ctypes.c_void_p(stream)),
-                   "sa_ulysses_combine")
+        if attn_fn is None:
+            ops.bsattn_fwd(r[0].unsqueeze(0), r[1].unsqueeze(0), r[2].unsqueeze(0), mu,
+                           out=self._attn_out, lse=self._attn_lse)
+            lse = self._attn_lse
+        else:
+            lse = attn_fn(r[0].unsqueeze(0), r[1].unsqueeze(0), r[2].unsqueeze(0), mu,
+                          self._attn_out)
+            if lse is not None and (tuple(lse.shape) != tuple(self._attn_lse.shape)
+                                    or lse.dtype != torch.float32 or not lse.is_contiguous()):
+                raise ValueError("attn_fn must return an fp32 [1, n_per, S] LSE or None")
+        _lib.check(self._lib.sa_ulysses_combine(
+            self._attn_out.data_ptr(), None if lse is None else lse.data_ptr(), self.B, self.Sr,
+            self.H, self.D, self.world, self.rank, self.n_per, self._out_ptrs,
+            None if lse is None else self._lse_ptrs, ctypes.c_void_p(stream)),
+            "sa_ulysses_combine")
         self._fence()
-        return self.out, self.lse
+        return self.out, (self.lse if lse is not None else None)
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's (a collective call:
