@@ -163,6 +163,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  // A launch made after an earlier bounded wait gave up (the status word is
+  // already set) does no work: its outputs could not be trusted either, and
+  // the word stays set for the host to read. Checked once per CTA, before
+  // any barrier, TMEM or tile counter is touched.
+  if (p.status != nullptr) {
+    __shared__ int s_skip;
+    if (threadIdx.x == 0) s_skip = status_set(p.status) ? 1 : 0;
+    __syncthreads();
+    if (s_skip) return;
+  }
+
   // ---- set-up: barriers, TMEM ----------------------------------------------
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
