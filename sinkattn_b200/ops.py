@@ -520,15 +520,17 @@ def calibration_pass(
     """Pooling + pooled softmax + batch mean + coverage mask for a sequence of
     layers, each given as a (q, k) pair of bf16 [B,H,S,D] CUDA tensors.
 
-    At the calibration shapes (D = 128, block 128, at most 256 blocks) each
-    layer is one fused launch (sa_calibration_layer) on the caller's stream,
-    back to back, with the layer's score and mask work overlapping its own
-    pooling; `chunk` and `head_groups` then have no effect (fused=False
-    selects the pipeline below at any shape; both give the same bits). The coverage
-    masks use row totals summed on the device (fp64, rounded); with
-    want_flags the SA_ROW_* flags of every row are returned too.
+    Several layers run a pipeline over layers (below), which overlaps each
+    chunk's scores and masks with the next chunk's pooling; one layer at the
+    calibration shapes (D = 128, block 128, at most 256 blocks) is one fused
+    launch (sa_calibration_layer), whose score and mask work overlaps its own
+    pooling. `fused` forces either choice (fused=True needs those shapes);
+    with it, `chunk` and `head_groups` have no effect. The two agree to within
+    one ulp on the batch means. The coverage masks use row totals summed on
+    the device (fp64, rounded); with want_flags the SA_ROW_* flags of every
+    row are returned too.
 
-    Other shapes run a pipeline over layers: the work goes in units of
+    The pipeline: the work goes in units of
     (layer, group of H/head_groups heads) and the
     units in chunks of `chunk`: every unit of a chunk is pooled back to back
     on one side stream (HBM-bound, one persistent TMA kernel per unit), then
@@ -548,7 +550,7 @@ def calibration_pass(
     L = len(layers)
     flags = torch.empty((L, H, nb), dtype=torch.int32, device=dev) if want_flags else None
     if fused is None:
-        fused = _fused_calibration_ok(q0, block)
+        fused = L == 1 and _fused_calibration_ok(q0, block)
     elif fused and not _fused_calibration_ok(q0, block):
         raise ValueError("the fused calibration layer needs D = 128, block 128 and S <= 32768")
     if fused:
