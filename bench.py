@@ -1056,12 +1056,14 @@ def run_case(args):
             flops = kept_flops(mask)
             fn = lambda: ops.bsattn_fwd(q, k, v, mask)  # noqa: E731
         else:
+            # one layer's calibration as the product runs it: one fused launch
             ws = torch.empty(ops.pool_scores_workspace_size(B, H, S, D), dtype=torch.uint8, device=dev)
+            cm = torch.empty(H, NB, NB, dtype=torch.bool, device=dev)
             flops = 0.0
 
             def fn():
-                _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
-                ops.coverage_mask(bm, force_sink_col=True)
+                ops.calibration_layer(q, k, want_batch_mean=False, mask_out=cm,
+                                      force_sink_col=True, workspace=ws)
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -1079,10 +1081,11 @@ def run_case(args):
     elif args.case == "calib-small":
         q, k, _ = wan_qk(seed=0, B=2, H=4, dtype=torch.bfloat16, device=dev)
         ws = torch.empty(ops.pool_scores_workspace_size(2, 4, S, D), dtype=torch.uint8, device=dev)
+        cm = torch.empty(4, NB, NB, dtype=torch.bool, device=dev)
 
         def fn():
-            _, bm = ops.pool_scores(q, k, want_scores=False, want_batch_mean=True, workspace=ws)
-            ops.coverage_mask(bm, force_sink_col=True)
+            ops.calibration_layer(q, k, want_batch_mean=False, mask_out=cm, force_sink_col=True,
+                                  workspace=ws)
     else:
         raise SystemExit(f"unknown case {args.case}")
     fn()
