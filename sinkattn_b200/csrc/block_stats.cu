@@ -5,10 +5,13 @@
 //          score[qb, kb] = mean over the query rows r of block qb of
 //            sum_{n in kb} exp(s_rn - m_r) / max(sum_n exp(s_rn - m_r), 1e-6),
 //          s = q k^T / sqrt(D), m_r the row maximum over all keys.
-//          Two sweeps over the keys: the first finds m_r (maxima only, no
-//          exponentials); the second computes every block's unnormalised mass
-//          and the row sum in the same exponentials and keeps the masses in a
-//          per-CTA scratch slot, which the epilogue normalises and averages.
+//          One sweep over the keys: every block's mass is taken under the
+//          block's own row maximum R_j (c_j = sum_{n in j} exp2(s_rn - R_j),
+//          each term at most 1), and the scratch slot keeps c_j and R_j. The
+//          epilogue rescales by exp2(R_j - m_r) once the row maximum m_r is
+//          known, sums the row total from the same products in block order,
+//          and normalises and averages: one exponential per (row, key) and one
+//          per (row, block), where two sweeps needed the keys' QK twice.
 //   MAX    the Triton pooling kernel attn_with_pooling (sinkattention/pooling_kernel.py:
 //          11-248), whose statistics are maxima (the "pooled" name notwithstanding):
 //            R[r, kb] = bf16( max_{n in kb} s_rn * log2(e) )         (line 45-48)
@@ -36,9 +39,10 @@
 //   released by both issuers (by a commit after its MMAs, or an arrival when
 //   the work item has no second tile).
 // TMEM: S buffers [0,128) and [256,384) of tile 0, [128,256) of tile 1;
-// Q_0 [384,448), Q_1 [448,512) (bf16 pairs, the A-operand layout). Each CTA owns one scratch slot of 2 x nk x 128 fp32
-// values (block masses, or the bf16-rounded block maxima), written with one
-// coalesced store per block.
+// Q_0 [384,448), Q_1 [448,512) (bf16 pairs, the A-operand layout). Each CTA owns one scratch slot
+// per query tile: nk x 128 fp32 values (the bf16-rounded block maxima) in max
+// mode, 2 x nk x 128 (block masses, then block maxima) in exact mode, written
+// with one coalesced store per block.
 
 #include <math.h>
 
@@ -120,8 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   SmemCtl* ctl = reinterpret_cast<SmemCtl*>(ring + kStages * kTileBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int passes = p.mode == kExact ? 2 : 1;
-  const int items = passes * p.nk;  // K tiles per work item
+  const int items = p.nk;  // K tiles per work item
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -236,7 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    float* slot = p.scratch + ((int64_t)blockIdx.x * kGroups + grp) * p.nk * kBM;
+    const int slot_words = (p.mode == kExact ? 2 : 1) * p.nk * kBM;
+    float* slot = p.scratch + ((int64_t)blockIdx.x * kGroups + grp) * slot_words;
+    float* slot_r = slot + (int64_t)p.nk * kBM;  // exact mode: the blocks' maxima
     float* red = ctl->red[grp][0];    // red[wq][j] at red[wq * kMaxNB + j]
     float* po_s = ctl->po[grp];
     float* psum = ctl->psum[grp];
@@ -278,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = buf_id(grp, cnt % nbg);
         const uint32_t sph = (uint32_t)(cnt / nbg) & 1u;
         ++cnt;
-        const int pass = it / p.nk, j = it % p.nk;
+        const int j = it;
         if (ok)
           ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf], sph, p.status, abort_flag));
         if (!ok) continue;
@@ -302,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 128; ++c)
             if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
         }
-        if (p.mode == kMax || pass == 0) {
+        {
           float mxp[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) mxp[u] = __uint_as_float(r[0][u]);
@@ -318,26 +323,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float R = bmax * p.scale_log2;
           m = fmaxf(m, R);
           // MAX: the block maximum rounded as the Triton kernel stores it
-          // (pooling_kernel.py:45-48); EXACT keeps only the running maximum.
-          if (p.mode == kMax) slot[(int64_t)j * kBM + row] = bf16_round(R);
-          continue;
-        }
-        // EXACT, second sweep: this block's mass for the row under its final
-        // maximum m (every key of the row has been seen in the first sweep)
-        const float negm = -m;
-        float sp[4] = {0.f, 0.f, 0.f, 0.f};
+          // (pooling_kernel.py:45-48).
+          if (p.mode == kMax) {
+            slot[(int64_t)j * kBM + row] = bf16_round(R);
+            continue;
+          }
+          // EXACT: this block's mass under its own maximum R, kept with R
+          const float negR = -R;
+          float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          sp[c & 3] += ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, negm));
-        const float mass = (sp[0] + sp[1]) + (sp[2] + sp[3]);
-        l += mass;
-        slot[(int64_t)j * kBM + row] = mass;
+          for (int c = 0; c < 128; ++c)
+            sp[c & 3] += ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, negR));
+          slot[(int64_t)j * kBM + row] = (sp[0] + sp[1]) + (sp[2] + sp[3]);
+          slot_r[(int64_t)j * kBM + row] = R;
+        }
       }
       __syncwarp();
       float* out = p.scores + ((int64_t)(b * p.H + h) * p.nq + qb) * p.nk;
       if (p.mode == kExact) {
-        // sum over the tile's rows of mass / max(l, 1e-6) (sparse_attention.py:224),
-        // divided by the number of valid rows (the mean of line 225)
+        // the masses under the row maximum m, and the row total l from them in
+        // block order; then the sum over the tile's rows of mass / max(l, 1e-6)
+        // (sparse_attention.py:224), divided by the number of valid rows (the
+        // mean of line 225)
+        for (int j = 0; j < p.nk; ++j) {
+          const int64_t e = (int64_t)j * kBM + row;
+          const float w = row_valid ? slot[e] * ex2_approx(slot_r[e] - m) : 0.f;
+          slot[e] = w;
+          l += w;
+        }
         const float lc = fmaxf(l, 1e-6f);
         for (int j = 0; j < p.nk; ++j) {
           float v = row_valid ? __fdiv_rn(slot[(int64_t)j * kBM + row], lc) : 0.f;
@@ -431,7 +444,8 @@ extern "C" size_t sa_block_stats_workspace_size(int B, int H, int S, int mode) {
   if (B < 1 || H < 1 || S < 1) return 0;
   if (mode != sa::stats::kExact && mode != sa::stats::kMax) return 0;
   const size_t nk = (size_t)((S + 127) / 128);
-  return (size_t)stats_grid(B, H, S) * sa::stats::kGroups * nk * 128 * sizeof(float);
+  const size_t words = (mode == sa::stats::kExact ? 2 : 1) * nk * 128;
+  return (size_t)stats_grid(B, H, S) * sa::stats::kGroups * words * sizeof(float);
 }
 
 extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_strides[4],

@@ -174,7 +174,7 @@ __device__ __forceinline__ void score_bar() {
 }
 
 // Bounded spin until pred() holds; gives up (false) on timeout, recording
-// SA_DEV_WAIT_TIMEOUT, or as soon as another wait of the launch gave up.
+// SA_DEV_WAIT_TIMEOUT. It does not read the status word (possibly host memory).
 template <class Pred>
 __device__ bool spin_until(Pred pred, int32_t* status, uint32_t sleep_ns) {
   if (pred()) return true;
@@ -183,7 +183,6 @@ __device__ bool spin_until(Pred pred, int32_t* status, uint32_t sleep_ns) {
     __nanosleep(sleep_ns);
     if (pred()) return true;
     if ((it & 63u) == 0u) {
-      if (status_set(status)) return false;
       if (global_timer_ns() - t0 > kWaitNs) {
         report_timeout(status);
         return false;
