@@ -1034,7 +1034,11 @@ def run_case(args):
         Bc, Hc = (B, H) if args.case == "stats-wan" else (1, 2)
         q, k, _ = wan_qk(seed=0, B=Bc, H=Hc, dtype=torch.bfloat16, device=dev)
         res = {"case": args.case, "B": Bc, "H": Hc, "S": S}
-        for mode, sweeps in (("exact", 2), ("max", 1)):
+        # Both modes run Q K^T once (2 D FLOP per (query, key) pair); the
+        # exact mode also takes one exponential per pair. `exact_ref_tflops`
+        # counts the reference's exact algorithm, which computes Q K^T twice
+        # (a maximum sweep, then a mass sweep).
+        for mode in ("exact", "max"):
             ws = torch.empty(max(1, ops._lib.load().sa_block_stats_workspace_size(
                 Bc, Hc, S, ops._STATS_MODES[mode])), dtype=torch.uint8, device=dev)
             out = torch.empty(Bc, Hc, NB, NB, dtype=torch.float32, device=dev)
@@ -1045,7 +1049,10 @@ def run_case(args):
             total, _ = time_steps(fn, args.steps, torch.cuda.current_stream(dev))
             ms = total / args.steps
             res[mode + "_ms"] = ms
-            res[mode + "_mma_tflops"] = sweeps * 2.0 * S * S * D * Bc * Hc / (ms / 1e3) / 1e12
+            res[mode + "_mma_tflops"] = 2.0 * S * S * D * Bc * Hc / (ms / 1e3) / 1e12
+            if mode == "exact":
+                res["exact_ref_tflops"] = 2 * res["exact_mma_tflops"]
+                res["exact_gexp_per_s"] = float(S) * S * Bc * Hc / (ms / 1e3) / 1e9
         print(json.dumps(res))
         return 0
     if args.case in ("attn-wan", "calib-wan"):
