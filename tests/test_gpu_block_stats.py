@@ -54,6 +54,28 @@ def test_exact_matches_oracle(oracle, B, H, S, scale):
     np.testing.assert_allclose(got, want, rtol=2e-3, atol=1e-6)
 
 
+def test_exact_row_maximum_jump(oracle):
+    """Key blocks whose logits exceed every earlier block's by more than 100
+    in base 2 for the first 64 query rows and not for the others: the row
+    maximum jumps late in the sweep, so the early blocks' masses are rescaled
+    by factors far below the fp32 range of their own sums."""
+    from sinkattn_b200 import ops
+
+    S = 640
+    g = torch.Generator().manual_seed(3)
+    base = torch.randn(128, generator=g)
+    q = torch.randn(1, 1, S, 128, generator=g)
+    q[0, 0, :64] = base + 0.05 * torch.randn(64, 128, generator=g)
+    k = torch.randn(1, 1, S, 128, generator=g)
+    k[0, 0, 300] = 8.0 * base  # key block 2: logits ~1000 for the first 64 rows
+    k[0, 0, 600] = 12.0 * base  # key block 4: a second jump
+    q, k = q.to(torch.bfloat16), k.to(torch.bfloat16)
+    got = ops.block_stats(q.cuda(), k.cuda(), mode="exact").cpu().numpy()
+    want = oracle.exact_block_mass_scores(q.float().numpy(), k.float().numpy())
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, rtol=2e-3, atol=1e-6)
+
+
 def test_exact_strided_layout(oracle):
     """[B,S,H,D] storage viewed as [B,H,S,D] (the Wan layout) needs no copy."""
     from sinkattn_b200 import ops
