@@ -436,8 +436,14 @@ SA_API int sa_mix_outputs(const void* o_s, const int64_t os_strides[4], const fl
  *   bf16 (contiguous) and LSE [n_per][P*Sr] fp32 (nullable) are written into
  *   out_dst[p] ([B][Sr][H][128] bf16) and lse_dst[p] ([B][H][Sr] fp32) of the
  *   rank p owning each row's stretch of the sequence.
+ * sa_ulysses_dispatch_units / sa_ulysses_combine_units: the same for the unit
+ *   slots j0 <= j < j1 of every owner only (slot j of rank r is unit
+ *   r*n_per + j), so that the exchange of one group of slots can run while
+ *   attention works on another; the plain forms are [0, n_per).
  * Neither waits on another rank: the caller orders them against the peers'
  * use of the same buffers (stream-ordered collectives before and after).
+ * Their kernels run 128-thread blocks at no more than 32 registers a thread,
+ * so that a block fits on an SM beside an attention block.
  */
 SA_API int sa_ipc_alloc(size_t bytes, void** ptr);
 SA_API int sa_ipc_free(void* ptr);
@@ -450,6 +456,13 @@ SA_API int sa_ulysses_dispatch(int T, const void* const* src, const int64_t* src
 SA_API int sa_ulysses_combine(const void* out_units, const float* lse_units, int B, int Sr, int H,
                               int D, int P, int rank, int n_per, void* const* out_dst,
                               float* const* lse_dst, cudaStream_t stream);
+SA_API int sa_ulysses_dispatch_units(int T, const void* const* src, const int64_t* src_strides,
+                                     int B, int Sr, int H, int D, int P, int rank, int n_per,
+                                     int j0, int j1, void* const* dst, cudaStream_t stream);
+SA_API int sa_ulysses_combine_units(const void* out_units, const float* lse_units, int B, int Sr,
+                                    int H, int D, int P, int rank, int n_per, int j0, int j1,
+                                    void* const* out_dst, float* const* lse_dst,
+                                    cudaStream_t stream);
 
 /*
  * The status word. No counterpart in the reference, whose kernels cannot

@@ -97,6 +97,10 @@ _SIGNATURES = {
     "sa_ipc_close": (_i, [_vp]),
     "sa_ulysses_dispatch": (_i, [_i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp]),
     "sa_ulysses_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "sa_ulysses_dispatch_units": (_i, [_i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp,
+                                       _vp]),
+    "sa_ulysses_combine_units": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp,
+                                      _vp]),
     "sa_status_create": (_vp, []),
     "sa_status_device_pointer": (_i, [_vp, _vp]),
     "sa_status_destroy": (_i, [_vp]),

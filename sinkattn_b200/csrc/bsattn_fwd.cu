@@ -163,16 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // A launch made after an earlier bounded wait gave up (the status word is
-  // already set) does no work: its outputs could not be trusted either, and
-  // the word stays set for the host to read. Checked once per CTA, before
-  // any barrier, TMEM or tile counter is touched.
-  if (p.status != nullptr) {
-    __shared__ int s_skip;
-    if (threadIdx.x == 0) s_skip = status_set(p.status) ? 1 : 0;
-    __syncthreads();
-    if (s_skip) return;
-  }
+  // The status word is written on failure and never read here: it lives in
+  // mapped host memory, and one read of it per CTA at entry cost 60-90 us per
+  // launch (148 PCIe round trips).
 
   // ---- set-up: barriers, TMEM ----------------------------------------------
   if (threadIdx.x == 0) {

@@ -36,51 +36,40 @@ struct DispatchParams {
   int64_t st[kMaxTensors][3];  // element strides of b, s, h (d is unit stride)
   uint8_t* dst[kMaxRanks];     // each rank's receive buffer [T][n_per][S][D]
   int T, B, Sr, H, P, rank, n_per;
+  int j0, nj;                  // the owners' unit slots j0 .. j0 + nj - 1
 };
 
-// Source and destination of 16-byte piece i (row (t, b, s, h), h fastest).
-__device__ __forceinline__ void dispatch_piece(const DispatchParams& p, int64_t i,
-                                               const uint8_t*& from, uint8_t*& to) {
+// 128-thread CTAs at no more than 32 registers a thread: one fits on an SM
+// beside a persistent attention CTA (512 threads, up to 120 registers), so the
+// exchange of one group of units can run while attention works on another.
+constexpr int kXThreads = 128;
+constexpr int kXMinBlocks = 16;
+
+// Thread i moves 16-byte piece (i mod 16) of row i / 16; rows are ordered
+// (t, owner, slot, s) with s fastest, so a warp reads two 256-byte rows of the
+// shard and writes 512 contiguous bytes of the owner's receive buffer.
+__global__ void __launch_bounds__(kXThreads, kXMinBlocks) dispatch_kernel(const DispatchParams p) {
+  const int U = p.B * p.H;
   const int64_t S = (int64_t)p.P * p.Sr;
-  const int piece = (int)(i % kPieces);
-  int64_t row = i / kPieces;
-  const int h = (int)(row % p.H);
-  row /= p.H;
-  const int s = (int)(row % p.Sr);
-  row /= p.Sr;
-  const int b = (int)(row % p.B);
-  const int t = (int)(row / p.B);
-  from = p.src[t] + ((b * p.st[t][0] + s * p.st[t][1] + h * p.st[t][2]) * 2 + piece * 16);
-  const int u = b * p.H + h;
-  const int owner = u / p.n_per, j = u - owner * p.n_per;
-  to = p.dst[owner] +
-       ((((int64_t)t * p.n_per + j) * S + (int64_t)p.rank * p.Sr + s) * kD * 2 + piece * 16);
-}
-
-// Each thread moves kUnroll pieces per step, loads first, so that several
-// loads are in flight before the (local or NVLink) stores.
-constexpr int kUnroll = 4;
-
-__global__ void __launch_bounds__(256) dispatch_kernel(const DispatchParams p) {
-  const int64_t n = (int64_t)p.T * p.B * p.Sr * p.H * kPieces;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n;
-       i0 += stride * kUnroll) {
-    uint4 v[kUnroll];
-    uint8_t* to[kUnroll];
-#pragma unroll
-    for (int e = 0; e < kUnroll; ++e) {
-      const int64_t i = i0 + e * stride;
-      to[e] = nullptr;
-      if (i < n) {
-        const uint8_t* from;
-        dispatch_piece(p, i, from, to[e]);
-        v[e] = *reinterpret_cast<const uint4*>(from);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < kUnroll; ++e)
-      if (to[e] != nullptr) *reinterpret_cast<uint4*>(to[e]) = v[e];
+  const uint32_t rows = (uint32_t)p.T * p.P * p.nj * p.Sr;
+  const uint32_t n = rows * kPieces;
+  for (uint32_t i = blockIdx.x * kXThreads + threadIdx.x; i < n; i += gridDim.x * kXThreads) {
+    const int piece = (int)(i & (kPieces - 1));
+    uint32_t r = i / kPieces;
+    const int s = (int)(r % (uint32_t)p.Sr);
+    r /= (uint32_t)p.Sr;
+    const int j = p.j0 + (int)(r % (uint32_t)p.nj);
+    r /= (uint32_t)p.nj;
+    const int owner = (int)(r % (uint32_t)p.P);
+    const int t = (int)(r / (uint32_t)p.P);
+    const int u = owner * p.n_per + j;
+    if (u >= U) continue;  // a padding unit
+    const int b = u / p.H, h = u - b * p.H;
+    const uint4 v = *reinterpret_cast<const uint4*>(
+        p.src[t] + ((b * p.st[t][0] + s * p.st[t][1] + h * p.st[t][2]) * 2 + piece * 16));
+    *reinterpret_cast<uint4*>(
+        p.dst[owner] +
+        ((((int64_t)t * p.n_per + j) * S + (int64_t)p.rank * p.Sr + s) * kD * 2 + piece * 16)) = v;
   }
   __threadfence_system();
 }
@@ -91,54 +80,40 @@ struct CombineParams {
   uint8_t* out_dst[kMaxRanks];  // each rank's [B][Sr][H][D] bf16
   float* lse_dst[kMaxRanks];    // each rank's [B][H][Sr] fp32 (nullable as a whole)
   int B, Sr, H, P, rank, n_per;
+  int j0, nj;                   // this rank's unit slots j0 .. j0 + nj - 1
 };
 
-__global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
+// Thread i moves 16-byte piece (i mod 17) of output row i / 17 (piece 16: the
+// row's LSE value); rows are (slot, s) with s fastest.
+__global__ void __launch_bounds__(kXThreads, kXMinBlocks) combine_kernel(const CombineParams p) {
   const int U = p.B * p.H;
-  const int64_t S = (int64_t)p.P * p.Sr;
-  const int64_t n = (int64_t)p.n_per * S * (kPieces + 1);
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n;
-       i0 += stride * kUnroll) {
-    uint4 v[kUnroll];
-    float l[kUnroll];
-    uint8_t* to[kUnroll];
-    float* lto[kUnroll];
-#pragma unroll
-    for (int e = 0; e < kUnroll; ++e) {
-      const int64_t i = i0 + e * stride;
-      to[e] = nullptr;
-      lto[e] = nullptr;
-      if (i >= n) continue;
-      const int64_t row = i / (kPieces + 1);
-      const int piece = (int)(i - row * (kPieces + 1));  // kPieces: the LSE value
-      const int j = (int)(row / S);
-      const int64_t s = row - (int64_t)j * S;
-      const int u = p.rank * p.n_per + j;
-      if (u >= U) continue;  // a padding unit
-      const int b = u / p.H, h = u - (u / p.H) * p.H;
-      const int owner = (int)(s / p.Sr);
-      const int64_t sl = s - (int64_t)owner * p.Sr;
-      if (piece < kPieces) {
-        v[e] = *reinterpret_cast<const uint4*>(p.out + (row * kD * 2 + piece * 16));
-        to[e] = p.out_dst[owner] + ((((int64_t)b * p.Sr + sl) * p.H + h) * kD * 2 + piece * 16);
-      } else if (p.lse_dst[0] != nullptr) {
-        l[e] = p.lse[row];
-        lto[e] = p.lse_dst[owner] + ((int64_t)b * p.H + h) * p.Sr + sl;
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < kUnroll; ++e) {
-      if (to[e] != nullptr) *reinterpret_cast<uint4*>(to[e]) = v[e];
-      if (lto[e] != nullptr) *lto[e] = l[e];
+  const uint32_t S = (uint32_t)p.P * p.Sr;
+  const uint32_t n = (uint32_t)p.nj * S * (kPieces + 1);
+  for (uint32_t i = blockIdx.x * kXThreads + threadIdx.x; i < n; i += gridDim.x * kXThreads) {
+    const uint32_t rr = i / (kPieces + 1);
+    const int piece = (int)(i - rr * (kPieces + 1));
+    const int j = p.j0 + (int)(rr / S);
+    const uint32_t s = rr % S;
+    const int u = p.rank * p.n_per + j;
+    if (u >= U) continue;  // a padding unit
+    const int b = u / p.H, h = u - b * p.H;
+    const int owner = (int)(s / (uint32_t)p.Sr);
+    const int sl = (int)(s - (uint32_t)owner * p.Sr);
+    const int64_t row = (int64_t)j * S + s;
+    if (piece < kPieces) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p.out + (row * kD * 2 + piece * 16));
+      *reinterpret_cast<uint4*>(p.out_dst[owner] +
+                                ((((int64_t)b * p.Sr + sl) * p.H + h) * kD * 2 + piece * 16)) = v;
+    } else if (p.lse_dst[0] != nullptr) {
+      p.lse_dst[owner][((int64_t)b * p.H + h) * p.Sr + sl] = p.lse[row];
     }
   }
   __threadfence_system();
 }
 
 int grid_for(int64_t work) {
-  const int64_t want = (work + 256 * kUnroll - 1) / (256 * kUnroll);
-  const int64_t cap = (int64_t)sm_count_current_device() * 8;
+  const int64_t want = (work + kXThreads - 1) / kXThreads;
+  const int64_t cap = (int64_t)sm_count_current_device() * kXMinBlocks;
   return (int)(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
@@ -186,9 +161,10 @@ extern "C" int sa_ipc_close(void* ptr) {
   return SA_OK;
 }
 
-extern "C" int sa_ulysses_dispatch(int T, const void* const* src, const int64_t* src_strides,
-                                   int B, int Sr, int H, int D, int P, int rank, int n_per,
-                                   void* const* dst, cudaStream_t stream) {
+extern "C" int sa_ulysses_dispatch_units(int T, const void* const* src,
+                                         const int64_t* src_strides, int B, int Sr, int H, int D,
+                                         int P, int rank, int n_per, int j0, int j1,
+                                         void* const* dst, cudaStream_t stream) {
   SA_CHECK_ARG(src != nullptr && src_strides != nullptr && dst != nullptr,
                "sa_ulysses_dispatch: null pointer argument");
   SA_CHECK_ARG(T >= 1 && T <= kMaxTensors, "sa_ulysses_dispatch: 1 to %d tensors, got %d",
@@ -200,6 +176,11 @@ extern "C" int sa_ulysses_dispatch(int T, const void* const* src, const int64_t*
   SA_CHECK_ARG(B >= 1 && Sr >= 1 && H >= 1, "sa_ulysses_dispatch: empty shard");
   SA_CHECK_ARG(n_per >= 1 && (int64_t)n_per * P >= (int64_t)B * H,
                "sa_ulysses_dispatch: %d units per rank cannot hold %d units", n_per, B * H);
+  SA_CHECK_ARG(0 <= j0 && j0 < j1 && j1 <= n_per,
+               "sa_ulysses_dispatch: unit slots [%d, %d) not a non-empty range of 0..%d", j0, j1,
+               n_per);
+  SA_CHECK_ARG((int64_t)T * P * (j1 - j0) * Sr * sa::xchg::kPieces < ((int64_t)1 << 32),
+               "sa_ulysses_dispatch: too many rows in one call");
   sa::xchg::DispatchParams p = {};
   for (int t = 0; t < T; ++t) {
     SA_CHECK_ARG(src[t] != nullptr && ((uintptr_t)src[t] % 16) == 0,
@@ -225,16 +206,25 @@ extern "C" int sa_ulysses_dispatch(int T, const void* const* src, const int64_t*
   p.P = P;
   p.rank = rank;
   p.n_per = n_per;
-  const int64_t work = (int64_t)T * B * Sr * H * sa::xchg::kPieces;
-  sa::xchg::dispatch_kernel<<<sa::xchg::grid_for(work), 256, 0, stream>>>(p);
+  p.j0 = j0;
+  p.nj = j1 - j0;
+  const int64_t work = (int64_t)T * P * p.nj * Sr * sa::xchg::kPieces;
+  sa::xchg::dispatch_kernel<<<sa::xchg::grid_for(work), sa::xchg::kXThreads, 0, stream>>>(p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
 
-extern "C" int sa_ulysses_combine(const void* out_units, const float* lse_units, int B, int Sr,
-                                  int H, int D, int P, int rank, int n_per,
-                                  void* const* out_dst, float* const* lse_dst,
-                                  cudaStream_t stream) {
+extern "C" int sa_ulysses_dispatch(int T, const void* const* src, const int64_t* src_strides,
+                                   int B, int Sr, int H, int D, int P, int rank, int n_per,
+                                   void* const* dst, cudaStream_t stream) {
+  return sa_ulysses_dispatch_units(T, src, src_strides, B, Sr, H, D, P, rank, n_per, 0,
+                                   n_per > 0 ? n_per : 1, dst, stream);
+}
+
+extern "C" int sa_ulysses_combine_units(const void* out_units, const float* lse_units, int B,
+                                        int Sr, int H, int D, int P, int rank, int n_per, int j0,
+                                        int j1, void* const* out_dst, float* const* lse_dst,
+                                        cudaStream_t stream) {
   SA_CHECK_ARG(out_units != nullptr && out_dst != nullptr,
                "sa_ulysses_combine: null pointer argument");
   SA_CHECK_ARG((lse_units == nullptr) == (lse_dst == nullptr),
@@ -246,6 +236,11 @@ extern "C" int sa_ulysses_combine(const void* out_units, const float* lse_units,
   SA_CHECK_ARG(B >= 1 && Sr >= 1 && H >= 1, "sa_ulysses_combine: empty shard");
   SA_CHECK_ARG(n_per >= 1 && (int64_t)n_per * P >= (int64_t)B * H,
                "sa_ulysses_combine: %d units per rank cannot hold %d units", n_per, B * H);
+  SA_CHECK_ARG(0 <= j0 && j0 < j1 && j1 <= n_per,
+               "sa_ulysses_combine: unit slots [%d, %d) not a non-empty range of 0..%d", j0, j1,
+               n_per);
+  SA_CHECK_ARG((int64_t)(j1 - j0) * P * Sr * (sa::xchg::kPieces + 1) < ((int64_t)1 << 32),
+               "sa_ulysses_combine: too many rows in one call");
   SA_CHECK_ARG(((uintptr_t)out_units % 16) == 0, "sa_ulysses_combine: out_units not 16-byte aligned");
   sa::xchg::CombineParams p = {};
   p.out = reinterpret_cast<const uint8_t*>(out_units);
@@ -265,8 +260,18 @@ extern "C" int sa_ulysses_combine(const void* out_units, const float* lse_units,
   p.P = P;
   p.rank = rank;
   p.n_per = n_per;
-  const int64_t work = (int64_t)n_per * P * Sr * (sa::xchg::kPieces + 1);
-  sa::xchg::combine_kernel<<<sa::xchg::grid_for(work), 256, 0, stream>>>(p);
+  p.j0 = j0;
+  p.nj = j1 - j0;
+  const int64_t work = (int64_t)p.nj * P * Sr * (sa::xchg::kPieces + 1);
+  sa::xchg::combine_kernel<<<sa::xchg::grid_for(work), sa::xchg::kXThreads, 0, stream>>>(p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
+}
+
+extern "C" int sa_ulysses_combine(const void* out_units, const float* lse_units, int B, int Sr,
+                                  int H, int D, int P, int rank, int n_per,
+                                  void* const* out_dst, float* const* lse_dst,
+                                  cudaStream_t stream) {
+  return sa_ulysses_combine_units(out_units, lse_units, B, Sr, H, D, P, rank, n_per, 0,
+                                  n_per > 0 ? n_per : 1, out_dst, lse_dst, stream);
 }

@@ -120,11 +120,6 @@ __device__ __forceinline__ void report_timeout(int32_t* status) {
   __threadfence_system();
 }
 
-// Whether a kernel reported a failure (read at kernel entry only: it may be a
-// read of host memory).
-__device__ __forceinline__ bool status_set(const int32_t* status) {
-  return status != nullptr && *reinterpret_cast<const volatile int32_t*>(status) != 0;
-}
 
 // Bounded wait for the phase with the given parity to complete. Gives up
 // (returns false) after limit_ns, recording SA_DEV_WAIT_TIMEOUT in *status and

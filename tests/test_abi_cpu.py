@@ -352,6 +352,13 @@ def test_ulysses_exchange_validation(lib):
         _lib.SA_EINVAL and "together" in _lib.last_error()
     assert lib.sa_ulysses_combine(256, None, 2, 4, 3, 128, 2, 5, 3, dst, None, None) == \
         _lib.SA_EINVAL
+    for j0, j1 in ((2, 2), (0, 4), (-1, 1), (3, 2)):
+        assert lib.sa_ulysses_dispatch_units(3, src, st, 2, 4, 3, 128, 2, 0, 3, j0, j1, dst,
+                                             None) == _lib.SA_EINVAL
+        assert "slots" in _lib.last_error()
+        assert lib.sa_ulysses_combine_units(256, None, 2, 4, 3, 128, 2, 0, 3, j0, j1, dst, None,
+                                            None) == _lib.SA_EINVAL
+        assert "slots" in _lib.last_error()
     ptr = ctypes.c_void_p()
     assert lib.sa_ipc_alloc(0, ctypes.byref(ptr)) == _lib.SA_EINVAL
     assert lib.sa_ipc_get_handle(None, None) == _lib.SA_EINVAL

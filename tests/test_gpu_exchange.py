@@ -78,3 +78,53 @@ def test_dispatch_and_combine_layouts(B, H, P, Sr):
         for p in range(P):
             assert torch.equal(out_dst[p][b, :, h], outs[r][j, p * Sr:(p + 1) * Sr]), (u, p)
             assert torch.equal(lse_dst[p][b, h], lses[r][j, p * Sr:(p + 1) * Sr]), (u, p)
+
+
+@pytest.mark.parametrize("B,H,P,Sr,groups", [(2, 3, 3, 64, 2), (2, 12, 2, 48, 3),
+                                             (1, 5, 2, 100, 2)])
+def test_unit_groups_cover_the_whole_exchange(B, H, P, Sr, groups):
+    """Dispatch and combine run group by group over the unit slots (the
+    pipelined exchange) write exactly what the whole-range calls write."""
+    from sinkattn_b200 import _lib
+
+    lib = _lib.load()
+    D = 128
+    n_per = -(-(B * H) // P)
+    S = P * Sr
+    edges = [n_per * c // groups for c in range(groups + 1)]
+    g = torch.Generator(device="cuda").manual_seed(7 * B + H + P)
+    shards = [tuple(torch.randn(B, Sr, H, D, device="cuda", generator=g).bfloat16()
+                    for _ in range(3)) for _ in range(P)]
+
+    def run(ranges):
+        recv = [torch.zeros(3, n_per, S, D, dtype=torch.bfloat16, device="cuda")
+                for _ in range(P)]
+        dst = (ctypes.c_void_p * P)(*[r.data_ptr() for r in recv])
+        for p, (q, k, v) in enumerate(shards):
+            src = (ctypes.c_void_p * 3)(q.data_ptr(), k.data_ptr(), v.data_ptr())
+            st = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride())
+            for j0, j1 in ranges:
+                _lib.check(lib.sa_ulysses_dispatch_units(3, src, st, B, Sr, H, D, P, p, n_per,
+                                                         j0, j1, dst, _stream()),
+                           "sa_ulysses_dispatch_units")
+        out_dst = [torch.zeros(B, Sr, H, D, dtype=torch.bfloat16, device="cuda")
+                   for _ in range(P)]
+        lse_dst = [torch.zeros(B, H, Sr, device="cuda") for _ in range(P)]
+        od = (ctypes.c_void_p * P)(*[o.data_ptr() for o in out_dst])
+        ld = (ctypes.c_void_p * P)(*[o.data_ptr() for o in lse_dst])
+        for r in range(P):
+            out = recv[r][0].contiguous()  # any [n_per, S, D] data will do
+            lse = recv[r][1, :, :, 0].float().contiguous()
+            for j0, j1 in ranges:
+                _lib.check(lib.sa_ulysses_combine_units(out.data_ptr(), lse.data_ptr(), B, Sr, H,
+                                                        D, P, r, n_per, j0, j1, od, ld,
+                                                        _stream()),
+                           "sa_ulysses_combine_units")
+        torch.cuda.synchronize()
+        return recv, out_dst, lse_dst
+
+    whole = run([(0, n_per)])
+    parts = run([(edges[c], edges[c + 1]) for c in range(groups)])
+    for a, b in zip(whole, parts):
+        for x, y in zip(a, b):
+            assert torch.equal(x, y)
