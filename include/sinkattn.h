@@ -435,7 +435,8 @@ SA_API int sa_mix_outputs(const void* o_s, const int64_t os_strides[4], const fl
  * sa_ulysses_combine: this rank's units' attention output [n_per][P*Sr][128]
  *   bf16 (contiguous) and LSE [n_per][P*Sr] fp32 (nullable) are written into
  *   out_dst[p] ([B][Sr][H][128] bf16) and lse_dst[p] ([B][H][Sr] fp32) of the
- *   rank p owning each row's stretch of the sequence.
+ *   rank p owning each row's stretch of the sequence. All of them 16-byte
+ *   aligned.
  * sa_ulysses_dispatch_units / sa_ulysses_combine_units: the same for the unit
  *   slots j0 <= j < j1 of every owner only (slot j of rank r is unit
  *   r*n_per + j), so that the exchange of one group of slots can run while

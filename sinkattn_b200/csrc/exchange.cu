@@ -29,7 +29,34 @@ namespace xchg {
 constexpr int kD = 128;
 constexpr int kMaxRanks = 8;
 constexpr int kMaxTensors = 3;
-constexpr int kPieces = kD * 2 / 16;  // 16-byte pieces of one bf16 row
+constexpr int kRowBytes = kD * 2;     // one bf16 row
+constexpr int kPieces = kRowBytes / 16;  // 16-byte pieces of one row
+
+// One piece of a row: 32 bytes moved with one 256-bit load and store where
+// every address allows it (half the stores, over NVLink included), else 16.
+template <int kBytes>
+struct Piece;
+template <>
+struct Piece<16> {
+  uint4 v;
+  __device__ __forceinline__ void load(const uint8_t* a) { v = *reinterpret_cast<const uint4*>(a); }
+  __device__ __forceinline__ void store(uint8_t* a) const { *reinterpret_cast<uint4*>(a) = v; }
+};
+template <>
+struct Piece<32> {
+  uint32_t r[8];
+  __device__ __forceinline__ void load(const uint8_t* a) {
+    asm volatile("ld.global.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "l"(a));
+  }
+  __device__ __forceinline__ void store(uint8_t* a) const {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(a), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+  }
+};
 
 struct DispatchParams {
   const uint8_t* src[kMaxTensors];
@@ -45,31 +72,34 @@ struct DispatchParams {
 constexpr int kXThreads = 128;
 constexpr int kXMinBlocks = 16;
 
-// Thread i moves 16-byte piece (i mod 16) of row i / 16; rows are ordered
-// (t, owner, slot, s) with s fastest, so a warp reads two 256-byte rows of the
-// shard and writes 512 contiguous bytes of the owner's receive buffer.
+// Thread i moves piece (i mod n) of row i / n, n = 256 / kBytes; rows are
+// ordered (t, slot, s, owner) with the owner fastest, so that every stretch
+// of the grid-stride loop stores to every owner (NVLink and local HBM at
+// once), and each warp moves whole 256-byte rows.
+template <int kBytes>
 __global__ void __launch_bounds__(kXThreads, kXMinBlocks) dispatch_kernel(const DispatchParams p) {
+  constexpr int kN = kRowBytes / kBytes;
   const int U = p.B * p.H;
   const int64_t S = (int64_t)p.P * p.Sr;
   const uint32_t rows = (uint32_t)p.T * p.P * p.nj * p.Sr;
-  const uint32_t n = rows * kPieces;
+  const uint32_t n = rows * kN;
   for (uint32_t i = blockIdx.x * kXThreads + threadIdx.x; i < n; i += gridDim.x * kXThreads) {
-    const int piece = (int)(i & (kPieces - 1));
-    uint32_t r = i / kPieces;
+    const int piece = (int)(i & (kN - 1));
+    uint32_t r = i / kN;
+    const int owner = (int)(r % (uint32_t)p.P);
+    r /= (uint32_t)p.P;
     const int s = (int)(r % (uint32_t)p.Sr);
     r /= (uint32_t)p.Sr;
     const int j = p.j0 + (int)(r % (uint32_t)p.nj);
-    r /= (uint32_t)p.nj;
-    const int owner = (int)(r % (uint32_t)p.P);
-    const int t = (int)(r / (uint32_t)p.P);
+    const int t = (int)(r / (uint32_t)p.nj);
     const int u = owner * p.n_per + j;
     if (u >= U) continue;  // a padding unit
     const int b = u / p.H, h = u - b * p.H;
-    const uint4 v = *reinterpret_cast<const uint4*>(
-        p.src[t] + ((b * p.st[t][0] + s * p.st[t][1] + h * p.st[t][2]) * 2 + piece * 16));
-    *reinterpret_cast<uint4*>(
-        p.dst[owner] +
-        ((((int64_t)t * p.n_per + j) * S + (int64_t)p.rank * p.Sr + s) * kD * 2 + piece * 16)) = v;
+    Piece<kBytes> v;
+    v.load(p.src[t] + ((b * p.st[t][0] + s * p.st[t][1] + h * p.st[t][2]) * 2 + piece * kBytes));
+    v.store(p.dst[owner] + ((((int64_t)t * p.n_per + j) * S + (int64_t)p.rank * p.Sr + s) *
+                                kRowBytes +
+                            piece * kBytes));
   }
   __threadfence_system();
 }
@@ -81,31 +111,47 @@ struct CombineParams {
   float* lse_dst[kMaxRanks];    // each rank's [B][H][Sr] fp32 (nullable as a whole)
   int B, Sr, H, P, rank, n_per;
   int j0, nj;                   // this rank's unit slots j0 .. j0 + nj - 1
+  int lse_w;                    // LSE values per store: 4 (16 bytes) when Sr % 4 == 0, else 1
 };
 
-// Thread i moves 16-byte piece (i mod 17) of output row i / 17 (piece 16: the
-// row's LSE value); rows are (slot, s) with s fastest.
+// Threads i < n_out move 16-byte piece (i mod 16) of output row i / 16; rows
+// are (slot, s mod Sr, s div Sr) with the receiving rank s div Sr fastest, so
+// that every stretch of the loop stores to every rank. The threads after them
+// move the LSE, lse_w consecutive rows of one rank per store (a 4-byte store
+// per row would be one NVLink write of 4 bytes).
+template <int kBytes>
 __global__ void __launch_bounds__(kXThreads, kXMinBlocks) combine_kernel(const CombineParams p) {
+  constexpr int kN = kRowBytes / kBytes;
   const int U = p.B * p.H;
   const uint32_t S = (uint32_t)p.P * p.Sr;
-  const uint32_t n = (uint32_t)p.nj * S * (kPieces + 1);
-  for (uint32_t i = blockIdx.x * kXThreads + threadIdx.x; i < n; i += gridDim.x * kXThreads) {
-    const uint32_t rr = i / (kPieces + 1);
-    const int piece = (int)(i - rr * (kPieces + 1));
-    const int j = p.j0 + (int)(rr / S);
-    const uint32_t s = rr % S;
+  const uint32_t n_out = (uint32_t)p.nj * S * kN;
+  const uint32_t n_lse = p.lse_dst[0] != nullptr ? (uint32_t)p.nj * S / (uint32_t)p.lse_w : 0u;
+  for (uint32_t i = blockIdx.x * kXThreads + threadIdx.x; i < n_out + n_lse;
+       i += gridDim.x * kXThreads) {
+    const bool is_out = i < n_out;
+    const uint32_t w = is_out ? 1u : (uint32_t)p.lse_w;
+    uint32_t rr = is_out ? i / kN : (i - n_out);  // output row, or LSE group
+    const int piece = is_out ? (int)(i & (kN - 1)) : 0;
+    const int owner = (int)(rr % (uint32_t)p.P);
+    rr /= (uint32_t)p.P;
+    const uint32_t per_owner = (uint32_t)p.Sr / w;  // rows (or LSE groups) per rank
+    const int sl = (int)((rr % per_owner) * w);
+    const int j = p.j0 + (int)(rr / per_owner);
     const int u = p.rank * p.n_per + j;
     if (u >= U) continue;  // a padding unit
     const int b = u / p.H, h = u - b * p.H;
-    const int owner = (int)(s / (uint32_t)p.Sr);
-    const int sl = (int)(s - (uint32_t)owner * p.Sr);
-    const int64_t row = (int64_t)j * S + s;
-    if (piece < kPieces) {
-      const uint4 v = *reinterpret_cast<const uint4*>(p.out + (row * kD * 2 + piece * 16));
-      *reinterpret_cast<uint4*>(p.out_dst[owner] +
-                                ((((int64_t)b * p.Sr + sl) * p.H + h) * kD * 2 + piece * 16)) = v;
-    } else if (p.lse_dst[0] != nullptr) {
-      p.lse_dst[owner][((int64_t)b * p.H + h) * p.Sr + sl] = p.lse[row];
+    const int64_t row = (int64_t)j * S + (int64_t)owner * p.Sr + sl;
+    if (is_out) {
+      Piece<kBytes> v;
+      v.load(p.out + (row * kRowBytes + piece * kBytes));
+      v.store(p.out_dst[owner] +
+              ((((int64_t)b * p.Sr + sl) * p.H + h) * kRowBytes + piece * kBytes));
+    } else {
+      float* to = p.lse_dst[owner] + ((int64_t)b * p.H + h) * p.Sr + sl;
+      if (w == 4u)
+        *reinterpret_cast<float4*>(to) = *reinterpret_cast<const float4*>(p.lse + row);
+      else
+        *to = p.lse[row];
     }
   }
   __threadfence_system();
@@ -208,8 +254,18 @@ extern "C" int sa_ulysses_dispatch_units(int T, const void* const* src,
   p.n_per = n_per;
   p.j0 = j0;
   p.nj = j1 - j0;
-  const int64_t work = (int64_t)T * P * p.nj * Sr * sa::xchg::kPieces;
-  sa::xchg::dispatch_kernel<<<sa::xchg::grid_for(work), sa::xchg::kXThreads, 0, stream>>>(p);
+  bool wide = true;  // every row and destination 32-byte aligned
+  for (int t = 0; t < T; ++t)
+    wide = wide && ((uintptr_t)src[t] % 32) == 0 && p.st[t][0] % 16 == 0 &&
+           p.st[t][1] % 16 == 0 && p.st[t][2] % 16 == 0;
+  for (int r = 0; r < P; ++r) wide = wide && ((uintptr_t)dst[r] % 32) == 0;
+  const int64_t rows = (int64_t)T * P * p.nj * Sr;
+  if (wide)
+    sa::xchg::dispatch_kernel<32><<<sa::xchg::grid_for(rows * (sa::xchg::kRowBytes / 32)),
+                                    sa::xchg::kXThreads, 0, stream>>>(p);
+  else
+    sa::xchg::dispatch_kernel<16><<<sa::xchg::grid_for(rows * (sa::xchg::kRowBytes / 16)),
+                                    sa::xchg::kXThreads, 0, stream>>>(p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
@@ -241,6 +297,8 @@ extern "C" int sa_ulysses_combine_units(const void* out_units, const float* lse_
                n_per);
   SA_CHECK_ARG((int64_t)(j1 - j0) * P * Sr * (sa::xchg::kPieces + 1) < ((int64_t)1 << 32),
                "sa_ulysses_combine: too many rows in one call");
+  SA_CHECK_ARG(((uintptr_t)lse_units % 16) == 0,
+               "sa_ulysses_combine: lse_units not 16-byte aligned");
   SA_CHECK_ARG(((uintptr_t)out_units % 16) == 0, "sa_ulysses_combine: out_units not 16-byte aligned");
   sa::xchg::CombineParams p = {};
   p.out = reinterpret_cast<const uint8_t*>(out_units);
@@ -250,7 +308,8 @@ extern "C" int sa_ulysses_combine_units(const void* out_units, const float* lse_
                  "sa_ulysses_combine: output of rank %d null or not 16-byte aligned", r);
     p.out_dst[r] = reinterpret_cast<uint8_t*>(out_dst[r]);
     if (lse_dst != nullptr) {
-      SA_CHECK_ARG(lse_dst[r] != nullptr, "sa_ulysses_combine: LSE of rank %d null", r);
+      SA_CHECK_ARG(lse_dst[r] != nullptr && ((uintptr_t)lse_dst[r] % 16) == 0,
+                   "sa_ulysses_combine: LSE of rank %d null or not 16-byte aligned", r);
       p.lse_dst[r] = lse_dst[r];
     }
   }
@@ -262,8 +321,19 @@ extern "C" int sa_ulysses_combine_units(const void* out_units, const float* lse_
   p.n_per = n_per;
   p.j0 = j0;
   p.nj = j1 - j0;
-  const int64_t work = (int64_t)p.nj * P * Sr * (sa::xchg::kPieces + 1);
-  sa::xchg::combine_kernel<<<sa::xchg::grid_for(work), sa::xchg::kXThreads, 0, stream>>>(p);
+  p.lse_w = Sr % 4 == 0 ? 4 : 1;
+  bool wide = ((uintptr_t)out_units % 32) == 0;
+  for (int r = 0; r < P; ++r) wide = wide && ((uintptr_t)out_dst[r] % 32) == 0;
+  const int64_t rows = (int64_t)p.nj * P * Sr;
+  const int64_t lse_work = lse_dst != nullptr ? rows / p.lse_w : 0;
+  if (wide)
+    sa::xchg::combine_kernel<32><<<sa::xchg::grid_for(rows * (sa::xchg::kRowBytes / 32) +
+                                                      lse_work),
+                                   sa::xchg::kXThreads, 0, stream>>>(p);
+  else
+    sa::xchg::combine_kernel<16><<<sa::xchg::grid_for(rows * (sa::xchg::kRowBytes / 16) +
+                                                      lse_work),
+                                   sa::xchg::kXThreads, 0, stream>>>(p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }

@@ -26,7 +26,11 @@ def _stream():
 
 
 @pytest.mark.parametrize("B,H,P,Sr", [(2, 3, 3, 64), (1, 5, 2, 100), (2, 12, 8, 32)])
-def test_dispatch_and_combine_layouts(B, H, P, Sr):
+@pytest.mark.parametrize("narrow", [False, True])
+def test_dispatch_and_combine_layouts(B, H, P, Sr, narrow):
+    """narrow: V rows 272 bytes apart and the unit outputs 16 bytes off a
+    32-byte boundary, so that the kernels take their 16-byte path; otherwise
+    every address allows 32-byte pieces."""
     from sinkattn_b200 import _lib
 
     lib = _lib.load()
@@ -40,7 +44,8 @@ def test_dispatch_and_combine_layouts(B, H, P, Sr):
     for p in range(P):
         q = torch.randn(B, Sr, H, D, device="cuda", generator=g).bfloat16()
         k = torch.randn(B, Sr, H + 1, D, device="cuda", generator=g).bfloat16()[:, :, :H]
-        v = torch.randn(B, Sr, H, D, device="cuda", generator=g).bfloat16()
+        pad = 8 if narrow else 0
+        v = torch.randn(B, Sr, H, D + pad, device="cuda", generator=g).bfloat16()[..., :D]
         shards.append((q, k, v))
     recv = [torch.zeros(3, n_per, S, D, dtype=torch.bfloat16, device="cuda") for _ in range(P)]
     dst = (ctypes.c_void_p * P)(*[r.data_ptr() for r in recv])
@@ -62,7 +67,9 @@ def test_dispatch_and_combine_layouts(B, H, P, Sr):
             if r * n_per + j >= U:
                 assert not recv[r][:, j].any()
 
-    outs = [torch.randn(n_per, S, D, device="cuda", generator=g).bfloat16() for _ in range(P)]
+    off = 8 if narrow else 0  # bf16 elements: 16 bytes
+    outs = [torch.randn(n_per * S * D + off, device="cuda", generator=g).bfloat16()[off:]
+            .view(n_per, S, D) for _ in range(P)]
     lses = [torch.randn(n_per, S, device="cuda", generator=g) for _ in range(P)]
     out_dst = [torch.zeros(B, Sr, H, D, dtype=torch.bfloat16, device="cuda") for _ in range(P)]
     lse_dst = [torch.zeros(B, H, Sr, device="cuda") for _ in range(P)]

@@ -58,12 +58,15 @@ def _worker(rank, world, port, result_dir):
         # kernels into CUDA-IPC-mapped buffers), twice on the same buffers
         from sinkattn_b200.sharding import UlyssesPeerExchange
 
-        ex = UlyssesPeerExchange(B, S, H, device=dev)
-        for _ in range(2):
-            out_p, lse_p = ex(qs, ks, vs, mask.to(dev))
-            torch.cuda.synchronize()
-            assert torch.equal(out_p, out) and torch.equal(lse_p, lse)
-        ex.close()
+        # one unit group, then two and three groups (each group's exchange
+        # overlapped with another group's attention on a second stream)
+        for chunks in (1, 2, 3):
+            ex = UlyssesPeerExchange(B, S, H, device=dev, chunks=chunks)
+            for _ in range(2):
+                out_p, lse_p = ex(qs, ks, vs, mask.to(dev))
+                torch.cuda.synchronize()
+                assert torch.equal(out_p, out) and torch.equal(lse_p, lse), chunks
+            ex.close()
         torch.save({"out": out.cpu(), "lse": lse.cpu()}, os.path.join(result_dir, f"r{rank}.pt"))
         dist.barrier()
     finally:
