@@ -167,13 +167,17 @@ def test_accumulate_finalize(oracle):
     np.testing.assert_allclose(std.cpu().numpy(), rstd, rtol=1e-4, atol=1e-6)
 
 
-@pytest.mark.parametrize("S,pool,prefix", [(32760, 30, 0), (1000, 30, 0), (1000, 30, 77),
-                                           (500, 7, 600), (1000, 40, 3), (4100, 128, 0)])
-def test_mean_pool_seq(oracle, S, pool, prefix):
+@pytest.mark.parametrize("S,pool,prefix,H", [(32760, 30, 0, 3), (1000, 30, 0, 3), (1000, 30, 77, 3),
+                                             (500, 7, 600, 3), (1000, 40, 3, 3), (4100, 128, 0, 3),
+                                             (1000, 200, 5, 3), (31, 30, 0, 3), (64, 30, 40, 3),
+                                             (2000, 30, 0, 30), (1000, 64, 10, 13)])
+def test_mean_pool_seq(oracle, S, pool, prefix, H):
+    """Gap pooling with a kept prefix; head counts that split into uneven
+    groups of heads per load (30 = 12 + 12 + 6, 13 at pool 64 = 6 + 6 + 1)."""
     from sinkattn_b200 import ops
 
     g = torch.Generator().manual_seed(S + pool)
-    x = torch.randn(2, S, 3, 128, generator=g).bfloat16().cuda().permute(0, 2, 1, 3)
+    x = torch.randn(2, S, H, 128, generator=g).bfloat16().cuda().permute(0, 2, 1, 3)
     out = ops.mean_pool_seq(x, pool, prefix)
     torch.cuda.synchronize()
     ref = oracle.bf16_round(oracle.mean_pool_sequence_preserve_prefix(
