@@ -155,10 +155,10 @@ __global__ void mean_pool_seq_kernel(const __nv_bfloat16* __restrict__ x, int64_
 // warp loads the next box while consumer warp w sums head w's pool rows of
 // the current one (lane l: columns 4l .. 4l+3) and writes the pooled row.
 // At the Wan shape (gap 30, 12 heads: 92 KB boxes) 38 us against 44 us for
-// mean_pool_seq_kernel; boxes of 6, 4 or 3 heads measured 39, 44 and 56 us. The prefix rows are copied first
-// with plain 16-byte loads. A pooled row that runs past the end adds the
-// final token for each missing row, as line 111's padding does; heads past H
-// in the last head group are skipped.
+// mean_pool_seq_kernel; boxes of 6, 4 or 3 heads measured 39, 44 and 56 us.
+// The prefix rows are copied first with plain 16-byte loads. A pooled row that
+// runs past the end adds the final token for each missing row, as line 111's
+// padding does; heads past H in the last head group are skipped.
 constexpr int kMpStages = 2;
 constexpr int kMpStageBytes = 96 * 1024;
 constexpr int kMpMaxHeads = 12;  // consumer warps
