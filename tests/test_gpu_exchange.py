@@ -9,6 +9,8 @@ every index the kernels compute against the layout written out with torch:
             [t, u % n_per, p*Sr + s];
   combine:  owner r's unit row (j, s) -> rank s // Sr, at [b, s % Sr, h]
             (output) and [b, h, s % Sr] (LSE); padding units are skipped.
+Shard lengths that are not a multiple of 4 (63, 21) take the combine's
+one-value-per-store LSE path; the others move the LSE four rows per store.
 The exchange across real GPUs is in test_gpu_multi.py.
 """
 from __future__ import annotations
@@ -25,7 +27,8 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-@pytest.mark.parametrize("B,H,P,Sr", [(2, 3, 3, 64), (1, 5, 2, 100), (2, 12, 8, 32)])
+@pytest.mark.parametrize("B,H,P,Sr", [(2, 3, 3, 64), (1, 5, 2, 100), (2, 12, 8, 32),
+                                      (2, 12, 8, 63)])
 @pytest.mark.parametrize("narrow", [False, True])
 def test_dispatch_and_combine_layouts(B, H, P, Sr, narrow):
     """narrow: V rows 272 bytes apart and the unit outputs 16 bytes off a
@@ -88,7 +91,7 @@ def test_dispatch_and_combine_layouts(B, H, P, Sr, narrow):
 
 
 @pytest.mark.parametrize("B,H,P,Sr,groups", [(2, 3, 3, 64, 2), (2, 12, 2, 48, 3),
-                                             (1, 5, 2, 100, 2)])
+                                             (1, 5, 2, 100, 2), (2, 3, 3, 21, 2)])
 def test_unit_groups_cover_the_whole_exchange(B, H, P, Sr, groups):
     """Dispatch and combine run group by group over the unit slots (the
     pipelined exchange) write exactly what the whole-range calls write."""
