@@ -98,6 +98,19 @@ __device__ __forceinline__ void stats_bar_sync(int group) {
   asm volatile("bar.sync %0, 128;" ::"r"(group + 1) : "memory");
 }
 
+// Epilogue: the scratch values of kEpi consecutive blocks of one row, loaded
+// before any of them is used (blocks past nk repeat the last one).
+constexpr int kEpi = 8;
+__device__ __forceinline__ void epi_load(const float* c, const float* r, int nk, int j0, int row,
+                                         float (&cv)[kEpi], float (&rv)[kEpi]) {
+#pragma unroll
+  for (int u = 0; u < kEpi; ++u) {
+    const int64_t e = (int64_t)min(j0 + u, nk - 1) * kBM + row;
+    cv[u] = c[e];
+    rv[u] = r != nullptr ? r[e] : 0.f;
+  }
+}
+
 // Work item t: query tiles 2 qp and 2 qp + 1 (if it exists) of head (b, h).
 __device__ __forceinline__ void pair_coords(const Params& p, int t, int& qp, int& h, int& b,
                                             int& ntp) {
@@ -344,19 +357,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the masses under the row maximum m, and the row total l from them in
         // block order; then the sum over the tile's rows of mass / max(l, 1e-6)
         // (sparse_attention.py:224), divided by the number of valid rows (the
-        // mean of line 225)
-        for (int j = 0; j < p.nk; ++j) {
-          const int64_t e = (int64_t)j * kBM + row;
-          const float w = row_valid ? slot[e] * ex2_approx(slot_r[e] - m) : 0.f;
-          slot[e] = w;
-          l += w;
+        // mean of line 225). The masses are recomputed in the second pass
+        // rather than stored back, and each pass loads kEpi blocks' values
+        // before using any: a store into the scratch inside the loop kept every
+        // iteration's loads from being issued before the previous store, and
+        // the epilogue ran at one L2 round trip per block (~25% of the kernel).
+        for (int j0 = 0; j0 < p.nk; j0 += kEpi) {
+          float cv[kEpi], rv[kEpi];
+          epi_load(slot, slot_r, p.nk, j0, row, cv, rv);
+#pragma unroll
+          for (int u = 0; u < kEpi; ++u)
+            if (j0 + u < p.nk) l += row_valid ? cv[u] * ex2_approx(rv[u] - m) : 0.f;
         }
         const float lc = fmaxf(l, 1e-6f);
-        for (int j = 0; j < p.nk; ++j) {
-          float v = row_valid ? __fdiv_rn(slot[(int64_t)j * kBM + row], lc) : 0.f;
+        for (int j0 = 0; j0 < p.nk; j0 += kEpi) {
+          float cv[kEpi], rv[kEpi];
+          epi_load(slot, slot_r, p.nk, j0, row, cv, rv);
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == 0) red[wq * kMaxNB + j] = v;
+          for (int u = 0; u < kEpi; ++u) {
+            const int j = j0 + u;
+            if (j >= p.nk) break;
+            float v = row_valid ? __fdiv_rn(cv[u] * ex2_approx(rv[u] - m), lc) : 0.f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) red[wq * kMaxNB + j] = v;
+          }
         }
         stats_bar_sync(grp);
         const float inv_rows = 1.0f / (float)rows_valid;
@@ -366,11 +391,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         // Po[qb, kb] = bf16(max over the tile's rows of exp2(R - m_r)); l_i = 1
         // in the Triton kernel, so there is no division (pooling_kernel.py:65-75).
-        for (int j = 0; j < p.nk; ++j) {
-          float x = row_valid ? ex2_approx(slot[(int64_t)j * kBM + row] - m) : 0.f;
+        for (int j0 = 0; j0 < p.nk; j0 += kEpi) {
+          float cv[kEpi], rv[kEpi];
+          epi_load(slot, nullptr, p.nk, j0, row, cv, rv);
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-          if (lane == 0) red[wq * kMaxNB + j] = x;
+          for (int u = 0; u < kEpi; ++u) {
+            const int j = j0 + u;
+            if (j >= p.nk) break;
+            float x = row_valid ? ex2_approx(cv[u] - m) : 0.f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+            if (lane == 0) red[wq * kMaxNB + j] = x;
+          }
         }
         stats_bar_sync(grp);
         float part = 0.f;
