@@ -204,7 +204,22 @@ __device__ __forceinline__ void coverage_of_row(const Params& p, int r, float* r
     return;
   }
   const float* bm = (p.bmean != nullptr ? p.bmean : p.bm_scratch) + (int64_t)r * nb;
-  for (int c = lane; c < nb; c += 32) rowbuf[c] = __ldcg(bm + c);
+  // eight loads issued before the first store of their batch (see coverage_row)
+  constexpr int kBatch = NPAD / 32 < 8 ? NPAD / 32 : 8;
+#pragma unroll
+  for (int q0 = 0; q0 < NPAD / 32; q0 += kBatch) {
+    float v[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int c = lane + 32 * (q0 + u);
+      v[u] = c < nb ? __ldcg(bm + c) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int c = lane + 32 * (q0 + u);
+      if (c < nb) rowbuf[c] = v[u];
+    }
+  }
   __syncwarp();
   cov::coverage_row<NPAD>(rowbuf, i, p.spec, nullptr, nullptr, skey,
                           reinterpret_cast<float*>(skey + NPAD), mrow,

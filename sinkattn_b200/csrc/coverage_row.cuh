@@ -93,11 +93,27 @@ __device__ __forceinline__ void coverage_row(const float* s, int row, const RowS
   // (sorted last) and candidate value NaN.
   double tot = 0.0, sel = 0.0;
   int n_cand_local = 0;  // non-required participating columns (candidate_counts, line 348)
-  for (int j = lane; j < NPAD; j += 32) {
+  // The row's values are loaded eight at a time, each eight before the first
+  // shared-memory store of their batch: loads and stores in one loop made
+  // each load wait for the previous iteration's stores (the compiler cannot
+  // tell the row from the scratch).
+  constexpr int kBatch = NPAD / 32 < 8 ? NPAD / 32 : 8;
+  static_assert((NPAD / 32) % kBatch == 0, "row batches");
+#pragma unroll
+  for (int q0 = 0; q0 < NPAD / 32; q0 += kBatch) {
+  float vin[kBatch];
+#pragma unroll
+  for (int u = 0; u < kBatch; ++u) {
+    const int j = lane + 32 * (q0 + u);
+    vin[u] = (j < nk && j >= c_lo) ? s[j] : 0.f;
+  }
+#pragma unroll
+  for (int u = 0; u < kBatch; ++u) {
+    const int j = lane + 32 * (q0 + u);
     uint32_t key = 0xFFFFFFFFu;
     float cv = __int_as_float(0x7fc00000);
     if (j < nk && j >= c_lo) {
-      const float v = s[j];
+      const float v = vin[u];
       const bool req = (j < T) || (p.force_sink && j == 0);
       tot += (double)v;
       if (!video && req) sel += (double)v;
@@ -107,6 +123,7 @@ __device__ __forceinline__ void coverage_row(const float* s, int row, const RowS
     }
     skey[j] = key;
     cval[j] = cv;
+  }
   }
   tot = warp_sum_f64(tot);
   sel = warp_sum_f64(sel);
