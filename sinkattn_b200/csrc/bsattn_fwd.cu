@@ -441,6 +441,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float l = 0.f;
       for (int j = 0; j < n && ok; ++j) {
         const int J = jg + j;
+        // the block's list entry, read before the wait (the list is complete
+        // once list_full has passed; after the wait's memory clobber the
+        // read would sit on the block's path)
+        const uint32_t ent = list[j];
         // warp-uniform outcome: the TMEM loads below are warp-collective
         if (!__all_sync(0xffffffffu,
                         mbar_wait(&ctl->s_full, (uint32_t)J & 1u, p.status, abort_flag))) {
@@ -456,7 +460,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         reg_fence32(r[1]);
         tc_fence_before();
         mbar_arrive(&ctl->s_free);  // S may be overwritten by the next QK
-        const uint32_t ent = list[j];
         const int kb = (int)(ent & 0x7fffu);
         const bool pooled = (ent & 0x8000u) != 0;
         const int valid = min(kHalf, (pooled ? p.Sk2 : p.Sk) - kb * kBN - st * kHalf);
