@@ -92,8 +92,8 @@ SA_API int sa_device_sm_count(void);
  * status: nullable device int32, set to SA_DEV_WAIT_TIMEOUT if a bounded wait
  *   in the kernel gave up.
  * The launch is a persistent grid (one CTA per SM) that takes query tiles from
- *   a tile counter inside the library: 64 counter slots per device, handed to
- *   launches round robin and reset by each launch's last CTA, so up to 64
+ *   a tile counter inside the library: 1024 counter slots per device, handed
+ *   to launches round robin and reset by each launch's last CTA, so up to 1024
  *   launches may be in flight on one device.
  */
 SA_API int sa_bsattn_fwd(const void* q, const void* k, const void* v,

@@ -93,7 +93,7 @@ struct Params {
 // the slot is zero for the next launch that uses it; launches take slots
 // round robin, so concurrent launches on different streams use different
 // slots.
-constexpr int kSchedSlots = 64;
+constexpr int kSchedSlots = 1024;  // 8 KB per device
 __device__ int g_sched[kSchedSlots][2];
 
 struct __align__(8) SmemCtl {
