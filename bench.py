@@ -535,6 +535,12 @@ def run_ours(args):
                      "frac": achieved / peak, "traffic": traffic,
                      "kernel": "sa::attn::bsattn_fwd_kernel",
                      "peak_kind": f"bf16_tflops ({peak_kind}, burst)",
+                     # context: the same against the sustained figure (a GEMM loop held
+                     # at the power cap), the regime the clock record shows when it
+                     # lists sw_power_cap during the timed steps
+                     "frac_of_sustained": achieved / float(
+                         peaks.get("bf16_tflops_sustained",
+                                   FALLBACK_PEAKS["bf16_tflops_sustained"])),
                      "algorithmic_flops_per_launch": flops20_r / len(segs)},
         "gpu_launches": args.steps * len(segs),
         "clocks": clk.summary(),
