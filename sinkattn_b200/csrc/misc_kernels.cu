@@ -398,7 +398,8 @@ extern "C" int sa_mean_pool_seq(const void* x, const int64_t x_strides[4], int B
   const int hb = D == 128 ? min(min(H, sa::misc::kMpMaxHeads),
                                 sa::misc::kMpStageBytes / (pool * 256))
                           : 0;
-  if (D == 128 && pool <= 256 && hb >= 1 && prefix < S) {
+  // (a box is at most 256 rows, and no taller than the sequence)
+  if (D == 128 && pool <= 256 && pool <= S && hb >= 1 && prefix < S) {
     sa::EncodeTiledFn enc = sa::encode_tiled_fn();
     if (enc == nullptr) return SA_ECUDA;
     const int pooled = (S - prefix + pool - 1) / pool;

@@ -170,7 +170,8 @@ def test_accumulate_finalize(oracle):
 @pytest.mark.parametrize("S,pool,prefix,H", [(32760, 30, 0, 3), (1000, 30, 0, 3), (1000, 30, 77, 3),
                                              (500, 7, 600, 3), (1000, 40, 3, 3), (4100, 128, 0, 3),
                                              (1000, 200, 5, 3), (31, 30, 0, 3), (64, 30, 40, 3),
-                                             (2000, 30, 0, 30), (1000, 64, 10, 13)])
+                                             (2000, 30, 0, 30), (1000, 64, 10, 13),
+                                             (20, 30, 0, 3), (20, 30, 5, 3)])
 def test_mean_pool_seq(oracle, S, pool, prefix, H):
     """Gap pooling with a kept prefix; head counts that split into uneven
     groups of heads per load (30 = 12 + 12 + 6, 13 at pool 64 = 6 + 6 + 1)."""
