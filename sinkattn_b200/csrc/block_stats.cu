@@ -325,12 +325,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int u = 0; u < 8; ++u) mxp[u] = __uint_as_float(r[0][u]);
 #pragma unroll
-          for (int c = 8; c < 128; c += 16) {
+          for (int c = 8; c + 16 <= 128; c += 16) {  // columns 8 .. 119
 #pragma unroll
             for (int u = 0; u < 8; ++u)
               mxp[u] = fmax3(mxp[u], __uint_as_float(r[(c + u) >> 5][(c + u) & 31]),
                              __uint_as_float(r[(c + 8 + u) >> 5][(c + 8 + u) & 31]));
           }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) mxp[u] = fmaxf(mxp[u], __uint_as_float(r[3][24 + u]));
           const float bmax = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
                                    fmaxf(mxp[6], mxp[7]));
           const float R = bmax * p.scale_log2;

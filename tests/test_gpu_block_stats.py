@@ -76,6 +76,24 @@ def test_exact_row_maximum_jump(oracle):
     np.testing.assert_allclose(got, want, rtol=2e-3, atol=1e-6)
 
 
+def test_negative_logits(oracle):
+    """Every logit negative (positive Q against negative K), so each block's
+    maximum is below zero: both modes against the oracle."""
+    from sinkattn_b200 import ops
+
+    g = torch.Generator().manual_seed(8)
+    q = torch.randn(1, 2, 512, 128, generator=g).abs()
+    k = -torch.randn(1, 2, 512, 128, generator=g).abs()
+    q, k = q.to(torch.bfloat16), k.to(torch.bfloat16)
+    qf, kf = q.float().numpy(), k.float().numpy()
+    got = ops.block_stats(q.cuda(), k.cuda(), mode="max").cpu().numpy()
+    want = oracle.triton_max_pool_scores(qf, kf)
+    assert (got == want).mean() >= 0.97
+    np.testing.assert_allclose(got, want, rtol=2 ** -6, atol=1e-6)
+    got = ops.block_stats(q.cuda(), k.cuda(), mode="exact").cpu().numpy()
+    np.testing.assert_allclose(got, oracle.exact_block_mass_scores(qf, kf), rtol=2e-3, atol=1e-6)
+
+
 def test_exact_strided_layout(oracle):
     """[B,S,H,D] storage viewed as [B,H,S,D] (the Wan layout) needs no copy."""
     from sinkattn_b200 import ops
