@@ -25,7 +25,13 @@
 //
 // Persistent grid (one CTA per SM) looping over pairs of 128-row query tiles
 // of one head: every K tile brought into shared memory serves both query
-// tiles, which halves the L2 -> shared-memory traffic per MMA. 384 threads:
+// tiles, which halves the L2 -> shared-memory traffic per MMA. Max mode runs
+// 384 threads (below); exact mode 640, its statistics warps 4-19 each owning
+// 64 columns of a row (warps 4-7 and 8-11 the two halves of tile 0, 12-15 and
+// 16-19 of tile 1), so that four warps per SMSP feed MUFU and each loads and
+// reduces half as much per block before its exponentials (two whole-row warps
+// per SMSP loaded and reduced in step while MUFU idled); each half keeps its
+// own (mass, maximum) per block and the epilogue combines them.
 //   warp 0      TMA producer: K tiles into a 5-slot ring
 //   warp 1      MMA issuer of query tile 0: S = Q_0 K^T (Q_0 from TMEM, K
 //               from shared memory) into its two TMEM buffers in turn
@@ -39,10 +45,11 @@
 //   released by both issuers (by a commit after its MMAs, or an arrival when
 //   the work item has no second tile).
 // TMEM: S buffers [0,128) and [256,384) of tile 0, [128,256) of tile 1;
-// Q_0 [384,448), Q_1 [448,512) (bf16 pairs, the A-operand layout). Each CTA owns one scratch slot
-// per query tile: nk x 128 fp32 values (the bf16-rounded block maxima) in max
-// mode, 2 x nk x 128 (block masses, then block maxima) in exact mode, written
-// with one coalesced store per block.
+// Q_0 [384,448), Q_1 [448,512) (bf16 pairs, the A-operand layout). Each CTA
+// owns one scratch slot per query tile: nk x 128 fp32 values (the bf16-rounded
+// block maxima) in max mode, 2 x nk x 2 x 128 (block masses of both halves,
+// then their maxima) in exact mode, written with one coalesced store per
+// block and warp.
 
 #include <math.h>
 
@@ -55,7 +62,10 @@ constexpr int kBM = 128, kBN = 128, kHD = 128;
 constexpr int kStages = 5;
 constexpr int kSBuf = 3;  // TMEM S buffers of 128 columns
 constexpr int kGroups = 2;  // query tiles per work item
-constexpr int kThreads = 128 + kGroups * 128;
+// threads of a launch whose statistics warps each own 128 / kHalves columns
+// of a row (kHalves = 2: four statistics warps per SMSP)
+template <int kHalves>
+constexpr int threads_of() { return 128 + kGroups * 128 * kHalves; }
 constexpr int kTileBytes = kBN * kHD * 2;
 constexpr int kBoxBytes = kTileBytes / 2;
 constexpr int kMaxNB = 1024;
@@ -69,7 +79,7 @@ struct Params {
   const __nv_bfloat16* q;
   int64_t qs0, qs1, qs2;
   float* scores;          // [B,H,nq,nk] fp32
-  float* scratch;         // [gridDim.x][kGroups][nk][128] fp32
+  float* scratch;         // [gridDim.x][kGroups][slot] fp32 (slot layout above)
   int32_t* status;
 };
 
@@ -85,6 +95,8 @@ struct __align__(8) SmemCtl {
   float red[kGroups][4][kMaxNB];  // per-warp column partials
   float po[kGroups][kMaxNB];      // MAX: bf16 column maxima before normalisation
   float psum[kGroups][4];
+  float mxh[kGroups][2][kBM];  // exact mode, two halves: each half's row maximum
+  float lxh[kGroups][2][kBM];  // ... and its part of the row total
 };
 
 constexpr size_t kSmemBytes = 1024 + kStages * kTileBytes + sizeof(SmemCtl);
@@ -94,8 +106,8 @@ __device__ __forceinline__ float bf16_round(float x) {
 }
 
 // Named barrier of one statistics group (ids 1 and 2, 128 threads each).
-__device__ __forceinline__ void stats_bar_sync(int group) {
-  asm volatile("bar.sync %0, 128;" ::"r"(group + 1) : "memory");
+__device__ __forceinline__ void stats_bar_sync(int group, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(group + 1), "r"(threads) : "memory");
 }
 
 // Epilogue: the scratch values of kEpi consecutive blocks of one row, loaded
@@ -128,7 +140,8 @@ constexpr int kNB0 = 2;
 __device__ __forceinline__ int nbuf_of(int a) { return a == 0 ? kNB0 : 1; }
 // physical buffer (columns [128 id, 128 id + 128)) of tile a's i-th buffer
 __device__ __forceinline__ int buf_id(int a, int i) { return a == 0 ? (i == 0 ? 0 : 2) : 1; }
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kHalves>
+__global__ void __launch_bounds__(threads_of<kHalves>(), 1)
     block_stats_kernel(const __grid_constant__ CUtensorMap tm_k, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -146,9 +159,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kSBuf; ++i) {
       mbar_init(&ctl->s_full[i], 1);
-      mbar_init(&ctl->s_empty[i], kBM);
+      mbar_init(&ctl->s_empty[i], kBM * kHalves);
     }
-    for (int a = 0; a < kGroups; ++a) mbar_init(&ctl->q_ready[a], kBM);
+    for (int a = 0; a < kGroups; ++a) mbar_init(&ctl->q_ready[a], kBM * kHalves);
     mbar_init(&ctl->mma_drain, kGroups);  // both issuers' MMAs
     ctl->abort_flag = 0;
     fence_barrier_init();
@@ -248,13 +261,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp >= 4) {
-    const int grp = (warp - 4) >> 2;  // query tile of the work item
+    constexpr int kCh = 4 / kHalves;     // 32-column chunks of S per warp
+    constexpr int kCols = 32 * kCh;      // columns of S per warp
+    constexpr int kGT = kBM * kHalves;   // threads of one statistics group
+    const int sw = warp - 4;
+    const int grp = sw / (4 * kHalves);                 // query tile of the work item
+    const int hf = kHalves == 2 ? ((sw >> 2) & 1) : 0;  // this warp's half of the columns
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
+    const int gt = hf * kBM + row;  // thread of the group
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const int slot_words = (p.mode == kExact ? 2 : 1) * p.nk * kBM;
+    // scratch: [block][half][row] masses (exact) or bf16-rounded maxima (max),
+    // then in exact mode [block][half][row] maxima
+    const int slot_words = (p.mode == kExact ? 2 : 1) * kHalves * p.nk * kBM;
     float* slot = p.scratch + ((int64_t)blockIdx.x * kGroups + grp) * slot_words;
-    float* slot_r = slot + (int64_t)p.nk * kBM;  // exact mode: the blocks' maxima
+    float* slot_r = slot + (int64_t)kHalves * p.nk * kBM;
     float* red = ctl->red[grp][0];    // red[wq][j] at red[wq * kMaxNB + j]
     float* po_s = ctl->po[grp];
     float* psum = ctl->psum[grp];
@@ -272,12 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_valid = grow < p.S;
       const int rows_valid = min(kBM, p.S - qb * kBM);
       // Q row -> TMEM (all S of this group's previous work item has been read,
-      // so the MMAs that read Q_grp are complete). Rows past S are zero.
+      // so the MMAs that read Q_grp are complete); with two halves each warp
+      // writes its half of the row. Rows past S are zero.
       {
         const uint4* src = reinterpret_cast<const uint4*>(
             p.q + (int64_t)b * p.qs0 + (int64_t)h * p.qs1 + (int64_t)grow * p.qs2);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
+          if (kHalves == 2 && half != hf) continue;
           uint32_t qv[32];
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
@@ -290,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&ctl->q_ready[grp]);
       }
-      float m = -INFINITY, l = 0.f;
+      float m = -INFINITY;
       for (int it = 0; it < items; ++it) {
         const int nbg = nbuf_of(grp);
         const int buf = buf_id(grp, cnt % nbg);
@@ -301,96 +324,130 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = __all_sync(0xffffffffu, mbar_wait(&ctl->s_full[buf], sph, p.status, abort_flag));
         if (!ok) continue;
         tc_fence_after();
-        uint32_t r[4][32];
-        const uint32_t s_addr = tmem + lane_off + buf * 128;
-        tmem_ld32(s_addr + 0, r[0]);
-        tmem_ld32(s_addr + 32, r[1]);
-        tmem_ld32(s_addr + 64, r[2]);
-        tmem_ld32(s_addr + 96, r[3]);
+        uint32_t r[kCh][32];
+        const uint32_t s_addr = tmem + lane_off + buf * 128 + hf * kCols;
+#pragma unroll
+        for (int c = 0; c < kCh; ++c) tmem_ld32(s_addr + 32 * c, r[c]);
         tmem_wait_ld();
-        reg_fence32(r[0]);
-        reg_fence32(r[1]);
-        reg_fence32(r[2]);
-        reg_fence32(r[3]);
+#pragma unroll
+        for (int c = 0; c < kCh; ++c) reg_fence32(r[c]);
         tc_fence_before();
         mbar_arrive(&ctl->s_empty[buf]);  // S copied out: the buffer may be refilled
-        const int valid = min(kBN, p.S - j * kBN);
-        if (valid < kBN) {
+        // valid keys among this warp's columns (none, in the second half of a
+        // last block with at most 64 keys)
+        const int valid = min(kBN, p.S - j * kBN) - hf * kCols;
+        if (valid < kCols) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < kCols; ++c)
             if (c >= valid) r[c >> 5][c & 31] = __float_as_uint(-INFINITY);
         }
-        {
-          float mxp[8];
+        float mxp[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) mxp[u] = __uint_as_float(r[0][u]);
+        for (int u = 0; u < 8; ++u) mxp[u] = __uint_as_float(r[0][u]);
 #pragma unroll
-          for (int c = 8; c + 16 <= 128; c += 16) {  // columns 8 .. 119
+        for (int c = 8; c + 16 <= kCols; c += 16) {  // columns 8 .. kCols - 9
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-              mxp[u] = fmax3(mxp[u], __uint_as_float(r[(c + u) >> 5][(c + u) & 31]),
-                             __uint_as_float(r[(c + 8 + u) >> 5][(c + 8 + u) & 31]));
-          }
+          for (int u = 0; u < 8; ++u)
+            mxp[u] = fmax3(mxp[u], __uint_as_float(r[(c + u) >> 5][(c + u) & 31]),
+                           __uint_as_float(r[(c + 8 + u) >> 5][(c + 8 + u) & 31]));
+        }
 #pragma unroll
-          for (int u = 0; u < 8; ++u) mxp[u] = fmaxf(mxp[u], __uint_as_float(r[3][24 + u]));
-          const float bmax = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
-                                   fmaxf(mxp[6], mxp[7]));
-          const float R = bmax * p.scale_log2;
-          m = fmaxf(m, R);
-          // MAX: the block maximum rounded as the Triton kernel stores it
-          // (pooling_kernel.py:45-48).
-          if (p.mode == kMax) {
-            slot[(int64_t)j * kBM + row] = bf16_round(R);
-            continue;
-          }
-          // EXACT: this block's mass under its own maximum R, kept with R
+        for (int u = 0; u < 8; ++u) mxp[u] = fmaxf(mxp[u], __uint_as_float(r[kCh - 1][24 + u]));
+        const float bmax = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                                 fmaxf(mxp[6], mxp[7]));
+        const float R = bmax * p.scale_log2;
+        m = fmaxf(m, R);
+        const int64_t e = ((int64_t)j * kHalves + hf) * kBM + row;
+        // MAX: the block maximum rounded as the Triton kernel stores it
+        // (pooling_kernel.py:45-48).
+        if (p.mode == kMax) {
+          slot[e] = bf16_round(R);
+          continue;
+        }
+        // EXACT: this block's (half's) mass under its own maximum R, kept with
+        // R; a half with no valid key has mass 0 and maximum -inf
+        float cs = 0.f;
+        if (R != -INFINITY) {
           const float negR = -R;
           float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < kCols; ++c)
             sp[c & 3] += ex2_approx(fmaf(__uint_as_float(r[c >> 5][c & 31]), p.scale_log2, negR));
-          slot[(int64_t)j * kBM + row] = (sp[0] + sp[1]) + (sp[2] + sp[3]);
-          slot_r[(int64_t)j * kBM + row] = R;
+          cs = (sp[0] + sp[1]) + (sp[2] + sp[3]);
         }
+        slot[e] = cs;
+        slot_r[e] = R;
       }
       __syncwarp();
       float* out = p.scores + ((int64_t)(b * p.H + h) * p.nq + qb) * p.nk;
       if (p.mode == kExact) {
-        // the masses under the row maximum m, and the row total l from them in
-        // block order; then the sum over the tile's rows of mass / max(l, 1e-6)
+        // the row maximum m over both halves; then the masses under m and the
+        // row total l from them (this warp's blocks j = hf, hf + kHalves, ...);
+        // then the sum over the tile's rows of mass / max(l, 1e-6)
         // (sparse_attention.py:224), divided by the number of valid rows (the
         // mean of line 225). The masses are recomputed in the second pass
         // rather than stored back, and each pass loads kEpi blocks' values
         // before using any: a store into the scratch inside the loop kept every
         // iteration's loads from being issued before the previous store, and
         // the epilogue ran at one L2 round trip per block (~25% of the kernel).
-        for (int j0 = 0; j0 < p.nk; j0 += kEpi) {
-          float cv[kEpi], rv[kEpi];
-          epi_load(slot, slot_r, p.nk, j0, row, cv, rv);
-#pragma unroll
-          for (int u = 0; u < kEpi; ++u)
-            if (j0 + u < p.nk) l += row_valid ? cv[u] * ex2_approx(rv[u] - m) : 0.f;
+        if (kHalves == 2) {
+          ctl->mxh[grp][hf][row] = m;
+          stats_bar_sync(grp, kGT);
+          m = fmaxf(ctl->mxh[grp][0][row], ctl->mxh[grp][1][row]);
         }
-        const float lc = fmaxf(l, 1e-6f);
-        for (int j0 = 0; j0 < p.nk; j0 += kEpi) {
-          float cv[kEpi], rv[kEpi];
-          epi_load(slot, slot_r, p.nk, j0, row, cv, rv);
+        auto masses = [&](int j0, float (&w)[kEpi]) {
+          float cv[kHalves][kEpi], rv[kHalves][kEpi];
 #pragma unroll
           for (int u = 0; u < kEpi; ++u) {
-            const int j = j0 + u;
-            if (j >= p.nk) break;
-            float v = row_valid ? __fdiv_rn(cv[u] * ex2_approx(rv[u] - m), lc) : 0.f;
+            const int jj = min(j0 + u * kHalves, p.nk - 1);
+#pragma unroll
+            for (int hh = 0; hh < kHalves; ++hh) {
+              const int64_t ee = ((int64_t)jj * kHalves + hh) * kBM + row;
+              cv[hh][u] = slot[ee];
+              rv[hh][u] = slot_r[ee];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kEpi; ++u) {
+            float x = 0.f;
+#pragma unroll
+            for (int hh = 0; hh < kHalves; ++hh) x += cv[hh][u] * ex2_approx(rv[hh][u] - m);
+            w[u] = x;
+          }
+        };
+        float l = 0.f;
+        for (int j0 = hf; j0 < p.nk; j0 += kEpi * kHalves) {
+          float w[kEpi];
+          masses(j0, w);
+#pragma unroll
+          for (int u = 0; u < kEpi; ++u)
+            if (j0 + u * kHalves < p.nk) l += row_valid ? w[u] : 0.f;
+        }
+        if (kHalves == 2) {
+          ctl->lxh[grp][hf][row] = l;
+          stats_bar_sync(grp, kGT);
+          l = ctl->lxh[grp][0][row] + ctl->lxh[grp][1][row];
+        }
+        const float lc = fmaxf(l, 1e-6f);
+        for (int j0 = hf; j0 < p.nk; j0 += kEpi * kHalves) {
+          float w[kEpi];
+          masses(j0, w);
+#pragma unroll
+          for (int u = 0; u < kEpi; ++u) {
+            const int jj = j0 + u * kHalves;
+            if (jj >= p.nk) break;
+            float v = row_valid ? __fdiv_rn(w[u], lc) : 0.f;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) red[wq * kMaxNB + j] = v;
+            if (lane == 0) red[wq * kMaxNB + jj] = v;
           }
         }
-        stats_bar_sync(grp);
+        stats_bar_sync(grp, kGT);
         const float inv_rows = 1.0f / (float)rows_valid;
-        for (int j = row; j < p.nk; j += kBM)
-          out[j] = ((red[j] + red[kMaxNB + j]) + (red[2 * kMaxNB + j] + red[3 * kMaxNB + j])) *
-                   inv_rows;
-      } else {
+        for (int jj = gt; jj < p.nk; jj += kGT)
+          out[jj] = ((red[jj] + red[kMaxNB + jj]) + (red[2 * kMaxNB + jj] + red[3 * kMaxNB + jj])) *
+                    inv_rows;
+      } else if constexpr (kHalves == 1) {
         // Po[qb, kb] = bf16(max over the tile's rows of exp2(R - m_r)); l_i = 1
         // in the Triton kernel, so there is no division (pooling_kernel.py:65-75).
         for (int j0 = 0; j0 < p.nk; j0 += kEpi) {
@@ -398,32 +455,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_load(slot, nullptr, p.nk, j0, row, cv, rv);
 #pragma unroll
           for (int u = 0; u < kEpi; ++u) {
-            const int j = j0 + u;
-            if (j >= p.nk) break;
+            const int jj = j0 + u;
+            if (jj >= p.nk) break;
             float x = row_valid ? ex2_approx(cv[u] - m) : 0.f;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-            if (lane == 0) red[wq * kMaxNB + j] = x;
+            if (lane == 0) red[wq * kMaxNB + jj] = x;
           }
         }
-        stats_bar_sync(grp);
+        stats_bar_sync(grp, kGT);
         float part = 0.f;
-        for (int j = row; j < p.nk; j += kBM) {
-          const float po = bf16_round(fmaxf(fmaxf(red[j], red[kMaxNB + j]),
-                                            fmaxf(red[2 * kMaxNB + j], red[3 * kMaxNB + j])));
-          po_s[j] = po;
+        for (int jj = row; jj < p.nk; jj += kBM) {
+          const float po = bf16_round(fmaxf(fmaxf(red[jj], red[kMaxNB + jj]),
+                                            fmaxf(red[2 * kMaxNB + jj], red[3 * kMaxNB + jj])));
+          po_s[jj] = po;
           part += po;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
         if (lane == 0) psum[wq] = part;
-        stats_bar_sync(grp);
+        stats_bar_sync(grp, kGT);
         // Po / sum(Po) with bf16 tensors (pooling_kernel.py:243-244): the sum is
         // accumulated in fp32 and rounded to bf16, the quotient rounded to bf16.
         const float sum = bf16_round((psum[0] + psum[1]) + (psum[2] + psum[3]));
-        for (int j = row; j < p.nk; j += kBM) out[j] = bf16_round(__fdiv_rn(po_s[j], sum));
+        for (int jj = row; jj < p.nk; jj += kBM) out[jj] = bf16_round(__fdiv_rn(po_s[jj], sum));
       }
-      stats_bar_sync(grp);  // red / po are rewritten by the next work item's epilogue
+      stats_bar_sync(grp, kGT);  // red / po / mxh / lxh are rewritten by the next work item
     }
   }
 
@@ -478,7 +535,9 @@ extern "C" size_t sa_block_stats_workspace_size(int B, int H, int S, int mode) {
   if (B < 1 || H < 1 || S < 1) return 0;
   if (mode != sa::stats::kExact && mode != sa::stats::kMax) return 0;
   const size_t nk = (size_t)((S + 127) / 128);
-  const size_t words = (mode == sa::stats::kExact ? 2 : 1) * nk * 128;
+  // per query tile: [block][half][row] values (two halves in exact mode),
+  // and the same again for the maxima in exact mode
+  const size_t words = (mode == sa::stats::kExact ? 2 * 2 : 1) * nk * 128;
   return (size_t)stats_grid(B, H, S) * sa::stats::kGroups * words * sizeof(float);
 }
 
@@ -516,11 +575,15 @@ extern "C" int sa_block_stats(const void* q, const void* k, const int64_t q_stri
   p.scores = scores;
   p.scratch = reinterpret_cast<float*>(workspace);
   p.status = status;
-  if (int rc = sa::func_attr_once((const void*)block_stats_kernel,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  // exact mode: four statistics warps per SMSP (each 64 columns of a row);
+  // max mode: two (each a whole row)
+  auto* kern = mode == kExact ? block_stats_kernel<2> : block_stats_kernel<1>;
+  const int threads = mode == kExact ? threads_of<2>() : threads_of<1>();
+  if (int rc = sa::func_attr_once((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmemBytes);
       rc != SA_OK)
     return rc;
-  block_stats_kernel<<<stats_grid(B, H, S), kThreads, kSmemBytes, stream>>>(tk, p);
+  kern<<<stats_grid(B, H, S), threads, kSmemBytes, stream>>>(tk, p);
   SA_CUDA_TRY(cudaGetLastError());
   return SA_OK;
 }
