@@ -39,8 +39,11 @@
 //               (two issuing threads halve the per-MMA-group waits and
 //               commits that a single thread serialises)
 //   warp 2      TMEM allocator
-//   warps 4-7   statistics of query tile 0 (thread t owns query row t)
-//   warps 8-11  statistics of query tile 1
+//   warps 4-7   statistics of query tile 0 (thread t owns query row t);
+//               exact mode: columns 0-63 of tile 0, warps 8-11 its columns
+//               64-127
+//   warps 8-11  statistics of query tile 1 (exact mode: warps 12-19, the
+//               two halves as for tile 0)
 //   Each statistics group writes its tile's Q into TMEM. Every K tile is
 //   released by both issuers (by a commit after its MMAs, or an arrival when
 //   the work item has no second tile).
