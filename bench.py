@@ -1004,6 +1004,67 @@ def run_case(args):
                          "frac": nbytes / (ms / 1e3) / 1e9 / peak}
         print(json.dumps(res))
         return 0
+    if args.case == "exchange-local":
+        # the Ulysses exchange kernels at the Wan layer (B=2, H=12, S=32768) with
+        # the buffers of P=2 ranks on this one GPU: every store lands in local
+        # HBM, so this times the kernels against HBM rather than NVLink. A
+        # dispatch reads one rank's Q, K, V shards and writes them into both
+        # ranks' receive buffers; a combine reads one rank's unit outputs and
+        # LSE and writes them into both ranks' output shards.
+        import ctypes
+
+        from sinkattn_b200 import _lib
+        from sinkattn_b200.sharding import units_per_rank
+
+        P, Sr = 2, S // 2
+        n_per = units_per_rank(B * H, P)
+        lib = _lib.load()
+        g = torch.Generator(device=dev).manual_seed(0)
+        shards = [[torch.randn(B, Sr, H, D, generator=g, device=dev, dtype=torch.bfloat16)
+                   for _ in range(3)] for _ in range(P)]
+        recv = [torch.empty(3, n_per, S, D, dtype=torch.bfloat16, device=dev) for _ in range(P)]
+        outs = [torch.randn(n_per, S, D, generator=g, device=dev, dtype=torch.bfloat16)
+                for _ in range(P)]
+        lses = [torch.randn(n_per, S, generator=g, device=dev) for _ in range(P)]
+        out_dst = [torch.empty(B, Sr, H, D, dtype=torch.bfloat16, device=dev) for _ in range(P)]
+        lse_dst = [torch.empty(B, H, Sr, device=dev) for _ in range(P)]
+        VP = ctypes.c_void_p * P
+        dst = VP(*[r.data_ptr() for r in recv])
+        od = VP(*[o.data_ptr() for o in out_dst])
+        ld = VP(*[o.data_ptr() for o in lse_dst])
+        stream = torch.cuda.current_stream(dev)
+        sh = ctypes.c_void_p(stream.cuda_stream)
+
+        def dispatch(i):
+            q, k, v = shards[i % P]
+            src = (ctypes.c_void_p * 3)(q.data_ptr(), k.data_ptr(), v.data_ptr())
+            st = (ctypes.c_int64 * 12)(*q.stride(), *k.stride(), *v.stride())
+            _lib.check(lib.sa_ulysses_dispatch(3, src, st, B, Sr, H, D, P, i % P, n_per, dst,
+                                               sh), "sa_ulysses_dispatch")
+
+        def combine(i):
+            r = i % P
+            _lib.check(lib.sa_ulysses_combine(outs[r].data_ptr(), lses[r].data_ptr(), B, Sr, H, D,
+                                              P, r, n_per, od, ld, sh), "sa_ulysses_combine")
+
+        peak = float(load_peaks()[0].get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        shard = B * Sr * H * D * 2
+        cases = {"dispatch": (dispatch, 2 * 3 * shard),
+                 "combine": (combine, 2 * (n_per * S * D * 2 + n_per * S * 4))}
+        res = {"case": args.case, "B": B, "H": H, "S": S, "P": P, "peak_gbs": peak}
+        for name, (fn, nbytes) in cases.items():
+            it = iter(range(1 << 30))
+            call = lambda: fn(next(it))  # noqa: E731
+            for _ in range(3):
+                call()
+            torch.cuda.synchronize()
+            torch.cuda._sleep(50_000_000)  # queue every timed launch ahead of the device
+            _, per = time_steps(call, args.steps, stream)
+            ms = sorted(per)[len(per) // 2]
+            res[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms / 1e3) / 1e9,
+                         "frac": nbytes / (ms / 1e3) / 1e9 / peak}
+        print(json.dumps(res))
+        return 0
     if args.case == "zimage":
         # cfg4 (Z-Image 2048x2048): B=1, H=30, 16384 image + 512 text tokens = 132 blocks;
         # text rows and columns forced dense as the Z-Image processor does
@@ -1185,7 +1246,8 @@ def main(argv=None):
                     help="heads per host<->device chunk of the end-to-end leg")
     ap.add_argument("--case", choices=["attn-small", "calib-small", "attn-wan", "calib-wan",
                                        "calib-pass", "wan-runtime", "stats-wan", "stats-small",
-                                       "qkrope-wan", "misc-wan", "ulysses", "zimage"],
+                                       "qkrope-wan", "misc-wan", "ulysses", "zimage",
+                                       "exchange-local"],
                     default=None,
                     help="run one small profiling case instead of the benchmark")
     args = ap.parse_args(argv)
